@@ -1,0 +1,579 @@
+// Mass-bias attention forward for B200 (sm_100a):
+//   O = softmax(Q K^T / sqrt(64) + log m) V      per (batch, head), head_dim 64.
+//
+// Reference behaviour (vggt_omega/models/mass_bias_attention.py:17-82, :85-129): the per-key
+// bias is log(mass) rounded to the input dtype, added in the log2 domain
+// (logit * log2e/sqrt(d) + bias * log2e), online softmax with fp32 running max / sum / output,
+// probabilities rounded to the value dtype before the PV product, output divided by the
+// running sum and written in the input dtype.
+//
+// Kernel design (one CTA per 128-row query tile and (batch, head), 6 warps):
+//   warp 0      TMA producer: Q once, then K tiles running one tile ahead of V tiles; the
+//               log2-domain bias of a key tile rides with its V tile (bulk copy, 512 B).
+//   warp 1      allocates 256 TMEM columns, then one lane issues every tcgen05.mma:
+//                 S_j = Q K_j^T   (SS-MMA, M=128 N=128 K=64, fp32 accumulate in TMEM)
+//                 O_j = P_j V_j   (TS-MMA: P_j read from TMEM, V_j from shared memory)
+//   warps 2..5  softmax warpgroup: thread t owns query row t (its TMEM lane).  For tile j it
+//               reads S_j, forms the new running max, folds O_{j-1} into its register
+//               accumulator (rescaled), writes P_j = exp2(x - m) as packed 16-bit values back
+//               over S_j's first 64 columns and signals the MMA warp.
+//   TMEM: two 128-column buffers; buffer b = j % 2 holds S_j, then P_j (cols 0-63) and
+//   O_j (cols 64-127).  While the softmax works on S_j the tensor core runs QK for j+1.
+// Shared-memory tiles use the 128-byte swizzle written by TMA; the UMMA descriptors describe
+// the same layout (K-major for Q and K, MN-major for V).  No TMA multicast is used.
+#include <cudaTypedefs.h>
+
+#include <cmath>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace vb200 {
+namespace {
+
+static __device__ unsigned g_attn_err;
+
+constexpr int kBM = 128;  // query rows per CTA
+constexpr int kBN = 128;  // keys per tile
+constexpr int kHD = 64;   // head dim
+constexpr int kStages = 2;
+constexpr int kTileBytes = kBM * kHD * 2;  // 16 KB, also the K / V tile size (kBN == kBM)
+constexpr int kBiasBytes = kBN * 4;
+constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Shared-memory layout (offsets from a 1024-byte aligned base).
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTileBytes;
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffBias = kOffV + kStages * kTileBytes;
+constexpr int kOffBar = kOffBias + kStages * kBiasBytes;
+// barriers
+constexpr int kBarQFull = 0;
+constexpr int kBarKFull = 1;
+constexpr int kBarKEmpty = kBarKFull + kStages;
+constexpr int kBarVFull = kBarKEmpty + kStages;
+constexpr int kBarVEmpty = kBarVFull + kStages;
+constexpr int kBarSFull = kBarVEmpty + kStages;
+constexpr int kBarPFull = kBarSFull + 2;
+constexpr int kBarOFull = kBarPFull + 2;
+constexpr int kBarSFree = kBarOFull + 2;
+constexpr int kNumBars = kBarSFree + 2;
+constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+constexpr int kSmemUsed = kOffTmemSlot + 16;
+constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for aligning the dynamic base
+constexpr uint32_t kTmemCols = 256;
+
+struct AttnParams {
+  const float* bias;  // [n_tiles * kBN] log2-domain bias, -inf past Nk
+  void* out;
+  long long o_sb, o_sh, o_sn;  // element strides
+  int H, Nq, Nk, n_tiles;
+  float scale_log2;  // log2(e) / sqrt(64)
+};
+
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+template <bool kBF16>
+__global__ void __launch_bounds__(kThreads, 2)
+    mass_bias_attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                                  const __grid_constant__ CUtensorMap tmap_k,
+                                  const __grid_constant__ CUtensorMap tmap_v, AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int q_tile = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int batch = bh / p.H;
+  const int head = bh - batch * p.H;
+  const int n_tiles = p.n_tiles;
+  auto bar = [&](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kBarQFull), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kBarKFull + s), 1);
+      mbar_init(bar(kBarKEmpty + s), 1);
+      mbar_init(bar(kBarVFull + s), 1);
+      mbar_init(bar(kBarVEmpty + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(kBarSFull + b), 1);
+      mbar_init(bar(kBarPFull + b), 128);
+      mbar_init(bar(kBarOFull + b), 1);
+      mbar_init(bar(kBarSFree + b), 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_q);
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(sbase + kOffTmemSlot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kOffTmemSlot);
+
+  if (warp == 0) {
+    // ------------------------------- producer -------------------------------
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(bar(kBarQFull), kTileBytes);
+      tma_load_4d(sbase + kOffQ, &tmap_q, bar(kBarQFull), 0, q_tile * kBM, head, batch);
+      auto load_k = [&](int j) -> bool {
+        const int s = j % kStages;
+        if (j >= kStages && !mbar_wait(bar(kBarKEmpty + s), ((j / kStages) - 1) & 1, &g_attn_err))
+          return false;
+        mbar_arrive_expect_tx(bar(kBarKFull + s), kTileBytes);
+        tma_load_4d(sbase + kOffK + s * kTileBytes, &tmap_k, bar(kBarKFull + s), 0, j * kBN, head,
+                    batch);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j % kStages;
+        if (j >= kStages && !mbar_wait(bar(kBarVEmpty + s), ((j / kStages) - 1) & 1, &g_attn_err))
+          return false;
+        mbar_arrive_expect_tx(bar(kBarVFull + s), kTileBytes + kBiasBytes);
+        tma_load_4d(sbase + kOffV + s * kTileBytes, &tmap_v, bar(kBarVFull + s), 0, j * kBN, head,
+                    batch);
+        bulk_load(sbase + kOffBias + s * kBiasBytes, p.bias + static_cast<size_t>(j) * kBN,
+                  kBiasBytes, bar(kBarVFull + s));
+        return true;
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (*abort_flag) { ok = false; break; }
+        ok = load_k(j);
+        if (ok && j >= 1) ok = load_v(j - 1);
+      }
+      if (ok) ok = load_v(n_tiles - 1);
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, kBF16 ? 1 : 0, 0, 0);
+      constexpr uint32_t idesc_pv = idesc_f16(kBM, kHD, kBF16 ? 1 : 0, 0, 1);
+      bool ok = mbar_wait(bar(kBarQFull), 0, &g_attn_err);
+      auto issue_pv = [&](int jj) -> bool {
+        const int bb = jj & 1;
+        const int s = jj % kStages;
+        if (!mbar_wait(bar(kBarPFull + bb), (jj >> 1) & 1, &g_attn_err)) return false;
+        if (!mbar_wait(bar(kBarVFull + s), (jj / kStages) & 1, &g_attn_err)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = sbase + kOffV + s * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // V tile: key rows of 128 bytes; a K-step of 16 keys spans two 1024-byte atoms.
+          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 16384, 1024);
+          umma_ts(tmem + bb * 128 + 64, tmem + bb * 128 + kk * 8, bdesc, idesc_pv, kk > 0);
+        }
+        umma_commit(bar(kBarOFull + bb));
+        umma_commit(bar(kBarVEmpty + s));
+        return true;
+      };
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j % kStages;
+        const int b = j & 1;
+        if (*abort_flag) { ok = false; break; }
+        if (!mbar_wait(bar(kBarKFull + s), (j / kStages) & 1, &g_attn_err)) { ok = false; break; }
+        if (j >= 2 && !mbar_wait(bar(kBarSFree + b), ((j - 2) >> 1) & 1, &g_attn_err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t q_addr = sbase + kOffQ;
+        const uint32_t k_addr = sbase + kOffK + s * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          const uint64_t adesc = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
+          const uint64_t bdesc = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
+          umma_ss(tmem + b * 128, adesc, bdesc, idesc_qk, kk > 0);
+        }
+        umma_commit(bar(kBarSFull + b));
+        umma_commit(bar(kBarKEmpty + s));
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok) ok = issue_pv(n_tiles - 1);
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------- softmax warpgroup -------------------------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const float scale = p.scale_log2;
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    float acc[kHD];
+#pragma unroll
+    for (int i = 0; i < kHD; ++i) acc[i] = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      const int s = j % kStages;
+      if (*abort_flag) { ok = false; break; }
+      if (!mbar_wait(bar(kBarSFull + b), (j >> 1) & 1, &g_attn_err)) { ok = false; break; }
+      if (!mbar_wait(bar(kBarVFull + s), (j / kStages) & 1, &g_attn_err)) { ok = false; break; }
+      tc_fence_after();
+      const float4* bias4 = reinterpret_cast<const float4*>(smem + kOffBias + s * kBiasBytes);
+      const uint32_t s_addr = tmem + lane_off + b * 128;
+
+      // pass 1: row max of the log2-domain logits
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32x32b_x32(s_addr + c * 32, r);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 bv = bias4[(c * 32 + i) / 4];
+          mx = fmaxf(mx, fmaf(u2f(r[i + 0]), scale, bv.x));
+          mx = fmaxf(mx, fmaf(u2f(r[i + 1]), scale, bv.y));
+          mx = fmaxf(mx, fmaf(u2f(r[i + 2]), scale, bv.z));
+          mx = fmaxf(mx, fmaf(u2f(r[i + 3]), scale, bv.w));
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float corr = ex2_approx(m_run - m_use);  // 0 on the first tile
+
+      // fold O_{j-1} (computed against m_run) into the accumulator, rescaled to m_new
+      if (j >= 1) {
+        const int jj = j - 1;
+        const int bb = jj & 1;
+        if (!mbar_wait(bar(kBarOFull + bb), (jj >> 1) & 1, &g_attn_err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t o_addr = tmem + lane_off + bb * 128 + 64;
+#pragma unroll
+        for (int c = 0; c < kHD / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld32x32b_x16(o_addr + c * 16, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[c * 16 + i] = (acc[c * 16 + i] + u2f(r[i])) * corr;
+        }
+        tc_fence_before();
+        mbar_arrive(bar(kBarSFree + bb));
+      }
+      l_run *= corr;
+      m_run = m_new;
+
+      // pass 2: probabilities, row sum, packed 16-bit P written over S's first 64 columns
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32x32b_x32(s_addr + c * 32, r);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 bv = bias4[(c * 32 + i) / 4];
+          const float p0 = ex2_approx(fmaf(u2f(r[i + 0]), scale, bv.x) - m_use);
+          const float p1 = ex2_approx(fmaf(u2f(r[i + 1]), scale, bv.y) - m_use);
+          const float p2 = ex2_approx(fmaf(u2f(r[i + 2]), scale, bv.z) - m_use);
+          const float p3 = ex2_approx(fmaf(u2f(r[i + 3]), scale, bv.w) - m_use);
+          l_run += (p0 + p1) + (p2 + p3);
+          pk[i / 2 + 0] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+          pk[i / 2 + 1] = kBF16 ? pack_bf16x2(p2, p3) : pack_f16x2(p2, p3);
+        }
+        tmem_st32x32b_x16(s_addr + c * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(kBarPFull + b));
+    }
+
+    if (ok) {
+      const int jj = n_tiles - 1;
+      const int bb = jj & 1;
+      if (mbar_wait(bar(kBarOFull + bb), (jj >> 1) & 1, &g_attn_err)) {
+        tc_fence_after();
+        const uint32_t o_addr = tmem + lane_off + bb * 128 + 64;
+#pragma unroll
+        for (int c = 0; c < kHD / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld32x32b_x16(o_addr + c * 16, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[c * 16 + i] += u2f(r[i]);
+        }
+        const int grow = q_tile * kBM + row;
+        if (grow < p.Nq) {
+          const float inv = 1.f / l_run;
+          uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
+                          2 * (batch * p.o_sb + head * p.o_sh + static_cast<long long>(grow) * p.o_sn);
+#pragma unroll
+          for (int c = 0; c < kHD / 8; ++c) {
+            uint4 w;
+            uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float a = acc[c * 8 + 2 * i] * inv, bq = acc[c * 8 + 2 * i + 1] * inv;
+              wp[i] = kBF16 ? pack_bf16x2(a, bq) : pack_f16x2(a, bq);
+            }
+            *reinterpret_cast<uint4*>(orow + c * 16) = w;
+          }
+        }
+      } else {
+        ok = false;
+      }
+    }
+    if (!ok) *abort_flag = 1;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Padded log2-domain bias: bias[j] = float(round_to_dtype(log_mass[j])) * log2(e) for j < Nk,
+// 0 when no bias is given, -inf for the padding up to a whole key tile.
+template <typename TB, typename TQ>
+__global__ void prepare_bias_kernel(const TB* log_mass, float* bias, int Nk, int padded) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= padded) return;
+  float v = -INFINITY;
+  if (j < Nk) {
+    if (log_mass == nullptr) {
+      v = 0.f;
+    } else {
+      const float lm = to_f32<TB>(log_mass[j]);
+      v = to_f32<TQ>(from_f32<TQ>(lm)) * kLog2e;
+    }
+  }
+  bias[j] = v;
+}
+
+// fp32 path: one warp per (query row, batch*head); lanes stride over keys with their own
+// online-softmax state, merged across the warp at the end.  FMA arithmetic throughout.
+__global__ void __launch_bounds__(256)
+    mass_bias_attention_f32_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                   const float* __restrict__ v, const float* __restrict__ bias,
+                                   float* __restrict__ out, long long q_sb, long long q_sh,
+                                   long long q_sn, long long k_sb, long long k_sh, long long k_sn,
+                                   long long v_sb, long long v_sh, long long v_sn,
+                                   long long o_sb, long long o_sh, long long o_sn, int H, int Nq,
+                                   int Nk, float scale_log2) {
+  __shared__ float qs[8][kHD];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long gw = static_cast<long long>(blockIdx.x) * 8 + warp;
+  const int bh = blockIdx.y;
+  if (gw >= Nq) return;
+  const int batch = bh / H, head = bh - (bh / H) * H;
+  const float* qrow = q + batch * q_sb + head * q_sh + gw * q_sn;
+  qs[warp][lane] = qrow[lane];
+  qs[warp][lane + 32] = qrow[lane + 32];
+  __syncwarp();
+  float m = -INFINITY, l = 0.f, acc[kHD];
+#pragma unroll
+  for (int i = 0; i < kHD; ++i) acc[i] = 0.f;
+  const float* kb = k + batch * k_sb + head * k_sh;
+  const float* vb = v + batch * v_sb + head * v_sh;
+  for (int key = lane; key < Nk; key += 32) {
+    const float4* kr = reinterpret_cast<const float4*>(kb + key * k_sn);
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kHD / 4; ++i) {
+      const float4 kv = kr[i];
+      dot = fmaf(qs[warp][4 * i + 0], kv.x, dot);
+      dot = fmaf(qs[warp][4 * i + 1], kv.y, dot);
+      dot = fmaf(qs[warp][4 * i + 2], kv.z, dot);
+      dot = fmaf(qs[warp][4 * i + 3], kv.w, dot);
+    }
+    const float x = dot * scale_log2 + bias[key];
+    const float m_new = fmaxf(m, x);
+    const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+    const float corr = exp2f(m - m_use);
+    const float pr = exp2f(x - m_use);
+    l = l * corr + pr;
+    const float4* vr = reinterpret_cast<const float4*>(vb + key * v_sn);
+#pragma unroll
+    for (int i = 0; i < kHD / 4; ++i) {
+      const float4 vv = vr[i];
+      acc[4 * i + 0] = fmaf(pr, vv.x, acc[4 * i + 0] * corr);
+      acc[4 * i + 1] = fmaf(pr, vv.y, acc[4 * i + 1] * corr);
+      acc[4 * i + 2] = fmaf(pr, vv.z, acc[4 * i + 2] * corr);
+      acc[4 * i + 3] = fmaf(pr, vv.w, acc[4 * i + 3] * corr);
+    }
+    m = m_new;
+  }
+  // merge lane states (butterfly)
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, off);
+    const float lo = __shfl_xor_sync(0xffffffffu, l, off);
+    const float mn = fmaxf(m, mo);
+    const float mu = (mn == -INFINITY) ? 0.f : mn;
+    const float ca = exp2f(m - mu), cb = exp2f(mo - mu);
+#pragma unroll
+    for (int i = 0; i < kHD; ++i) {
+      const float ao = __shfl_xor_sync(0xffffffffu, acc[i], off);
+      acc[i] = acc[i] * ca + ao * cb;
+    }
+    l = l * ca + lo * cb;
+    m = mn;
+  }
+  float* orow = out + batch * o_sb + head * o_sh + gw * o_sn;
+  const float inv = 1.f / l;
+  // every lane holds the merged row; lane i writes elements i and i + 32
+#pragma unroll
+  for (int i = 0; i < kHD; ++i) {
+    if ((i & 31) == lane) orow[i] = acc[i] * inv;
+  }
+}
+
+}  // namespace
+
+unsigned attention_error_word(int clear) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_attn_err, sizeof(v));
+  if (clear) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_attn_err, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace vb200
+
+using namespace vb200;
+
+extern "C" size_t vb200_mass_bias_attention_workspace_size(int64_t Nk) {
+  const int64_t tiles = (Nk + kBN - 1) / kBN;
+  return align_up(static_cast<size_t>(tiles > 0 ? tiles : 1) * kBN * sizeof(float), 256);
+}
+
+namespace {
+
+int launch_bias(int dtype, const void* log_mass, int bias_dtype, float* bias, int Nk, int padded,
+                cudaStream_t st) {
+  const dim3 grid((padded + 255) / 256), block(256);
+  // TQ is the attention dtype the bias is rounded to; TB the stored bias type.
+#define VB200_BIAS_CASE(TB, TQ) \
+  prepare_bias_kernel<TB, TQ><<<grid, block, 0, st>>>(static_cast<const TB*>(log_mass), bias, Nk, padded)
+  if (bias_dtype == VB200_F32) {
+    if (dtype == VB200_BF16) VB200_BIAS_CASE(float, __nv_bfloat16);
+    else if (dtype == VB200_F16) VB200_BIAS_CASE(float, __half);
+    else VB200_BIAS_CASE(float, float);
+  } else if (bias_dtype == VB200_BF16) {
+    if (dtype == VB200_BF16) VB200_BIAS_CASE(__nv_bfloat16, __nv_bfloat16);
+    else if (dtype == VB200_F16) VB200_BIAS_CASE(__nv_bfloat16, __half);
+    else VB200_BIAS_CASE(__nv_bfloat16, float);
+  } else {
+    if (dtype == VB200_BF16) VB200_BIAS_CASE(__half, __nv_bfloat16);
+    else if (dtype == VB200_F16) VB200_BIAS_CASE(__half, __half);
+    else VB200_BIAS_CASE(__half, float);
+  }
+#undef VB200_BIAS_CASE
+  VB200_CHECK_LAUNCH("prepare_bias_kernel");
+  return VB200_OK;
+}
+
+int make_qkv_map(CUtensorMap* map, const void* base, int dtype, int64_t N, int64_t H, int64_t B,
+                 const int64_t* strides) {
+  // dims: (d, token, head, batch); size-1 dims get a harmless stride.
+  const uint64_t esz = 2;
+  uint64_t dims[4] = {static_cast<uint64_t>(kHD), static_cast<uint64_t>(N),
+                      static_cast<uint64_t>(H), static_cast<uint64_t>(B)};
+  uint64_t sn = static_cast<uint64_t>(strides[2]) * esz;
+  uint64_t sh = static_cast<uint64_t>(strides[1]) * esz;
+  uint64_t sb = static_cast<uint64_t>(strides[0]) * esz;
+  if (N == 1) sn = kHD * esz;
+  if (H == 1) sh = sn * static_cast<uint64_t>(N);
+  if (B == 1) sb = sh * static_cast<uint64_t>(H);
+  uint64_t str[3] = {sn, sh, sb};
+  uint32_t box[4] = {static_cast<uint32_t>(kHD), static_cast<uint32_t>(kBM), 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == VB200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode_tiled_map(map, dt, 4, base, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+
+extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k, const void* v,
+                                         const void* log_key_mass, int bias_dtype, void* out,
+                                         int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t D,
+                                         const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                                         const int64_t* os, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  VB200_REQUIRE(dtype == VB200_BF16 || dtype == VB200_F16 || dtype == VB200_F32,
+                "mass_bias_attention: unsupported dtype code %d", dtype);
+  VB200_REQUIRE(bias_dtype == VB200_BF16 || bias_dtype == VB200_F16 || bias_dtype == VB200_F32,
+                "mass_bias_attention: unsupported bias dtype code %d", bias_dtype);
+  VB200_REQUIRE(D == kHD, "the fused kernel supports head_dim=64 only (got %lld)", (long long)D);
+  VB200_REQUIRE(B >= 1 && H >= 1 && Nq >= 0 && Nk >= 1, "invalid sizes B=%lld H=%lld Nq=%lld Nk=%lld",
+                (long long)B, (long long)H, (long long)Nq, (long long)Nk);
+  VB200_REQUIRE(Nq < (1ll << 31) && Nk < (1ll << 31) && B * H < 65536, "sizes exceed the kernel's index range");
+  VB200_REQUIRE(q && k && v && out && qs && ks && vs && os, "null pointer argument");
+  if (Nq == 0) return VB200_OK;
+  const size_t need = vb200_mass_bias_attention_workspace_size(Nk);
+  VB200_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+                "workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  VB200_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, "workspace must be 256-byte aligned");
+  int rc = check_sm100();
+  if (rc != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* bias = static_cast<float*>(workspace);
+  const int n_tiles = static_cast<int>((Nk + kBN - 1) / kBN);
+  rc = launch_bias(dtype, log_key_mass, bias_dtype, bias, static_cast<int>(Nk), n_tiles * kBN, st);
+  if (rc != VB200_OK) return rc;
+  const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(kHD));
+
+  if (dtype == VB200_F32) {
+    const dim3 grid(static_cast<unsigned>((Nq + 7) / 8), static_cast<unsigned>(B * H));
+    mass_bias_attention_f32_kernel<<<grid, 256, 0, st>>>(
+        static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
+        bias, static_cast<float*>(out), qs[0], qs[1], qs[2], ks[0], ks[1], ks[2], vs[0], vs[1],
+        vs[2], os[0], os[1], os[2], static_cast<int>(H), static_cast<int>(Nq),
+        static_cast<int>(Nk), scale_log2);
+    VB200_CHECK_LAUNCH("mass_bias_attention_f32_kernel");
+    return VB200_OK;
+  }
+
+  VB200_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15u) == 0 && os[0] % 8 == 0 && os[1] % 8 == 0 &&
+                    os[2] % 8 == 0,
+                "output rows must be 16-byte aligned");
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_qkv_map(&tq, q, dtype, Nq, H, B, qs)) != VB200_OK) return rc;
+  if ((rc = make_qkv_map(&tk, k, dtype, Nk, H, B, ks)) != VB200_OK) return rc;
+  if ((rc = make_qkv_map(&tv, v, dtype, Nk, H, B, vs)) != VB200_OK) return rc;
+
+  AttnParams prm;
+  prm.bias = bias;
+  prm.out = out;
+  prm.o_sb = os[0];
+  prm.o_sh = os[1];
+  prm.o_sn = os[2];
+  prm.H = static_cast<int>(H);
+  prm.Nq = static_cast<int>(Nq);
+  prm.Nk = static_cast<int>(Nk);
+  prm.n_tiles = n_tiles;
+  prm.scale_log2 = scale_log2;
+  const dim3 grid(static_cast<unsigned>((Nq + kBM - 1) / kBM), static_cast<unsigned>(B * H));
+  // The shared-memory opt-in is per device: set it on every call (cheap, host-side only).
+  if (dtype == VB200_BF16) {
+    VB200_CHECK_CUDA(cudaFuncSetAttribute(mass_bias_attention_tc_kernel<true>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+                     "cudaFuncSetAttribute");
+    mass_bias_attention_tc_kernel<true><<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, prm);
+  } else {
+    VB200_CHECK_CUDA(cudaFuncSetAttribute(mass_bias_attention_tc_kernel<false>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+                     "cudaFuncSetAttribute");
+    mass_bias_attention_tc_kernel<false><<<grid, kThreads, kSmemBytes, st>>>(tq, tk, tv, prm);
+  }
+  VB200_CHECK_LAUNCH("mass_bias_attention_tc_kernel");
+  return VB200_OK;
+}

@@ -1,0 +1,606 @@
+// Bandwidth-bound kernels of the top-4 sparse-convex projection and the merge step:
+//   proj_gather   merged -> tokens (WeightedBilinearTokenPlan.restore, token_merging.py:387-414)
+//   proj_scatter  tokens -> merged (WeightedBilinearTokenPlan.compact, token_merging.py:343-370;
+//                 TokenPlan.compact, token_merging.py:176-191)
+//   plan_csr      per-plan grouping by parent + mass / log-mass
+//                 (WeightedBilinearTokenPlan.__post_init__ :323-333,
+//                  deterministic_weighted_normalizer :40-59)
+//   row_gather    compact_key (:372-376), TokenPlan.restore (:193-196)
+//   row_normalize F.normalize(x.float()).to(bf16) of build_fastvggt_plan (:1102-1103)
+//
+// All row kernels assign one warp per output row and move 16-byte vectors, so a 1024-channel
+// bf16 row is 4 coalesced 512-byte sweeps of the warp.  No kernel uses atomics on data: the
+// scatter direction reads a CSR built once per plan, so every output row is reduced by one
+// warp in a fixed order (keep row, then corner 0..3 partial sums, each in source order).
+#include <cub/cub.cuh>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace vb200 {
+namespace {
+
+static __device__ unsigned g_proj_err;
+
+constexpr int kWarpsPerBlock = 8;
+
+template <typename T>
+struct Vec {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+template <typename T>
+__device__ __forceinline__ void load_vec(const T* p, float (&v)[Vec<T>::N]) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+  if constexpr (sizeof(T) == 4) {
+    v[0] = __uint_as_float(raw.x);
+    v[1] = __uint_as_float(raw.y);
+    v[2] = __uint_as_float(raw.z);
+    v[3] = __uint_as_float(raw.w);
+  } else {
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < Vec<T>::N; ++i) v[i] = to_f32<T>(e[i]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_vec(T* p, const float (&v)[Vec<T>::N]) {
+  uint4 raw;
+  T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < Vec<T>::N; ++i) e[i] = from_f32<T>(v[i]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+// Round through T (identity for fp32).
+template <typename T>
+__device__ __forceinline__ float round_t(float v) {
+  return to_f32<T>(from_f32<T>(v));
+}
+
+// ------------------------------------------------------------------------------------------
+// row gather: out[i] = x[index[i]]
+// ------------------------------------------------------------------------------------------
+__global__ void row_gather_kernel(const uint8_t* __restrict__ x, long long x_rows, long long xs_bytes,
+                                  const int64_t* __restrict__ index, long long R,
+                                  uint8_t* __restrict__ out, long long os_bytes, int row_vecs) {
+  const long long r = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const int64_t src = index[r];
+  if (src < 0 || src >= x_rows) {
+    if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+    return;
+  }
+  const uint4* s = reinterpret_cast<const uint4*>(x + src * xs_bytes);
+  uint4* d = reinterpret_cast<uint4*>(out + r * os_bytes);
+  for (int i = lane; i < row_vecs; i += 32) d[i] = __ldg(s + i);
+}
+
+// ------------------------------------------------------------------------------------------
+// gather (restore): keep rows copied, source rows = sum_c w_c * y[parent_c]
+// ------------------------------------------------------------------------------------------
+template <typename T, int kMaxCorners>
+__global__ void proj_gather_kernel(const T* __restrict__ y, long long ys, const int64_t* __restrict__ keep,
+                                   long long K, const int64_t* __restrict__ src,
+                                   const int64_t* __restrict__ parent, const float* __restrict__ w,
+                                   long long S, int corners, T* __restrict__ out, long long os,
+                                   long long N_out, int C) {
+  constexpr int V = Vec<T>::N;
+  const long long r = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= K + S) return;
+  const int nvec = C / V;
+  if (r < K) {
+    const int64_t dst = keep[r];
+    if (dst < 0 || dst >= N_out) {
+      if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+      return;
+    }
+    const uint4* s = reinterpret_cast<const uint4*>(y + r * ys);
+    uint4* d = reinterpret_cast<uint4*>(out + dst * os);
+    for (int i = lane; i < nvec; i += 32) d[i] = __ldg(s + i);
+    return;
+  }
+  const long long sidx = r - K;
+  const int64_t dst = src[sidx];
+  if (dst < 0 || dst >= N_out) {
+    if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+    return;
+  }
+  const T* prow[kMaxCorners];
+  float wc[kMaxCorners];
+#pragma unroll
+  for (int c = 0; c < kMaxCorners; ++c) {
+    if (c < corners) {
+      int64_t pc = parent[sidx * corners + c];
+      if (pc < 0 || pc >= K) {
+        if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+        pc = 0;
+      }
+      prow[c] = y + pc * ys;
+      wc[c] = round_t<T>(w[sidx * corners + c]);  // weights.to(value.dtype)
+    } else {
+      prow[c] = y;
+      wc[c] = 0.f;
+    }
+  }
+  T* drow = out + dst * os;
+  for (int i = lane; i < nvec; i += 32) {
+    float vals[kMaxCorners][V];
+#pragma unroll
+    for (int c = 0; c < kMaxCorners; ++c)
+      if (c < corners) load_vec<T>(prow[c] + i * V, vals[c]);
+    float acc[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxCorners; ++c) {
+      if (c < corners) {
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] += round_t<T>(__fmul_rn(wc[c], vals[c][e]));
+      }
+    }
+    store_vec<T>(drow + i * V, acc);
+  }
+}
+
+template <typename T>
+__global__ void zero_rows_kernel(T* out, long long os, long long N, int C) {
+  constexpr int V = Vec<T>::N;
+  const long long r = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= N) return;
+  uint4* d = reinterpret_cast<uint4*>(out + r * os);
+  for (int i = lane; i < C / V; i += 32) d[i] = make_uint4(0, 0, 0, 0);
+}
+
+// ------------------------------------------------------------------------------------------
+// scatter (compact): out[j] = (keep_j + sum_c part_c) / normalizer_j
+//   kCB 16-byte vectors per lane are reduced per pass (kCB * 32 * V channels).
+// ------------------------------------------------------------------------------------------
+template <typename T, int kCB>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    proj_scatter_kernel(const T* __restrict__ x, long long x_rows, long long xs, const int64_t* __restrict__ keep,
+                        long long M, int corners, const int32_t* __restrict__ seg_offsets,
+                        const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
+                        const float* __restrict__ normalizer, T* __restrict__ out, long long os,
+                        int C) {
+  constexpr int V = Vec<T>::N;
+  constexpr int kChunk = kCB * 32 * V;  // channels per pass
+  const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= M) return;
+  const float norm = normalizer[j];
+  const T* krow = nullptr;
+  if (keep != nullptr) {
+    const int64_t kr = keep[j];
+    if (kr >= 0 && kr < x_rows) {
+      krow = x + kr * xs;
+    } else if (lane == 0) {
+      atomicOr(&g_proj_err, kErrBadArgument);
+    }
+  }
+  T* drow = out + j * os;
+  const int32_t* seg = seg_offsets + j * corners;
+
+  for (int base = 0; base < C; base += kChunk) {
+    float acc[kCB][V];
+#pragma unroll
+    for (int cb = 0; cb < kCB; ++cb) {
+      const int col = base + (cb * 32 + lane) * V;
+      if (krow != nullptr && col < C) {
+        load_vec<T>(krow + col, acc[cb]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[cb][e] = 0.f;
+      }
+    }
+    for (int c = 0; c < corners; ++c) {
+      const int e0 = seg[c], e1 = seg[c + 1];
+      if (e0 == e1) continue;
+      float part[kCB][V];
+#pragma unroll
+      for (int cb = 0; cb < kCB; ++cb)
+#pragma unroll
+        for (int e = 0; e < V; ++e) part[cb][e] = 0.f;
+      int e = e0;
+      // two entries per step keeps 2*kCB vector loads in flight per lane
+      for (; e + 1 < e1; e += 2) {
+        int s0 = __ldg(entry_src + e), s1 = __ldg(entry_src + e + 1);
+        float w0 = __ldg(entry_w + e), w1 = __ldg(entry_w + e + 1);
+        if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
+        if (s1 < 0 || s1 >= x_rows) { s1 = 0; w1 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
+        float v0[kCB][V], v1[kCB][V];
+#pragma unroll
+        for (int cb = 0; cb < kCB; ++cb) {
+          const int col = base + (cb * 32 + lane) * V;
+          if (col < C) {
+            load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0[cb]);
+            load_vec<T>(x + static_cast<long long>(s1) * xs + col, v1[cb]);
+          }
+        }
+#pragma unroll
+        for (int cb = 0; cb < kCB; ++cb) {
+          const int col = base + (cb * 32 + lane) * V;
+          if (col < C) {
+#pragma unroll
+            for (int q = 0; q < V; ++q) {
+              part[cb][q] = __fadd_rn(part[cb][q], __fmul_rn(w0, v0[cb][q]));
+              part[cb][q] = __fadd_rn(part[cb][q], __fmul_rn(w1, v1[cb][q]));
+            }
+          }
+        }
+      }
+      if (e < e1) {
+        int s0 = __ldg(entry_src + e);
+        float w0 = __ldg(entry_w + e);
+        if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
+#pragma unroll
+        for (int cb = 0; cb < kCB; ++cb) {
+          const int col = base + (cb * 32 + lane) * V;
+          if (col < C) {
+            float v0[V];
+            load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0);
+#pragma unroll
+            for (int q = 0; q < V; ++q) part[cb][q] = __fadd_rn(part[cb][q], __fmul_rn(w0, v0[q]));
+          }
+        }
+      }
+#pragma unroll
+      for (int cb = 0; cb < kCB; ++cb)
+#pragma unroll
+        for (int q = 0; q < V; ++q) acc[cb][q] = __fadd_rn(acc[cb][q], part[cb][q]);
+    }
+#pragma unroll
+    for (int cb = 0; cb < kCB; ++cb) {
+      const int col = base + (cb * 32 + lane) * V;
+      if (col < C) {
+        float o[V];
+#pragma unroll
+        for (int q = 0; q < V; ++q) o[q] = __fdiv_rn(acc[cb][q], norm);
+        store_vec<T>(drow + col, o);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// plan CSR
+// ------------------------------------------------------------------------------------------
+__global__ void csr_keys_kernel(const int64_t* __restrict__ parent, long long n, int corners,
+                                long long M, int32_t* __restrict__ keys, int32_t* __restrict__ vals,
+                                int32_t* __restrict__ counts, int32_t dropped_key) {
+  const long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= n) return;
+  const long long s = e / corners;
+  const int c = static_cast<int>(e - s * corners);
+  const int64_t p = parent[e];
+  int32_t key = dropped_key;  // sorts after every valid key; never counted
+  if (p >= 0 && p < M) {
+    key = static_cast<int32_t>(p * corners + c);
+    atomicAdd(counts + key, 1);  // integer counts: order-independent
+  } else {
+    atomicOr(&g_proj_err, kErrBadArgument);
+  }
+  keys[e] = key;
+  vals[e] = static_cast<int32_t>(s);
+}
+
+__global__ void csr_entries_kernel(const int32_t* __restrict__ sorted_keys,
+                                   const int32_t* __restrict__ sorted_src, long long n, int corners,
+                                   const float* __restrict__ weights, const int64_t* __restrict__ src_rows,
+                                   int32_t* __restrict__ entry_src, float* __restrict__ entry_w,
+                                   int32_t dropped_key) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int32_t key = sorted_keys[i];
+  const int32_t s = sorted_src[i];
+  if (key == dropped_key) {
+    entry_src[i] = 0;
+    entry_w[i] = 0.f;
+    return;
+  }
+  const int c = key % corners;
+  entry_src[i] = src_rows ? static_cast<int32_t>(src_rows[s]) : s;
+  entry_w[i] = weights[static_cast<long long>(s) * corners + c];
+}
+
+// mass_j = 1 + sum_c (sum of segment (j, c)); one warp per row, fixed-order warp reduction.
+__global__ void csr_mass_kernel(const int32_t* __restrict__ seg_offsets, const float* __restrict__ entry_w,
+                                long long M, int corners, float* __restrict__ mass,
+                                float* __restrict__ log_mass) {
+  const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= M) return;
+  float total = 1.f;
+  for (int c = 0; c < corners; ++c) {
+    const int e0 = seg_offsets[j * corners + c], e1 = seg_offsets[j * corners + c + 1];
+    float part = 0.f;
+    for (int e = e0 + lane; e < e1; e += 32) part += entry_w[e];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    total += part;
+  }
+  if (lane == 0) {
+    if (mass) mass[j] = total;
+    if (log_mass) log_mass[j] = logf(total);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// row normalisation to bf16
+// ------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void row_normalize_kernel(const T* __restrict__ x, long long x_rows, long long xs,
+                                     const int64_t* __restrict__ rows, long long R, int C, float eps,
+                                     __nv_bfloat16* __restrict__ out, long long os) {
+  constexpr int V = Vec<T>::N;
+  const long long r = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const long long src = rows ? rows[r] : r;
+  if (src < 0 || src >= x_rows) {
+    if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+    return;
+  }
+  const T* xr = x + src * xs;
+  float ss = 0.f;
+  for (int i = lane; i < C / V; i += 32) {
+    float v[V];
+    load_vec<T>(xr + i * V, v);
+#pragma unroll
+    for (int e = 0; e < V; ++e) ss = fmaf(v[e], v[e], ss);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float denom = fmaxf(sqrtf(ss), eps);
+  __nv_bfloat16* orow = out + r * os;
+  for (int i = lane; i < C / V; i += 32) {
+    float v[V];
+    load_vec<T>(xr + i * V, v);
+#pragma unroll
+    for (int e = 0; e < V; e += 2) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(__fdiv_rn(v[e], denom), __fdiv_rn(v[e + 1], denom));
+      *reinterpret_cast<__nv_bfloat162*>(orow + i * V + e) = b;
+    }
+  }
+}
+
+inline int elem_size(int dtype) { return dtype == VB200_F32 ? 4 : 2; }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline unsigned row_blocks(long long rows) {
+  return static_cast<unsigned>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
+}
+
+int check_rows(int dtype, const void* p, int64_t row_stride, int64_t C, const char* name) {
+  const int es = elem_size(dtype);
+  VB200_REQUIRE((C * es) % 16 == 0, "%s: channels (%lld) must be a multiple of %d", name,
+                (long long)C, 16 / es);
+  VB200_REQUIRE(aligned16(p) && (row_stride * es) % 16 == 0,
+                "%s: rows must be 16-byte aligned (row stride %lld elements)", name,
+                (long long)row_stride);
+  return VB200_OK;
+}
+
+struct CsrWorkspace {
+  size_t keys_in, keys_out, vals_in, vals_out, counts, sort_tmp, scan_tmp, total;
+  size_t sort_bytes, scan_bytes;
+};
+
+CsrWorkspace csr_layout(int64_t S, int64_t corners, int64_t M) {
+  const int n = static_cast<int>(S * corners);
+  const int nseg = static_cast<int>(M * corners + 1);
+  CsrWorkspace w{};
+  size_t sort_bytes = 0, scan_bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, static_cast<int32_t*>(nullptr),
+                                  static_cast<int32_t*>(nullptr), static_cast<int32_t*>(nullptr),
+                                  static_cast<int32_t*>(nullptr), n > 0 ? n : 1);
+  cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int32_t*>(nullptr),
+                                static_cast<int32_t*>(nullptr), nseg);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  const size_t nb = static_cast<size_t>(n > 0 ? n : 1) * 4;
+  w.keys_in = take(nb);
+  w.keys_out = take(nb);
+  w.vals_in = take(nb);
+  w.vals_out = take(nb);
+  w.counts = take(static_cast<size_t>(nseg) * 4);
+  w.sort_tmp = take(sort_bytes);
+  w.scan_tmp = take(scan_bytes);
+  w.total = off;
+  w.sort_bytes = sort_bytes;
+  w.scan_bytes = scan_bytes;
+  return w;
+}
+
+}  // namespace
+
+unsigned projection_error_word(int clear) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_proj_err, sizeof(v));
+  if (clear) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_proj_err, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace vb200
+
+using namespace vb200;
+
+extern "C" int vb200_row_gather(int dtype, const void* x, int64_t x_rows, int64_t xs, const int64_t* index,
+                                int64_t R, void* out, int64_t os, int64_t C, void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "row_gather: bad dtype %d", dtype);
+  VB200_REQUIRE(R >= 0 && C >= 0, "row_gather: negative size");
+  if (R == 0 || C == 0) return VB200_OK;
+  VB200_REQUIRE(x && out && index, "row_gather: null pointer");
+  int rc;
+  if ((rc = check_rows(dtype, x, xs, C, "row_gather input")) != VB200_OK) return rc;
+  if ((rc = check_rows(dtype, out, os, C, "row_gather output")) != VB200_OK) return rc;
+  const int es = elem_size(dtype);
+  row_gather_kernel<<<row_blocks(R), kWarpsPerBlock * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(x), x_rows, xs * es, index, R, static_cast<uint8_t*>(out), os * es,
+      static_cast<int>(C * es / 16));
+  VB200_CHECK_LAUNCH("row_gather_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int64_t* keep,
+                                 int64_t K, const int64_t* src, const int64_t* parent,
+                                 const float* w, int64_t S, int64_t corners, void* out, int64_t os,
+                                 int64_t N_out, int64_t C, int zero_fill, void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "proj_gather: bad dtype %d", dtype);
+  VB200_REQUIRE(K >= 0 && S >= 0 && N_out >= 0 && C >= 0, "proj_gather: negative size");
+  VB200_REQUIRE(corners >= 1 && corners <= 4, "proj_gather: corners must be in [1, 4] (got %lld)",
+                (long long)corners);
+  if (C == 0 || N_out == 0) return VB200_OK;
+  VB200_REQUIRE(out != nullptr && (K == 0 || (y && keep)) && (S == 0 || (src && parent && w)),
+                "proj_gather: null pointer");
+  VB200_REQUIRE(S == 0 || K > 0, "proj_gather: sources need at least one compact row to read");
+  int rc;
+  if (K > 0 && (rc = check_rows(dtype, y, ys, C, "proj_gather input")) != VB200_OK) return rc;
+  if ((rc = check_rows(dtype, out, os, C, "proj_gather output")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (zero_fill) {
+#define VB200_ZERO(T) zero_rows_kernel<T><<<row_blocks(N_out), kWarpsPerBlock * 32, 0, st>>>( \
+      static_cast<T*>(out), os, N_out, static_cast<int>(C))
+    if (dtype == VB200_F32) VB200_ZERO(float);
+    else if (dtype == VB200_BF16) VB200_ZERO(__nv_bfloat16);
+    else VB200_ZERO(__half);
+#undef VB200_ZERO
+    VB200_CHECK_LAUNCH("zero_rows_kernel");
+  }
+  if (K + S == 0) return VB200_OK;
+#define VB200_GATHER(T)                                                                      \
+  proj_gather_kernel<T, 4><<<row_blocks(K + S), kWarpsPerBlock * 32, 0, st>>>(               \
+      static_cast<const T*>(y), ys, keep, K, src, parent, w, S, static_cast<int>(corners), \
+      static_cast<T*>(out), os, N_out, static_cast<int>(C))
+  if (dtype == VB200_F32) VB200_GATHER(float);
+  else if (dtype == VB200_BF16) VB200_GATHER(__nv_bfloat16);
+  else VB200_GATHER(__half);
+#undef VB200_GATHER
+  VB200_CHECK_LAUNCH("proj_gather_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64_t xs, const int64_t* keep,
+                                  int64_t M, int64_t corners, const int32_t* seg_offsets,
+                                  const int32_t* entry_src, const float* entry_w,
+                                  const float* normalizer, void* out, int64_t os, int64_t C,
+                                  void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "proj_scatter: bad dtype %d", dtype);
+  VB200_REQUIRE(M >= 0 && C >= 0 && corners >= 1, "proj_scatter: bad sizes");
+  if (M == 0 || C == 0) return VB200_OK;
+  VB200_REQUIRE(x && out && seg_offsets && normalizer && x_rows > 0, "proj_scatter: null pointer or empty input");
+  int rc;
+  if ((rc = check_rows(dtype, x, xs, C, "proj_scatter input")) != VB200_OK) return rc;
+  if ((rc = check_rows(dtype, out, os, C, "proj_scatter output")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_SCATTER(T, CB)                                                                  \
+  proj_scatter_kernel<T, CB><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                  \
+      static_cast<const T*>(x), x_rows, xs, keep, M, static_cast<int>(corners), seg_offsets, entry_src, \
+      entry_w, normalizer, static_cast<T*>(out), os, static_cast<int>(C))
+  if (dtype == VB200_F32) {
+    if (C <= 128) VB200_SCATTER(float, 1);
+    else VB200_SCATTER(float, 4);
+  } else if (dtype == VB200_BF16) {
+    if (C <= 256) VB200_SCATTER(__nv_bfloat16, 1);
+    else VB200_SCATTER(__nv_bfloat16, 4);
+  } else {
+    if (C <= 256) VB200_SCATTER(__half, 1);
+    else VB200_SCATTER(__half, 4);
+  }
+#undef VB200_SCATTER
+  VB200_CHECK_LAUNCH("proj_scatter_kernel");
+  return VB200_OK;
+}
+
+extern "C" size_t vb200_plan_csr_workspace_size(int64_t S, int64_t corners, int64_t M) {
+  if (S < 0 || corners < 1 || M < 0) return 0;
+  return csr_layout(S, corners, M).total;
+}
+
+extern "C" int vb200_plan_csr_build(const int64_t* parent, const float* weights,
+                                    const int64_t* src_rows, int64_t S, int64_t corners, int64_t M,
+                                    int32_t* seg_offsets, int32_t* entry_src, float* entry_w,
+                                    float* mass, float* log_mass, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  VB200_REQUIRE(S >= 0 && M >= 0 && corners >= 1 && corners <= 16, "plan_csr_build: bad sizes");
+  VB200_REQUIRE(S * corners < (1ll << 30) && M * corners < (1ll << 30),
+                "plan_csr_build: sizes exceed the int32 index range");
+  VB200_REQUIRE(seg_offsets != nullptr, "plan_csr_build: seg_offsets must not be NULL");
+  VB200_REQUIRE(S == 0 || (parent && weights && entry_src && entry_w), "plan_csr_build: null pointer");
+  const CsrWorkspace lay = csr_layout(S, corners, M);
+  VB200_REQUIRE(workspace != nullptr && workspace_bytes >= lay.total,
+                "plan_csr_build: workspace of %zu bytes required (got %zu)", lay.total, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* keys_in = reinterpret_cast<int32_t*>(ws + lay.keys_in);
+  int32_t* keys_out = reinterpret_cast<int32_t*>(ws + lay.keys_out);
+  int32_t* vals_in = reinterpret_cast<int32_t*>(ws + lay.vals_in);
+  int32_t* vals_out = reinterpret_cast<int32_t*>(ws + lay.vals_out);
+  int32_t* counts = reinterpret_cast<int32_t*>(ws + lay.counts);
+  const long long n = S * corners;
+  const int nseg = static_cast<int>(M * corners + 1);
+  const int32_t dropped = static_cast<int32_t>(M * corners);
+  VB200_CHECK_CUDA(cudaMemsetAsync(counts, 0, static_cast<size_t>(nseg) * 4, st), "cudaMemsetAsync");
+  if (n > 0) {
+    csr_keys_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
+        parent, n, static_cast<int>(corners), M, keys_in, vals_in, counts, dropped);
+    VB200_CHECK_LAUNCH("csr_keys_kernel");
+    int end_bit = 1;
+    while ((1ll << end_bit) <= dropped) ++end_bit;
+    size_t sort_bytes = lay.sort_bytes;
+    VB200_CHECK_CUDA(cub::DeviceRadixSort::SortPairs(ws + lay.sort_tmp, sort_bytes, keys_in, keys_out,
+                                                     vals_in, vals_out, static_cast<int>(n), 0,
+                                                     end_bit, st),
+                     "cub::DeviceRadixSort::SortPairs");
+  }
+  size_t scan_bytes = lay.scan_bytes;
+  VB200_CHECK_CUDA(cub::DeviceScan::ExclusiveSum(ws + lay.scan_tmp, scan_bytes, counts, seg_offsets,
+                                                 nseg, st),
+                   "cub::DeviceScan::ExclusiveSum");
+  if (n > 0) {
+    csr_entries_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(
+        keys_out, vals_out, n, static_cast<int>(corners), weights, src_rows, entry_src, entry_w, dropped);
+    VB200_CHECK_LAUNCH("csr_entries_kernel");
+  }
+  if (M > 0 && (mass || log_mass)) {
+    csr_mass_kernel<<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(
+        seg_offsets, entry_w, M, static_cast<int>(corners), mass, log_mass);
+    VB200_CHECK_LAUNCH("csr_mass_kernel");
+  }
+  return VB200_OK;
+}
+
+extern "C" int vb200_row_normalize_bf16(int dtype, const void* x, int64_t x_rows, int64_t xs, const int64_t* rows,
+                                        int64_t R, int64_t C, float eps, void* out, int64_t os,
+                                        void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "row_normalize: bad dtype %d", dtype);
+  VB200_REQUIRE(R >= 0 && C >= 0, "row_normalize: negative size");
+  if (R == 0 || C == 0) return VB200_OK;
+  VB200_REQUIRE(x && out, "row_normalize: null pointer");
+  int rc;
+  if ((rc = check_rows(dtype, x, xs, C, "row_normalize input")) != VB200_OK) return rc;
+  if ((rc = check_rows(VB200_BF16, out, os, C, "row_normalize output")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_NORM(T)                                                                  \
+  row_normalize_kernel<T><<<row_blocks(R), kWarpsPerBlock * 32, 0, st>>>(              \
+      static_cast<const T*>(x), x_rows, xs, rows, R, static_cast<int>(C), eps,         \
+      static_cast<__nv_bfloat16*>(out), os)
+  if (dtype == VB200_F32) VB200_NORM(float);
+  else if (dtype == VB200_BF16) VB200_NORM(__nv_bfloat16);
+  else VB200_NORM(__half);
+#undef VB200_NORM
+  VB200_CHECK_LAUNCH("row_normalize_kernel");
+  return VB200_OK;
+}

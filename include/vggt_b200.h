@@ -1,0 +1,163 @@
+/*
+ * vggt_b200.h — C ABI of the B200 (sm_100a) kernels for VGGT-Omega's token-merged global
+ * attention: the merge step, mass-bias attention and the top-4 sparse-convex projection.
+ *
+ * Conventions
+ *   - Every entry point returns 0 on success and a negative VB200_E* code on failure; the
+ *     text of the last failure on the calling thread is returned by vb200_last_error().
+ *     Argument errors are detected on the host before anything is launched.
+ *   - Pointers are device pointers unless stated; sizes and strides are in ELEMENTS.
+ *   - Work is enqueued on `stream` (a cudaStream_t, passed as void*); nothing synchronises
+ *     the stream and nothing allocates device memory unless the entry point says so.
+ *   - Index tensors are int64 (torch.long), as in the reference plans.
+ *
+ * Each declaration names the reference interface it replaces (paths inside
+ * shuang-yang18/4D_TTT_merging).
+ */
+#ifndef VGGT_B200_H_
+#define VGGT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VB200_API __attribute__((visibility("default")))
+#else
+#define VB200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define VB200_F32 0
+#define VB200_BF16 1
+#define VB200_F16 2
+
+/* status codes */
+#define VB200_OK 0
+#define VB200_EINVAL -1      /* shape / dtype / stride / alignment error   (Python: ValueError) */
+#define VB200_ECUDA -2       /* CUDA runtime or driver error               (Python: RuntimeError) */
+#define VB200_EUNSUPPORTED -3 /* device is not sm_100 / feature not built  (Python: RuntimeError) */
+
+/* ---- library ---------------------------------------------------------------------------- */
+VB200_API int vb200_version(void);
+VB200_API const char* vb200_last_error(void);
+/* OR of the error words that kernels write when a bounded wait runs out (bit 0) or an index
+ * is out of range (bit 1).  Synchronises the current device; clears the words when clear!=0. */
+VB200_API int vb200_device_error_flags(unsigned* flags, int clear);
+
+/* ---- a1/a2/a3: mass-bias attention --------------------------------------------------------
+ * out = softmax(q k^T / sqrt(D) + log_key_mass) v for every (batch, head); D must be 64.
+ * Replaces mass_bias_attention() / _mass_bias_attention_fwd
+ *   (vggt_omega/models/mass_bias_attention.py:85-129, :17-82) and the SDPA-with-mask call
+ *   (vggt_omega/models/layers/attention.py:400); with log_key_mass == NULL it is the dense
+ *   special-query SDPA (attention.py:406-423).
+ * dtype: VB200_BF16 / VB200_F16 run on tcgen05 tensor cores (fp32 softmax state); VB200_F32
+ *   runs an fp32 FMA path.  log_key_mass has `bias_dtype` and Nk entries; as in the
+ *   reference it is rounded to `dtype` before use.
+ * strides: {batch, head, token} for each of q, k, v, out; the channel stride is 1.
+ * workspace: device scratch of vb200_mass_bias_attention_workspace_size(Nk) bytes (the
+ *   padded log2-domain bias), 256-byte aligned. */
+VB200_API size_t vb200_mass_bias_attention_workspace_size(int64_t Nk);
+VB200_API int vb200_mass_bias_attention(int dtype, const void* q, const void* k, const void* v,
+                              const void* log_key_mass, int bias_dtype, void* out, int64_t B,
+                              int64_t H, int64_t Nq, int64_t Nk, int64_t D,
+                              const int64_t* q_strides, const int64_t* k_strides,
+                              const int64_t* v_strides, const int64_t* o_strides,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- a7/a8: plan preprocessing --------------------------------------------------------------
+ * Groups the S*corners (source, corner) pairs of a weighted plan by compact parent so that
+ * every reduction below runs in a fixed order with no atomics.  Segment (j, c) lists, in
+ * ascending source order, the sources whose corner-c parent is j; segments are laid out
+ * j-major, c-minor.  Also emits mass_j = 1 + sum of the weights in j's segments (summed
+ * corner by corner, source order inside a corner) and log(mass_j).
+ * Replaces WeightedBilinearTokenPlan.__post_init__ (models/token_merging.py:323-333) and
+ * deterministic_weighted_normalizer (token_merging.py:40-59).
+ * parent: [S, corners] int64 compact ids in [0, M); weights: [S, corners] fp32;
+ * src_rows: [S] int64 token row of each source (the plan's source_original), or NULL for
+ *   identity.  Outputs: seg_offsets [M*corners + 1] int32, entry_src [S*corners] int32 (the
+ *   token row of the entry's source), entry_w [S*corners] fp32, mass [M] fp32, log_mass [M]
+ *   fp32 (either may be NULL).  A parent outside [0, M) sets device error bit 1 and the pair
+ *   is dropped.
+ * workspace: vb200_plan_csr_workspace_size(S, corners, M) bytes, 256-byte aligned. */
+VB200_API size_t vb200_plan_csr_workspace_size(int64_t S, int64_t corners, int64_t M);
+VB200_API int vb200_plan_csr_build(const int64_t* parent, const float* weights, const int64_t* src_rows,
+                         int64_t S, int64_t corners, int64_t M, int32_t* seg_offsets,
+                         int32_t* entry_src, float* entry_w, float* mass, float* log_mass,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- a4: top-4 scatter-accumulate (tokens -> merged) ----------------------------------------
+ * out[j] = (x[keep[j]] + sum_c sum_{e in seg(j,c)} w_e * x[entry_src[e]]) / normalizer[j]
+ * accumulated in fp32 (each product rounded to fp32, corner partial sums added in corner
+ * order), written in `dtype`.  keep may be NULL (hard-merge mean pooling: the accumulator
+ * starts at zero).  Row strides in elements; C % 8 == 0 for 16-bit types, C % 4 for fp32;
+ * rows 16-byte aligned.  Rows of x outside [0, x_rows) referenced by keep or entry_src set
+ * device error bit 1 and are skipped (keep: the accumulator starts at zero).
+ * Replaces WeightedBilinearTokenPlan.compact / compact_query (token_merging.py:343-370,
+ * :382-385) and TokenPlan.compact (token_merging.py:176-191, deterministic here). */
+VB200_API int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64_t x_row_stride,
+                       const int64_t* keep, int64_t M, int64_t corners,
+                       const int32_t* seg_offsets, const int32_t* entry_src,
+                       const float* entry_w, const float* normalizer, void* out,
+                       int64_t out_row_stride, int64_t C, void* stream);
+
+/* ---- a6: top-4 gather (merged -> tokens) ----------------------------------------------------
+ * out[keep[k]] = y[k];  out[src[s]] = sum_c w[s,c] * y[parent[s,c]]
+ * For 16-bit dtypes the weights are rounded to `dtype` and each product is rounded to
+ * `dtype` before the (fp32) 4-term sum, which is rounded once — the reference's
+ * value-dtype arithmetic.  Rows of `out` covered by neither keep nor src are left as they
+ * are unless zero_fill != 0 (then they are zeroed), as new_zeros does in the reference.
+ * Replaces WeightedBilinearTokenPlan.restore / restore_query (token_merging.py:387-426). */
+VB200_API int vb200_proj_gather(int dtype, const void* y, int64_t y_row_stride, const int64_t* keep,
+                      int64_t K, const int64_t* src, const int64_t* parent, const float* w,
+                      int64_t S, int64_t corners, void* out, int64_t out_row_stride,
+                      int64_t N_out, int64_t C, int zero_fill, void* stream);
+
+/* ---- a5/a10: plain row gather -----------------------------------------------------------------
+ * out[i] = x[index[i]] for i < R; an index outside [0, x_rows) sets device error bit 1 and
+ * leaves out[i] untouched.  Replaces compact_key (token_merging.py:372-376),
+ * TokenPlan.restore (token_merging.py:193-196) and the keep gathers of TokenPlan.compact. */
+VB200_API int vb200_row_gather(int dtype, const void* x, int64_t x_rows, int64_t x_row_stride, const int64_t* index,
+                     int64_t R, void* out, int64_t out_row_stride, int64_t C, void* stream);
+
+/* ---- a9/a11: merge step ----------------------------------------------------------------------
+ * Row L2 normalisation to bf16 (F.normalize(x.float(), dim=-1, eps).to(bfloat16)),
+ * as in build_fastvggt_plan (token_merging.py:1102-1103).  `rows` may be NULL (identity)
+ * or gather rows of x. */
+VB200_API int vb200_row_normalize_bf16(int dtype, const void* x, int64_t x_rows, int64_t x_row_stride, const int64_t* rows,
+                             int64_t R, int64_t C, float eps, void* out, int64_t out_row_stride,
+                             void* stream);
+
+/* Cosine-similarity GEMM with a fused running top-k epilogue (k = 1 or 4).
+ * score[r, n] = bf16_round( <query[r], basis[n]> ) over D channels (fp32 accumulation on
+ * tcgen05), ranked per row; ties keep the lower basis index.  With groups: query rows
+ * [q_begin[g], q_begin[g+1]) are matched only against basis rows [b_begin[g], b_begin[g+1]);
+ * groups == 1 with NULL tables means all rows against all basis rows.
+ * query: [R, D] bf16, row stride q_row_stride; basis: [Nb, D] bf16 (K-major, i.e. the rows
+ * of the dictionary, row stride b_row_stride).  D % 64 == 0.  values [R, k] fp32,
+ * indices [R, k] int64 (basis index, global), ordered best first.
+ * Replaces streaming_top4 (models/sparse_convex_kernels.py:309-329), the
+ * `(q.bf16 @ basis.bf16).topk(4)` retrievals (models/sparse_convex.py:264, 294, 546-547,
+ * 2402-2404) and the bmm + max(-1) of build_fastvggt_plan (token_merging.py:1106-1111). */
+VB200_API int vb200_sim_topk(const void* query, int64_t q_row_stride, const void* basis,
+                   int64_t b_row_stride, int64_t R, int64_t Nb, int64_t D, int k,
+                   const int64_t* q_begin, const int64_t* b_begin, int64_t groups,
+                   float* values, int64_t* indices, void* stream);
+
+/* ---- next tier: 4-support simplex solvers ------------------------------------------------
+ * Replaces four_support_projected_gradient (models/sparse_convex_kernels.py:283-296) and
+ * four_support_active_set (sparse_convex_kernels.py:332-353).  gram [rows,4,4], rhs
+ * [rows,4], out [rows,4], all fp32 contiguous. */
+VB200_API int vb200_four_support_projected_gradient(const float* gram, const float* rhs, float* out,
+                                          int64_t rows, int steps, void* stream);
+VB200_API int vb200_four_support_active_set(const float* gram, const float* rhs, float* out,
+                                  int64_t rows, float ridge, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VGGT_B200_H_ */

@@ -1,0 +1,188 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference implementation.
+
+Runs the reference's own PyTorch code (shuang-yang18/4D_TTT_merging, imported read-only from
+REFERENCE_ROOT, default /root/reference) on CPU with seeded inputs and stores inputs and
+outputs in ``tests/golden/golden.npz``.  It is run once in the build container; the GPU box
+never needs the reference.  Cases:
+
+  block_compact_q / block_preserve_q
+      SelfAttention.forward(x, token_plan=WeightedBilinearTokenPlan) — the global-attention
+      call site (vggt_omega/models/layers/attention.py:264-439): qkv, q/k LayerNorm, compact,
+      SDPA with the log-mass bias (the non-Triton branch, :400), dense special queries
+      (:406-423), proj, restore.  Compact-query and query-preserving plans.
+  plan_*     WeightedBilinearTokenPlan.compact / restore in fp32 and bf16 and
+             deterministic_weighted_normalizer (vggt_omega/models/token_merging.py:40-59, 253-426).
+  fast_*     build_fastvggt_plan + TokenPlan.compact / restore (token_merging.py:143-196, 1045-1122).
+  topk_*     (q.bf16 @ basis.bf16).topk(4) and .max(-1) (vggt_omega/models/sparse_convex.py:264).
+  pg_*       _adaptive_fit in "adaptive_convex" mode (sparse_convex.py:128-160): top-4 supports
+             and 32 projected-gradient steps.
+  as_*       _convex_fit (sparse_convex.py:2260-2305): exact 15-active-set solve.
+  rand_*     torch.rand with a seeded CPU generator (the anchor draw of the planners).
+
+Usage: python tests/golden/make_golden.py [--reference PATH]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+OUT = Path(__file__).resolve().parent / "golden.npz"
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu()
+    if t.dtype == torch.bfloat16:
+        return t.float().numpy()
+    return t.numpy()
+
+
+def make_plan(WeightedBilinearTokenPlan, deterministic_weighted_normalizer, gen, N, K, frames,
+              special_per_frame, preserve_queries):
+    tokens_per_frame = N // frames
+    special = torch.cat([torch.arange(f * tokens_per_frame, f * tokens_per_frame + special_per_frame)
+                         for f in range(frames)])
+    others = torch.tensor([i for i in range(N) if i not in set(special.tolist())])
+    perm = others[torch.randperm(others.numel(), generator=gen)]
+    keep = torch.sort(torch.cat([special, perm[: K - special.numel()]])).values
+    mask = torch.ones(N, dtype=torch.bool)
+    mask[keep] = False
+    source = torch.nonzero(mask).flatten()
+    S = source.numel()
+    parent = torch.stack([torch.randperm(K, generator=gen)[:4] for _ in range(S)])
+    w = torch.softmax(torch.randn(S, 4, generator=gen), dim=-1)
+    norm = deterministic_weighted_normalizer(parent[None], w[None], K)
+    original_to_compact = torch.full((N,), -1, dtype=torch.long)
+    original_to_compact[keep] = torch.arange(K)
+    plan = WeightedBilinearTokenPlan(
+        keep=keep[None], source_original=source[None], source_parent_compact=parent[None],
+        source_pool_weights=w[None], source_restore_weights=w[None], original_tokens=N,
+        normalizer=norm, preserve_queries=preserve_queries,
+        preserve_destination_keys=preserve_queries, dense_special_queries=True,
+        special_query_original=special, special_query_compact=original_to_compact[special],
+        key_log_mass=norm[..., 0].log(),
+    )
+    return plan, dict(keep=keep, source=source, parent=parent, weights=w, normalizer=norm[0, :, 0],
+                      special=special, special_compact=original_to_compact[special])
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("REFERENCE_ROOT", "/root/reference"))
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from vggt_omega.models.layers.attention import SelfAttention
+    from vggt_omega.models.sparse_convex import _adaptive_fit, _convex_fit
+    from vggt_omega.models.token_merging import (TokenPlan, WeightedBilinearTokenPlan,
+                                                 build_fastvggt_plan,
+                                                 deterministic_weighted_normalizer)
+
+    torch.set_num_threads(1)  # fixed reduction order in the CPU kernels
+    out: dict[str, np.ndarray] = {}
+
+    # ---------------- block: the global-attention call site ----------------
+    for tag, preserve in (("block_compact_q", False), ("block_preserve_q", True)):
+        torch.manual_seed(1 if preserve else 0)
+        gen = torch.Generator().manual_seed(11 if preserve else 10)
+        dim, heads, frames, tpf, special = 128, 2, 2, 56, 5
+        N, K = frames * tpf, 40
+        attn = SelfAttention(dim, num_heads=heads, qkv_bias=True, proj_bias=True, mask_k_bias=True,
+                             use_qk_norm=True).eval()
+        with torch.no_grad():
+            for p in attn.parameters():
+                p.copy_(torch.randn(p.shape, generator=gen) * (0.2 if p.ndim > 1 else 0.5))
+        plan, pd = make_plan(WeightedBilinearTokenPlan, deterministic_weighted_normalizer, gen, N, K,
+                             frames, special, preserve)
+        x = torch.randn(1, N, dim, generator=gen)
+        with torch.no_grad():
+            y = attn(x, token_plan=plan)
+        out[f"{tag}_x"] = _np(x)
+        out[f"{tag}_y"] = _np(y)
+        for name, p in attn.named_parameters():
+            out[f"{tag}_p_{name}"] = _np(p)
+        out[f"{tag}_p_qkv.bias_mask"] = _np(attn.qkv.bias_mask)
+        for k_, v_ in pd.items():
+            out[f"{tag}_{k_}"] = _np(v_)
+
+    # ---------------- plan ops ----------------
+    gen = torch.Generator().manual_seed(20)
+    N, K, Cc = 240, 64, 64
+    plan, pd = make_plan(WeightedBilinearTokenPlan, deterministic_weighted_normalizer, gen, N, K, 3, 5, False)
+    v32 = torch.randn(1, N, Cc, generator=gen)
+    y32 = torch.randn(1, K, Cc, generator=gen)
+    out["plan_value"] = _np(v32)
+    out["plan_compact_f32"] = _np(plan.compact(v32))
+    out["plan_compact_bf16"] = _np(plan.compact(v32.bfloat16()))
+    out["plan_y"] = _np(y32)
+    out["plan_restore_f32"] = _np(plan.restore(y32))
+    out["plan_restore_bf16"] = _np(plan.restore(y32.bfloat16()))
+    for k_, v_ in pd.items():
+        out[f"plan_{k_}"] = _np(v_)
+
+    # ---------------- FastVGGT plan + TokenPlan ----------------
+    gen = torch.Generator().manual_seed(30)
+    frames, hw, pts = 3, (8, 8), 5
+    tpf = pts + hw[0] * hw[1]
+    tokens = torch.randn(1, frames * tpf, 64, generator=gen)
+    fplan = build_fastvggt_plan(tokens, frames=frames, tokens_per_frame=tpf, patch_token_start=pts,
+                                patch_hw=hw, merge_ratio=0.5, protect_ratio=0.1, seed=3)
+    value = torch.randn(1, frames * tpf, 32, generator=gen)
+    compacted = fplan.compact(value)
+    out["fast_tokens"] = _np(tokens)
+    out["fast_keep"] = _np(fplan.keep[0])
+    out["fast_inverse"] = _np(fplan.inverse[0])
+    out["fast_value"] = _np(value)
+    out["fast_compact"] = _np(compacted)
+    out["fast_restore"] = _np(fplan.restore(compacted))
+
+    # ---------------- bf16 top-4 / argmax ----------------
+    gen = torch.Generator().manual_seed(40)
+    q = F.normalize(torch.randn(96, 64, generator=gen), dim=-1).bfloat16()
+    b = F.normalize(torch.randn(160, 64, generator=gen), dim=-1).bfloat16()
+    score = q @ b.T
+    tv, ti = score.topk(4, dim=-1)
+    mv, mi = score.max(dim=-1)
+    out["topk_q"] = _np(q)
+    out["topk_b"] = _np(b)
+    out["topk_values"] = _np(tv)
+    out["topk_indices"] = _np(ti)
+    out["topk_max_values"] = _np(mv)
+    out["topk_max_indices"] = _np(mi)
+
+    # ---------------- projected gradient (adaptive_convex) ----------------
+    gen = torch.Generator().manual_seed(50)
+    feats = F.normalize(torch.randn(160, 48, generator=gen), dim=-1)
+    basis_ids = torch.randperm(160, generator=gen)[:40]
+    fit = _adaptive_fit(feats, basis_ids, max_support=4, mode="adaptive_convex", coefficient_limit=1.0,
+                        chunk=1024, steps=32)
+    out["pg_features"] = _np(feats)
+    out["pg_basis_ids"] = _np(basis_ids)
+    for k_ in ("support_ids", "weights", "cosine"):
+        if k_ in fit:
+            out[f"pg_{k_}"] = _np(fit[k_])
+
+    # ---------------- exact active set ----------------
+    gen = torch.Generator().manual_seed(60)
+    src = F.normalize(torch.randn(128, 32, generator=gen), dim=-1)
+    sup = F.normalize(src[:, None, :] + 0.7 * torch.randn(128, 4, 32, generator=gen), dim=-1)
+    cos, alpha = _convex_fit(src, sup)
+    out["as_source"] = _np(src)
+    out["as_supports"] = _np(sup)
+    out["as_alpha"] = _np(alpha)
+    out["as_cosine"] = _np(cos)
+
+    # ---------------- CPU generator stream ----------------
+    out["rand_seed3"] = _np(torch.rand(2, 4, 4, 2, generator=torch.Generator(device="cpu").manual_seed(3)))
+
+    np.savez_compressed(OUT, **out)
+    print(f"wrote {OUT} ({OUT.stat().st_size / 1024:.0f} KB, {len(out)} arrays)")
+    print("adaptive fit keys:", sorted(fit.keys()))
+
+
+if __name__ == "__main__":
+    main()

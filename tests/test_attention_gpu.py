@@ -1,0 +1,113 @@
+"""Mass-bias attention on the GPU (tcgen05 path for bf16 / fp16, FMA path for fp32) against
+the oracle restatement of vggt_omega/models/mass_bias_attention.py:85-129, through the C ABI."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import TORCH_DTYPE, assert_close, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(seed, B, H, Nq, Nk, dtype, oracle, mass_max=50):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, H, Nq, 64)).astype(np.float32)
+    k = rng.standard_normal((B, H, Nk, 64)).astype(np.float32)
+    v = rng.standard_normal((B, H, Nk, 64)).astype(np.float32)
+    mass = rng.integers(1, mass_max, size=Nk).astype(np.float32)
+    log_mass = np.log(mass).astype(np.float32)
+    q, k, v = (oracle.round_to(t, dtype) for t in (q, k, v))
+    return q, k, v, log_mass
+
+
+def _run(pkg, q, k, v, log_mass, dtype, device, bias_dtype=torch.float32):
+    td = TORCH_DTYPE[dtype]
+    qt, kt, vt = (torch.from_numpy(t).to(device=device, dtype=td) for t in (q, k, v))
+    lm = None if log_mass is None else torch.from_numpy(log_mass).to(device=device, dtype=bias_dtype)
+    out = pkg.mass_bias_attention(qt, kt, vt, lm)
+    torch.cuda.synchronize()
+    assert out.dtype == td
+    return to_np(out)
+
+
+SHAPES = [
+    (1, 1, 1, 1),      # single query, single key
+    (1, 2, 5, 7),      # everything inside one partial tile
+    (1, 3, 130, 129),  # ragged query and key tails
+    (2, 2, 257, 300),  # batch > 1, three query tiles, three key tiles
+    (1, 4, 1029, 1029),
+    (1, 2, 640, 2176),  # many key tiles (pipeline phases wrap several times)
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_against_oracle(pkg, oracle, cuda_device, dtype, shape):
+    B, H, Nq, Nk = shape
+    q, k, v, lm = _inputs(sum(shape), B, H, Nq, Nk, dtype, oracle)
+    out = _run(pkg, q, k, v, lm, dtype, cuda_device)
+    ref = oracle.mass_bias_attention(q, k, v, lm, dtype=dtype, round_p=dtype != "f32")
+    assert_close(out, ref, dtype)
+    assert pkg.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("bias_dtype", [torch.float32, torch.bfloat16])
+def test_bias_rounding_and_no_bias(pkg, oracle, cuda_device, bias_dtype):
+    q, k, v, lm = _inputs(7, 1, 2, 300, 333, "bf16", oracle, mass_max=5000)
+    out = _run(pkg, q, k, v, lm, "bf16", cuda_device, bias_dtype=bias_dtype)
+    ref = oracle.mass_bias_attention(q, k, v, lm, dtype="bf16", round_p=True)
+    assert_close(out, ref, "bf16")
+    # None bias = plain softmax attention (the dense special-query call)
+    out0 = _run(pkg, q, k, v, None, "bf16", cuda_device)
+    assert_close(out0, oracle.mass_bias_attention(q, k, v, None, dtype="bf16", round_p=True), "bf16")
+
+
+def test_config1_shape_fp32(pkg, oracle, cuda_device):
+    """Config 1 (fp32): N=4116 queries over M=1029 merged keys with integer masses, 16 heads
+    (4 heads checked against the oracle to keep the CPU side short)."""
+    c1 = oracle.c1_inputs(seed=0)
+    q, k, v = c1["q"][:, :4], c1["k"][:, :4], c1["v"][:, :4]
+    out = _run(pkg, q, k, v, c1["log_mass"], "f32", cuda_device)
+    ref = oracle.mass_bias_attention(q, k, v, c1["log_mass"])
+    assert_close(out, ref, "f32")
+
+
+def test_strided_views_and_autocast(pkg, oracle, cuda_device):
+    """q/k/v as views of an interleaved [B, N, 3, H, 64] qkv buffer (the layout of the
+    attention layer), fp32 under bf16 autocast -> bf16 output, as the reference wrapper."""
+    rng = np.random.default_rng(3)
+    B, N, H = 1, 333, 4
+    qkv = torch.from_numpy(rng.standard_normal((B, N, 3, H, 64)).astype(np.float32)).to(cuda_device)
+    q, k, v = (t.transpose(1, 2) for t in qkv.unbind(2))
+    lm = torch.from_numpy(np.log(rng.integers(1, 9, N)).astype(np.float32)).to(cuda_device)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = pkg.mass_bias_attention(q, k, v, lm)
+    assert out.dtype == torch.bfloat16
+    qb, kb, vb = (oracle.round_bf16(to_np(t)) for t in (q, k, v))
+    ref = oracle.mass_bias_attention(qb, kb, vb, to_np(lm), dtype="bf16", round_p=True)
+    assert_close(to_np(out), ref, "bf16")
+    # the returned [B,H,N,64] tensor is a view of a token-major buffer
+    assert out.transpose(1, 2).is_contiguous()
+
+
+def test_output_into_strided_buffer(pkg, oracle, cuda_device):
+    q, k, v, lm = _inputs(11, 1, 2, 200, 150, "bf16", oracle)
+    dev = cuda_device
+    qt, kt, vt = (torch.from_numpy(t).to(dev, torch.bfloat16) for t in (q, k, v))
+    big = torch.zeros(1, 200, 4, 64, device=dev, dtype=torch.bfloat16)
+    out = big[:, :, 1:3].transpose(1, 2)  # heads interleaved with untouched columns
+    pkg.mass_bias_attention_into(qt, kt, vt, torch.from_numpy(lm).to(dev), out)
+    torch.cuda.synchronize()
+    ref = oracle.mass_bias_attention(q, k, v, lm, dtype="bf16", round_p=True)
+    assert_close(to_np(out), ref, "bf16")
+    assert torch.count_nonzero(big[:, :, 0]) == 0 and torch.count_nonzero(big[:, :, 3]) == 0
+
+
+def test_errors(pkg, cuda_device):
+    q = torch.zeros(1, 2, 8, 64, device=cuda_device, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="log_key_mass length"):
+        pkg.mass_bias_attention(q, q, q, torch.zeros(7, device=cuda_device))
+    with pytest.raises(ValueError, match="head_dim"):
+        pkg.mass_bias_attention(q[..., :32], q[..., :32], q[..., :32], torch.zeros(8, device=cuda_device))

@@ -1,0 +1,78 @@
+"""CPU checks of the C ABI: the library loads, exports exactly the symbols that
+include/vggt_b200.h declares, and rejects bad arguments on the host (before any launch) with
+the reference's exception types."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+import torch
+
+from conftest import REPO
+
+HEADER = REPO / "include" / "vggt_b200.h"
+
+
+def _declared() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"VB200_API\s+[\w\s\*]+?\b(vb200_\w+)\s*\(", text))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "vb200_mass_bias_attention" in names and "vb200_proj_gather" in names
+    assert len(names) >= 14
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.load_library()
+    for name in sorted(_declared()):
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+
+
+def test_binding_covers_header(pkg):
+    assert set(pkg._clib.EXPORTED_SYMBOLS) == _declared()
+
+
+def test_version_and_error_text(pkg):
+    lib = pkg.load_library()
+    assert lib.vb200_version() >= 1
+    # head_dim 32 is rejected on the host before any CUDA call
+    strides = (ctypes.c_int64 * 3)(1, 1, 1)
+    rc = lib.vb200_mass_bias_attention(1, 16, 16, 16, None, 0, 16, 1, 1, 1, 1, 32, strides, strides,
+                                       strides, strides, 16, 1 << 20, None)
+    assert rc == pkg._clib.EINVAL
+    assert b"head_dim=64" in lib.vb200_last_error()
+    with pytest.raises(ValueError, match="head_dim"):
+        pkg._clib.check(rc, "mass_bias_attention")
+
+
+def test_reference_exceptions_without_gpu(pkg):
+    q = torch.zeros(1, 2, 4, 32)
+    with pytest.raises(ValueError, match="head_dim=64"):
+        pkg.mass_bias_attention(q, q, q, torch.zeros(4))
+    with pytest.raises(ValueError, match="batch, heads"):
+        pkg.mass_bias_attention(q[0], q[0], q[0], torch.zeros(4))
+    q = torch.zeros(1, 2, 4, 64)
+    with pytest.raises(ValueError, match="incompatible"):
+        pkg.mass_bias_attention(q, q[:, :, :3], q, torch.zeros(3))
+    # well-formed CPU tensors: no CPU fallback
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.mass_bias_attention(q, q, q, torch.zeros(4))
+    with pytest.raises(ValueError, match="Gram"):
+        pkg.four_support_projected_gradient(torch.zeros(3, 3, 3), torch.zeros(3, 4))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.four_support_projected_gradient(torch.zeros(3, 4, 4), torch.zeros(3, 4))
+    with pytest.raises(RuntimeError):
+        pkg.streaming_top4(torch.zeros(4, 64), torch.zeros(64, 8))
+
+
+def test_host_side_size_checks(pkg):
+    lib = pkg.load_library()
+    assert lib.vb200_mass_bias_attention_workspace_size(1) == 512
+    assert lib.vb200_mass_bias_attention_workspace_size(129) == 1024
+    rc = lib.vb200_proj_gather(1, None, 0, None, 0, None, None, None, 0, 9, None, 0, 0, 8, 0, None)
+    assert rc == pkg._clib.EINVAL and b"corners" in lib.vb200_last_error()
+    rc = lib.vb200_sim_topk(None, 0, None, 0, 4, 4, 64, 3, None, None, 1, None, None, None)
+    assert rc != 0

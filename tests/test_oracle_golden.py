@@ -1,0 +1,138 @@
+"""Pin the CPU oracle to the reference: every golden vector in tests/golden/golden.npz was
+produced by the reference's own PyTorch code (tests/golden/make_golden.py)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+
+def _params(golden, tag):
+    prefix = f"{tag}_p_"
+    return {k[len(prefix):]: v for k, v in golden.items() if k.startswith(prefix)}
+
+
+def _plan(golden, tag):
+    return {k: golden[f"{tag}_{k}"] for k in
+            ("keep", "source", "parent", "weights", "normalizer", "special", "special_compact")}
+
+
+@pytest.mark.parametrize("tag,preserve", [("block_compact_q", False), ("block_preserve_q", True)])
+def test_global_attention_block(golden, oracle, tag, preserve):
+    y = oracle.global_attention_forward(golden[f"{tag}_x"][0], _params(golden, tag), _plan(golden, tag),
+                                        heads=2, preserve_queries=preserve)
+    ref = golden[f"{tag}_y"][0]
+    np.testing.assert_allclose(y, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_normalizer(golden, oracle):
+    mass = oracle.normalizer(golden["plan_parent"], golden["plan_weights"], len(golden["plan_keep"]))
+    np.testing.assert_allclose(mass, golden["plan_normalizer"], rtol=1e-6, atol=1e-6)
+    # known answer: sum of (mass - 1) equals the total weight
+    assert abs((mass - 1).sum() - golden["plan_weights"].sum()) < 1e-3
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_compact(golden, oracle, dtype):
+    value = golden["plan_value"][0]
+    if dtype == "bf16":
+        value = oracle.round_bf16(value)
+    out = oracle.compact(value, golden["plan_keep"], golden["plan_source"], golden["plan_parent"],
+                         golden["plan_weights"], golden["plan_normalizer"], dtype=dtype)
+    ref = golden[f"plan_compact_{dtype}"][0]
+    if dtype == "f32":
+        np.testing.assert_allclose(out, ref, rtol=1e-6, atol=1e-6)
+    else:  # one bf16 ulp where the fp32 accumulation order flips a rounding
+        np.testing.assert_allclose(out, ref, rtol=2 ** -7, atol=1e-6)
+        assert np.mean(out == ref) > 0.99
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_restore(golden, oracle, dtype):
+    y = golden["plan_y"][0]
+    if dtype == "bf16":
+        y = oracle.round_bf16(y)
+    out = oracle.restore(y, golden["plan_keep"], golden["plan_source"], golden["plan_parent"],
+                         golden["plan_weights"], golden["plan_value"].shape[1], dtype=dtype)
+    ref = golden[f"plan_restore_{dtype}"][0]
+    if dtype == "f32":
+        np.testing.assert_allclose(out, ref, rtol=1e-6, atol=1e-6)
+    else:
+        np.testing.assert_array_equal(out, ref)
+
+
+def test_torch_cpu_rand(golden, oracle):
+    ref = golden["rand_seed3"].reshape(-1)
+    np.testing.assert_array_equal(oracle.torch_cpu_rand(3, ref.size), ref)
+
+
+def test_fastvggt_plan_and_token_plan(golden, oracle):
+    keep, inverse, *_ = oracle.fastvggt_plan(golden["fast_tokens"][0], frames=3, tokens_per_frame=69,
+                                             patch_token_start=5, patch_hw=(8, 8), merge_ratio=0.5,
+                                             protect_ratio=0.1, seed=3)
+    np.testing.assert_array_equal(keep, golden["fast_keep"])
+    np.testing.assert_array_equal(inverse, golden["fast_inverse"])
+    comp = oracle.token_plan_compact(golden["fast_value"][0], inverse, len(keep))
+    np.testing.assert_allclose(comp, golden["fast_compact"][0], rtol=1e-6, atol=1e-6)
+    rest = oracle.token_plan_restore(golden["fast_compact"][0], inverse)
+    np.testing.assert_array_equal(rest, golden["fast_restore"][0])
+
+
+def test_similarity_topk(golden, oracle):
+    values, idx = oracle.similarity_topk(golden["topk_q"], golden["topk_b"], 4)
+    ref_v, ref_i = golden["topk_values"], golden["topk_indices"]
+    np.testing.assert_array_equal(values, ref_v)
+    # indices agree except where the reference broke an exact bf16 tie differently
+    scores = oracle.topk_scores(golden["topk_q"], golden["topk_b"])
+    chosen = np.take_along_axis(scores, idx, axis=1)
+    chosen_ref = np.take_along_axis(scores, ref_i.astype(np.int64), axis=1)
+    np.testing.assert_array_equal(chosen, chosen_ref)
+    assert np.mean(idx == ref_i) > 0.95
+    v1, i1 = oracle.similarity_topk(golden["topk_q"], golden["topk_b"], 1)
+    np.testing.assert_array_equal(v1[:, 0], golden["topk_max_values"])
+    assert np.all(scores[np.arange(len(i1)), golden["topk_max_indices"]] == v1[:, 0])
+
+
+def test_projected_gradient(golden, oracle):
+    feats = golden["pg_features"].astype(np.float64)
+    basis_ids = golden["pg_basis_ids"]
+    basis = oracle.round_bf16(feats[basis_ids].astype(np.float32))
+    query = oracle.round_bf16(feats.astype(np.float32))
+    _, local = oracle.similarity_topk(query, basis, 4)
+    ids = basis_ids[local]
+    ref_ids = golden["pg_support_ids"].astype(np.int64)
+    # supports agree up to exact bf16 ties: the chosen scores are identical
+    scores = oracle.topk_scores(query, oracle.round_bf16(feats.astype(np.float32)))
+    np.testing.assert_array_equal(np.take_along_axis(scores, ids, 1), np.take_along_axis(scores, ref_ids, 1))
+    assert np.mean(ids == ref_ids) > 0.95
+    sup = feats[ref_ids]  # [R,4,D]
+    gram = np.einsum("rid,rjd->rij", sup, sup).astype(np.float32)
+    rhs = np.einsum("rid,rd->ri", sup, feats).astype(np.float32)
+    alpha = oracle.projected_gradient(gram, rhs, 32)
+    np.testing.assert_allclose(alpha, golden["pg_weights"], rtol=1e-4, atol=2e-5)
+
+
+def test_active_set(golden, oracle):
+    src = golden["as_source"].astype(np.float64)
+    sup = golden["as_supports"].astype(np.float64)
+    gram = np.einsum("rid,rjd->rij", sup, sup)
+    rhs = np.einsum("rid,rd->ri", sup, src)
+    alpha = oracle.active_set(gram, rhs, 1e-4)
+    np.testing.assert_allclose(alpha, golden["as_alpha"], rtol=1e-3, atol=2e-4)
+
+
+def test_mass_bias_attention_known_answers(oracle):
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((1, 2, 5, 64)).astype(np.float32)
+    k = rng.standard_normal((1, 2, 7, 64)).astype(np.float32)
+    v = rng.standard_normal((1, 2, 7, 64)).astype(np.float32)
+    # duplicating a key m times equals one key with log-mass log(m)
+    kd = np.concatenate([k, k[:, :, :1], k[:, :, :1]], axis=2)
+    vd = np.concatenate([v, v[:, :, :1], v[:, :, :1]], axis=2)
+    dup = oracle.mass_bias_attention(q, kd, vd)
+    lm = np.zeros(7, np.float32)
+    lm[0] = np.log(3.0)
+    biased = oracle.mass_bias_attention(q, k, v, lm)
+    np.testing.assert_allclose(biased, dup, rtol=1e-6, atol=1e-7)
+    # zero log-mass is plain softmax attention
+    np.testing.assert_allclose(oracle.mass_bias_attention(q, k, v, np.zeros(7, np.float32)),
+                               oracle.mass_bias_attention(q, k, v), rtol=1e-12)
