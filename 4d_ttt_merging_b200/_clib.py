@@ -29,6 +29,7 @@ _p_i64 = ctypes.POINTER(ctypes.c_int64)
 _SIGNATURES = {
     "vb200_version": (_c_int, []),
     "vb200_last_error": (ctypes.c_char_p, []),
+    "vb200_launch_count": (ctypes.c_ulonglong, []),
     "vb200_device_error_flags": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
     "vb200_mass_bias_attention_workspace_size": (_c_size, [_c_i64]),
     "vb200_mass_bias_attention": (
@@ -60,6 +61,15 @@ _SIGNATURES = {
         _c_int,
         [_c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_i64, _c_vp,
          _c_vp, _c_vp],
+    ),
+    "vb200_merge_assign_workspace_size": (_c_size, [_c_i64, _c_i64]),
+    "vb200_merge_assign": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_size, _c_vp],
+    ),
+    "vb200_support_fit": (
+        _c_int,
+        [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_int, _c_vp],
     ),
     "vb200_four_support_projected_gradient": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_vp]),
     "vb200_four_support_active_set": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_float, _c_vp]),

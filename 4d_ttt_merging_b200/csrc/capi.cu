@@ -2,6 +2,7 @@
 // tensor-map encoder shared by the kernels.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -11,7 +12,10 @@ namespace vb200 {
 
 namespace {
 thread_local char g_last_error[1024] = "";
+std::atomic<unsigned long long> g_launches{0};
 }
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int set_error(int code, const char* fmt, ...) {
   va_list ap;
@@ -84,13 +88,17 @@ extern "C" {
 
 int vb200_version(void) { return 1; }
 
+unsigned long long vb200_launch_count(void) {
+  return vb200::g_launches.load(std::memory_order_relaxed);
+}
+
 const char* vb200_last_error(void) { return vb200::g_last_error; }
 
 int vb200_device_error_flags(unsigned* flags, int clear) {
   if (flags == nullptr) return vb200::set_error(VB200_EINVAL, "flags must not be NULL");
   VB200_CHECK_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
   *flags = vb200::attention_error_word(clear) | vb200::projection_error_word(clear) |
-           vb200::merge_error_word(clear);
+           vb200::merge_error_word(clear) | vb200::plan_error_word(clear);
   VB200_CHECK_CUDA(cudaGetLastError(), "reading device error words");
   return VB200_OK;
 }

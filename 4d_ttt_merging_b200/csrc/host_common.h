@@ -26,6 +26,7 @@ int encode_tiled_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, cons
 unsigned attention_error_word(int clear);
 unsigned projection_error_word(int clear);
 unsigned merge_error_word(int clear);
+unsigned plan_error_word(int clear);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -37,7 +38,15 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
     if (e_ != cudaSuccess) return vb200::cuda_error(e_, what); \
   } while (0)
 
-#define VB200_CHECK_LAUNCH(what) VB200_CHECK_CUDA(cudaGetLastError(), what)
+namespace vb200 {
+void count_launch();  // one of this library's kernels was launched
+}
+
+#define VB200_CHECK_LAUNCH(what)                     \
+  do {                                               \
+    vb200::count_launch();                           \
+    VB200_CHECK_CUDA(cudaGetLastError(), what);      \
+  } while (0)
 
 #define VB200_REQUIRE(cond, ...)                                     \
   do {                                                               \

@@ -1,0 +1,302 @@
+// Device-side plan construction for the merge step (no host synchronisation):
+//
+//   merge_assign  ranking + keep / inverse maps of build_fastvggt_plan
+//                 (vggt_omega/models/token_merging.py:1112-1121): sources are ordered by their
+//                 best score (stable, descending), the first `removed` are merged into their
+//                 argmax destination, the survivors are renumbered in token order.
+//   support_fit   Gram / right-hand side of each source's four supports
+//                 (vggt_omega/models/sparse_convex.py:2314-2316: gram = S S^T, rhs = S x) and,
+//                 optionally, the four-support projected-gradient solve
+//                 (sparse_convex_kernels.py:214-280) fused in the same kernel.
+#include <cub/cub.cuh>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace vb200 {
+namespace {
+
+static __device__ unsigned g_plan_err;
+
+__global__ void iota_kernel(int32_t* v, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) v[i] = static_cast<int32_t>(i);
+}
+
+// flags[n] = 1 for kept tokens; remap[n] = original id of the destination a removed token
+// merges into.
+__global__ void mark_removed_kernel(const int32_t* __restrict__ order, const int64_t* __restrict__ target,
+                                    const int64_t* __restrict__ source_idx, const int64_t* __restrict__ dest_idx,
+                                    long long removed, long long Dn, long long total,
+                                    int32_t* __restrict__ kept_flag, int64_t* __restrict__ remap) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= removed) return;
+  const int32_t s = order[i];
+  const int64_t n = source_idx[s];
+  const int64_t t = target[s];
+  if (n < 0 || n >= total || t < 0 || t >= Dn || dest_idx[t] < 0 || dest_idx[t] >= total) {
+    atomicOr(&g_plan_err, kErrBadArgument);
+    return;
+  }
+  kept_flag[n] = 0;
+  remap[n] = dest_idx[t];
+}
+
+__global__ void fill_ones_kernel(int32_t* v, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) v[i] = 1;
+}
+
+__global__ void keep_inverse_kernel(const int32_t* __restrict__ kept_flag, const int32_t* __restrict__ compact,
+                                    const int64_t* __restrict__ remap, long long total, long long keep_len,
+                                    int64_t* __restrict__ keep, int64_t* __restrict__ inverse) {
+  const long long n = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (n >= total) return;
+  if (kept_flag[n]) {
+    if (compact[n] >= keep_len) {  // duplicate source ids removed fewer tokens than declared
+      atomicOr(&g_plan_err, kErrBadArgument);
+      inverse[n] = -1;
+      return;
+    }
+    keep[compact[n]] = n;
+    inverse[n] = compact[n];
+  } else {
+    const int64_t t = remap[n];
+    inverse[n] = kept_flag[t] ? compact[t] : -1;  // a destination is never removed
+  }
+}
+
+struct AssignWorkspace {
+  size_t keys_out, vals_in, vals_out, flags, compact, remap, sort_tmp, scan_tmp, total;
+  size_t sort_bytes, scan_bytes;
+};
+
+AssignWorkspace assign_layout(int64_t S, int64_t total) {
+  const int s = static_cast<int>(S > 0 ? S : 1);
+  const int t = static_cast<int>(total > 0 ? total : 1);
+  size_t sort_bytes = 0, scan_bytes = 0;
+  cub::DeviceRadixSort::SortPairsDescending(nullptr, sort_bytes, static_cast<float*>(nullptr),
+                                            static_cast<float*>(nullptr), static_cast<int32_t*>(nullptr),
+                                            static_cast<int32_t*>(nullptr), s);
+  cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int32_t*>(nullptr),
+                                static_cast<int32_t*>(nullptr), t);
+  AssignWorkspace w{};
+  size_t off = 0;
+  auto take = [&](size_t b) { const size_t o = off; off = align_up(off + b, 256); return o; };
+  w.keys_out = take(static_cast<size_t>(s) * 4);
+  w.vals_in = take(static_cast<size_t>(s) * 4);
+  w.vals_out = take(static_cast<size_t>(s) * 4);
+  w.flags = take(static_cast<size_t>(t) * 4);
+  w.compact = take(static_cast<size_t>(t) * 4);
+  w.remap = take(static_cast<size_t>(t) * 8);
+  w.sort_tmp = take(sort_bytes);
+  w.scan_tmp = take(scan_bytes);
+  w.total = off;
+  w.sort_bytes = sort_bytes;
+  w.scan_bytes = scan_bytes;
+  return w;
+}
+
+// One warp per source: the 4x4 Gram of its supports and the 4 support-source products,
+// accumulated in fp32 over the channels (lane-strided, then a fixed butterfly), and with
+// steps > 0 the projected-gradient solve by lane 0.
+template <typename T>
+__global__ void support_fit_kernel(const T* __restrict__ feat, long long rows, long long fs,
+                                   const int64_t* __restrict__ src_rows,
+                                   const int64_t* __restrict__ parent_rows, long long S, int D,
+                                   float* __restrict__ gram, float* __restrict__ rhs,
+                                   float* __restrict__ alpha, int steps) {
+  constexpr int V = 16 / sizeof(T);
+  const long long s = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (s >= S) return;
+  long long r[5];
+  r[0] = src_rows ? src_rows[s] : s;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) r[c + 1] = parent_rows[s * 4 + c];
+  bool bad = false;
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+    if (r[c] < 0 || r[c] >= rows) { bad = true; r[c] = 0; }
+  }
+  if (bad && lane == 0) atomicOr(&g_plan_err, kErrBadArgument);
+  // products: g[i][j] for i <= j (10) + rhs[i] (4)
+  float acc[14];
+#pragma unroll
+  for (int i = 0; i < 14; ++i) acc[i] = 0.f;
+  for (int v0 = lane * V; v0 < D; v0 += 32 * V) {
+    float x[5][V];
+#pragma unroll
+    for (int c = 0; c < 5; ++c) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(feat + r[c] * fs + v0));
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int q = 0; q < V; ++q) x[c][q] = to_f32<T>(e[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < V; ++q) {
+      int idx = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = i; j < 4; ++j) {
+          acc[idx] = fmaf(x[i + 1][q], x[j + 1][q], acc[idx]);
+          ++idx;
+        }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[10 + i] = fmaf(x[i + 1][q], x[0][q], acc[10 + i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 14; ++i)
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
+  if (lane != 0) return;
+  float G[16], R4[4];
+  {
+    int idx = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = i; j < 4; ++j) { G[i * 4 + j] = acc[idx]; G[j * 4 + i] = acc[idx]; ++idx; }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) R4[i] = acc[10 + i];
+  }
+  if (gram) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) gram[s * 16 + i] = G[i];
+  }
+  if (rhs) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) rhs[s * 4 + i] = R4[i];
+  }
+  if (alpha == nullptr) return;
+  // projected gradient on the simplex (same iteration as the standalone solver)
+  const float n0 = fabsf(G[0]) + fabsf(G[1]) + fabsf(G[2]) + fabsf(G[3]);
+  const float n1 = fabsf(G[4]) + fabsf(G[5]) + fabsf(G[6]) + fabsf(G[7]);
+  const float n2 = fabsf(G[8]) + fabsf(G[9]) + fabsf(G[10]) + fabsf(G[11]);
+  const float n3 = fabsf(G[12]) + fabsf(G[13]) + fabsf(G[14]) + fabsf(G[15]);
+  const float step = 0.95f / fmaxf(fmaxf(fmaxf(n0, n1), fmaxf(n2, n3)), 1.0e-4f);
+  float a0 = 1.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  for (int it = 0; it < steps; ++it) {
+    const float p0 = a0 - step * (G[0] * a0 + G[1] * a1 + G[2] * a2 + G[3] * a3 - R4[0]);
+    const float p1 = a1 - step * (G[4] * a0 + G[5] * a1 + G[6] * a2 + G[7] * a3 - R4[1]);
+    const float p2 = a2 - step * (G[8] * a0 + G[9] * a1 + G[10] * a2 + G[11] * a3 - R4[2]);
+    const float p3 = a3 - step * (G[12] * a0 + G[13] * a1 + G[14] * a2 + G[15] * a3 - R4[3]);
+    float s0 = fmaxf(p0, p1), s1 = fminf(p0, p1), s2 = fmaxf(p2, p3), s3 = fminf(p2, p3), t;
+    t = fmaxf(s0, s2); s2 = fminf(s0, s2); s0 = t;
+    t = fmaxf(s1, s3); s3 = fminf(s1, s3); s1 = t;
+    t = fmaxf(s1, s2); s2 = fminf(s1, s2); s1 = t;
+    float theta = s0 - 1.f;
+    const float th2 = (s0 + s1 - 1.f) * 0.5f;
+    theta = s1 > th2 ? th2 : theta;
+    const float th3 = (s0 + s1 + s2 - 1.f) / 3.f;
+    theta = s2 > th3 ? th3 : theta;
+    const float th4 = (s0 + s1 + s2 + s3 - 1.f) * 0.25f;
+    theta = s3 > th4 ? th4 : theta;
+    a0 = fmaxf(p0 - theta, 0.f);
+    a1 = fmaxf(p1 - theta, 0.f);
+    a2 = fmaxf(p2 - theta, 0.f);
+    a3 = fmaxf(p3 - theta, 0.f);
+  }
+  alpha[s * 4 + 0] = a0;
+  alpha[s * 4 + 1] = a1;
+  alpha[s * 4 + 2] = a2;
+  alpha[s * 4 + 3] = a3;
+}
+
+inline unsigned blocks(long long n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
+
+}  // namespace
+
+unsigned plan_error_word(int clear) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_plan_err, sizeof(v));
+  if (clear) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_plan_err, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace vb200
+
+using namespace vb200;
+
+extern "C" size_t vb200_merge_assign_workspace_size(int64_t S, int64_t total) {
+  if (S < 0 || total < 0) return 0;
+  return assign_layout(S, total).total;
+}
+
+extern "C" int vb200_merge_assign(const float* best, const int64_t* target, const int64_t* source_idx,
+                                  const int64_t* dest_idx, int64_t S, int64_t Dn, int64_t total,
+                                  int64_t removed, int64_t* keep, int64_t* inverse, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  VB200_REQUIRE(S >= 0 && Dn >= 0 && total >= 0 && removed >= 0 && removed <= S && S <= total,
+                "merge_assign: bad sizes S=%lld Dn=%lld total=%lld removed=%lld", (long long)S,
+                (long long)Dn, (long long)total, (long long)removed);
+  VB200_REQUIRE(total < (1ll << 31), "merge_assign: total exceeds the int32 index range");
+  if (total == 0) return VB200_OK;
+  VB200_REQUIRE(keep && inverse, "merge_assign: null output");
+  VB200_REQUIRE(removed == 0 || (best && target && source_idx && dest_idx && Dn > 0),
+                "merge_assign: null input");
+  const AssignWorkspace lay = assign_layout(S, total);
+  VB200_REQUIRE(workspace != nullptr && workspace_bytes >= lay.total,
+                "merge_assign: workspace of %zu bytes required (got %zu)", lay.total, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* keys_out = reinterpret_cast<float*>(ws + lay.keys_out);
+  int32_t* vals_in = reinterpret_cast<int32_t*>(ws + lay.vals_in);
+  int32_t* vals_out = reinterpret_cast<int32_t*>(ws + lay.vals_out);
+  int32_t* flags = reinterpret_cast<int32_t*>(ws + lay.flags);
+  int32_t* compact = reinterpret_cast<int32_t*>(ws + lay.compact);
+  int64_t* remap = reinterpret_cast<int64_t*>(ws + lay.remap);
+  fill_ones_kernel<<<blocks(total, 256), 256, 0, st>>>(flags, total);
+  VB200_CHECK_LAUNCH("fill_ones_kernel");
+  if (removed > 0) {
+    iota_kernel<<<blocks(S, 256), 256, 0, st>>>(vals_in, S);
+    VB200_CHECK_LAUNCH("iota_kernel");
+    size_t sort_bytes = lay.sort_bytes;
+    // radix sort is stable: equal scores keep ascending source order (argsort(stable=True))
+    VB200_CHECK_CUDA(cub::DeviceRadixSort::SortPairsDescending(ws + lay.sort_tmp, sort_bytes, best, keys_out,
+                                                               vals_in, vals_out, static_cast<int>(S), 0, 32, st),
+                     "cub::DeviceRadixSort::SortPairsDescending");
+    mark_removed_kernel<<<blocks(removed, 256), 256, 0, st>>>(vals_out, target, source_idx, dest_idx, removed,
+                                                              Dn, total, flags, remap);
+    VB200_CHECK_LAUNCH("mark_removed_kernel");
+  }
+  size_t scan_bytes = lay.scan_bytes;
+  VB200_CHECK_CUDA(cub::DeviceScan::ExclusiveSum(ws + lay.scan_tmp, scan_bytes, flags, compact,
+                                                 static_cast<int>(total), st),
+                   "cub::DeviceScan::ExclusiveSum");
+  keep_inverse_kernel<<<blocks(total, 256), 256, 0, st>>>(flags, compact, remap, total, total - removed, keep,
+                                                          inverse);
+  VB200_CHECK_LAUNCH("keep_inverse_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_support_fit(int dtype, const void* feat, int64_t rows, int64_t row_stride,
+                                 const int64_t* src_rows, const int64_t* parent_rows, int64_t S,
+                                 int64_t D, float* gram, float* rhs, float* alpha, int steps,
+                                 void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16,
+                "support_fit: bad dtype %d", dtype);
+  VB200_REQUIRE(S >= 0 && D > 0 && rows > 0 && steps >= 0, "support_fit: bad sizes");
+  if (S == 0) return VB200_OK;
+  VB200_REQUIRE(feat && parent_rows, "support_fit: null pointer");
+  const int es = dtype == VB200_F32 ? 4 : 2;
+  VB200_REQUIRE((D * es) % 16 == 0 && (row_stride * es) % 16 == 0 &&
+                    (reinterpret_cast<uintptr_t>(feat) & 15u) == 0,
+                "support_fit: rows must be 16-byte aligned and D a multiple of %d", 16 / es);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_FIT(T)                                                                                \
+  support_fit_kernel<T><<<blocks(S, 8), 256, 0, st>>>(static_cast<const T*>(feat), rows, row_stride, \
+                                                       src_rows, parent_rows, S, static_cast<int>(D),  \
+                                                       gram, rhs, alpha, steps)
+  if (dtype == VB200_F32) VB200_FIT(float);
+  else if (dtype == VB200_BF16) VB200_FIT(__nv_bfloat16);
+  else VB200_FIT(__half);
+#undef VB200_FIT
+  VB200_CHECK_LAUNCH("support_fit_kernel");
+  return VB200_OK;
+}

@@ -130,8 +130,8 @@ def similarity_topk(query: torch.Tensor, basis: torch.Tensor, k: int, *,
                     basis_begin: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Row top-k (k = 1 or 4) of bf16_round(query @ basis.T) on tcgen05, ties to the lower
     index.  query [R, D] and basis [Nb, D] are bf16 with D % 64 == 0.  With group tables
-    (int64 [G+1] each, on the device) query rows [qb[g], qb[g+1]) are ranked only against
-    basis rows [bb[g], bb[g+1]).  Returns (values fp32 [R, k], indices int64 [R, k])."""
+    (host int64 [G+1] each) query rows [qb[g], qb[g+1]) are ranked only against basis rows
+    [bb[g], bb[g+1]).  Returns (values fp32 [R, k], indices int64 [R, k])."""
     C.require_cuda(query, "similarity_topk")
     if k not in (1, 4):
         raise ValueError("k must be 1 or 4")
@@ -150,8 +150,8 @@ def similarity_topk(query: torch.Tensor, basis: torch.Tensor, k: int, *,
     groups = 1
     if query_begin is not None:
         groups = query_begin.numel() - 1
-        query_begin = query_begin.to(device=query.device, dtype=torch.int64).contiguous()
-        basis_begin = basis_begin.to(device=query.device, dtype=torch.int64).contiguous()
+        query_begin = torch.as_tensor(query_begin, dtype=torch.int64, device="cpu").contiguous()
+        basis_begin = torch.as_tensor(basis_begin, dtype=torch.int64, device="cpu").contiguous()
     rc = C.lib().vb200_sim_topk(
         query.data_ptr(), query.stride(0), basis.data_ptr(), basis.stride(0), R, Nb, D, k,
         C.ptr(query_begin), C.ptr(basis_begin), groups, values.data_ptr(), indices.data_ptr(),

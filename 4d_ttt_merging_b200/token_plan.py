@@ -167,7 +167,9 @@ class WeightedBilinearTokenPlan:
     query_restore_weights: torch.Tensor | None = None
     compact_mlp: bool = False
     metadata: dict[str, float | int] = field(default_factory=dict)
-    _csr: PlanCSR | None = field(default=None, init=False, repr=False)
+    # Optional prebuilt parent-grouped CSR of (source_parent_compact, source_pool_weights)
+    # with token rows from source_original; built at construction when absent.
+    csr: PlanCSR | None = field(default=None, repr=False)
     _keep_flat: torch.Tensor | None = field(default=None, init=False, repr=False)
     _normalizer_flat: torch.Tensor | None = field(default=None, init=False, repr=False)
 
@@ -177,10 +179,11 @@ class WeightedBilinearTokenPlan:
         C.require_cuda(self.keep, "WeightedBilinearTokenPlan")
         self._keep_flat = _idx(self.keep)
         self._normalizer_flat = self.normalizer.reshape(-1).to(torch.float32).contiguous()
-        self._csr = build_plan_csr(
-            self.source_parent_compact[0], self.source_pool_weights[0], self.kept_tokens,
-            src_rows=self.source_original.reshape(-1),
-        )
+        if self.csr is None:
+            self.csr = build_plan_csr(
+                self.source_parent_compact[0], self.source_pool_weights[0], self.kept_tokens,
+                src_rows=self.source_original.reshape(-1),
+            )
 
     @property
     def kept_tokens(self) -> int:
@@ -189,10 +192,6 @@ class WeightedBilinearTokenPlan:
     @property
     def keep_ratio(self) -> float:
         return self.kept_tokens / self.original_tokens
-
-    @property
-    def csr(self) -> PlanCSR:
-        return self._csr
 
     def compact(self, value: torch.Tensor, *, merge: bool = True) -> torch.Tensor:
         """Pool source Q/K/V mass into its four retained bilinear parents."""
@@ -204,7 +203,7 @@ class WeightedBilinearTokenPlan:
         if self.source_original.shape[1] == 0 or not self.pool_source_content:
             from .ops import row_gather
             return row_gather(x, self._keep_flat).unsqueeze(0)
-        return _scatter(x, self._keep_flat, self._csr, self._normalizer_flat, self.kept_tokens).unsqueeze(0)
+        return _scatter(x, self._keep_flat, self.csr, self._normalizer_flat, self.kept_tokens).unsqueeze(0)
 
     def compact_key(self, value: torch.Tensor) -> torch.Tensor:
         """Keep physical keys unchanged for the Q-preserving KV-only path."""

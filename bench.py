@@ -1,0 +1,334 @@
+"""Benchmark of the token-merged global-attention hot path on B200.
+
+Workload (every N): configuration 2 of the reference's metric — one global-attention block,
+dim 1024, 16 heads x 64, bf16, random-init weights (seed 0); input 32 frames of 1029 tokens
+(32,928 tokens ~ N(0,1)); merge 4x to 8,232 merged keys by the four-support convex planner
+(tcgen05 top-4 retrieval inside 4-frame groups, fused Gram + projected-gradient fit, mass =
+1 + pooled weights); then compact Q/K/V -> mass-bias attention -> proj -> top-4 restore.
+A step is that whole pass.  With N GPUs the 32 frames are split over the ranks (query-row
+sharding aligned to frame groups; merged K/V and log-mass all-gathered with NCCL): total
+work is fixed, so scaling is "strong".
+
+Metric: frames/s of the whole job (value), with the attention TFLOP/s and projection GB/s of
+the same timed steps reported beside it.  Timing: W untimed warm-up steps; K timed steps,
+each bracketed by CUDA events on the compute stream with an L2 flush (256 MB write) between
+steps outside the events; barrier + synchronize around the loop; max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+FRAMES = 32
+TOKENS_PER_FRAME = 1029
+SPECIAL = 5
+DIM = 1024
+HEADS = 16
+MERGE_FACTOR = 4
+GROUP_FRAMES = 4
+METRIC = "global-attn block frames/s (mass-bias attention TFLOP/s, top-4 projection GB/s)"
+CPU_SAMPLE_FRAMES = 4  # one frame group
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clocks not sampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def _cpu_pipeline_inputs(seed: int = 0):
+    import numpy as np
+    oracle = importlib.import_module("oracle")
+    rng = np.random.default_rng(seed)
+    n = CPU_SAMPLE_FRAMES * TOKENS_PER_FRAME
+    tokens = rng.standard_normal((n, DIM)).astype(np.float32)
+    params = {
+        "qkv.weight": (rng.standard_normal((3 * DIM, DIM)) * 0.02).astype(np.float32),
+        "qkv.bias": (rng.standard_normal(3 * DIM) * 0.02).astype(np.float32),
+        "qkv.bias_mask": np.concatenate([np.ones(DIM), np.zeros(DIM), np.ones(DIM)]).astype(np.float32),
+        "q_norm.weight": np.ones(64, np.float32), "q_norm.bias": np.zeros(64, np.float32),
+        "k_norm.weight": np.ones(64, np.float32), "k_norm.bias": np.zeros(64, np.float32),
+        "proj.weight": (rng.standard_normal((DIM, DIM)) * 0.02).astype(np.float32),
+        "proj.bias": np.zeros(DIM, np.float32),
+    }
+    layout = oracle.pipeline.uniform_layout(CPU_SAMPLE_FRAMES, TOKENS_PER_FRAME, SPECIAL, MERGE_FACTOR, GROUP_FRAMES)
+    return oracle, tokens, params, layout
+
+
+def _cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        info = threadpool_info()
+        return max((i.get("num_threads", 1) for i in info), default=1)
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(repeats: int = 2) -> dict:
+    """The oracle port of one step on a bounded sample (one 4-frame group), timed on this
+    host's cores; frames/s scaled from the sample."""
+    oracle, tokens, params, layout = _cpu_pipeline_inputs()
+    oracle.pipeline.block_step(tokens, params, layout)  # warm-up
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        oracle.pipeline.block_step(tokens, params, layout)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": CPU_SAMPLE_FRAMES / t, "unit": "frames/s", "cores": _cpu_threads(), "kind": "port",
+            "sample": f"one {CPU_SAMPLE_FRAMES}-frame group ({CPU_SAMPLE_FRAMES * TOKENS_PER_FRAME} tokens) of the "
+                      f"same step (plan + block) in the numpy oracle, median of {repeats} after 1 warm-up, "
+                      f"{t:.2f} s per sample"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    oracle, tokens, params, layout = _cpu_pipeline_inputs()
+    for _ in range(args.warmup):
+        oracle.pipeline.block_step(tokens, params, layout)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.pipeline.block_step(tokens, params, layout)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = CPU_SAMPLE_FRAMES * args.steps / total
+    cores = _cpu_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 2 sample: one 4-frame group of the single global-attention block "
+                               "(plan + compact + mass-bias attention + proj + restore), CPU oracle port"},
+        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cores, "kind": "port",
+                         "sample": f"{CPU_SAMPLE_FRAMES} frames ({CPU_SAMPLE_FRAMES * TOKENS_PER_FRAME} tokens) per step"},
+        "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    pkg = importlib.import_module("4d_ttt_merging_b200")
+    lib = pkg.load_library()
+
+    torch.manual_seed(0)
+    attn = pkg.GlobalAttention(DIM, HEADS, device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for p in attn.parameters():
+            if p.ndim > 1:
+                p.normal_(0.0, 0.02)
+            else:
+                p.normal_(0.0, 0.02)
+        attn.q_norm.weight.fill_(1.0)
+        attn.k_norm.weight.fill_(1.0)
+    block = pkg.parallel.ShardedGlobalBlock(attn, frames=FRAMES, tokens_per_frame=TOKENS_PER_FRAME,
+                                            patch_token_start=SPECIAL, merge_factor=MERGE_FACTOR,
+                                            group_frames=GROUP_FRAMES, world=world, rank=rank)
+    sh = block.shard
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    tokens_all = torch.randn(FRAMES * TOKENS_PER_FRAME, DIM, generator=gen).to(torch.bfloat16)
+    host_in = tokens_all[sh.token_begin:sh.token_end].contiguous().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    tokens = host_in.to(dev)[None]
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        block.step(tokens)
+    torch.cuda.synchronize()
+    if pkg.device_error_flags() != 0:
+        raise RuntimeError("device error flags set during warm-up")
+
+    # ---- timed device steps (inputs resident in HBM) ----
+    block.timers = {}
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    launches0 = lib.vb200_launch_count()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record()
+            block.step(tokens)
+            ev[i][1].record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = lib.vb200_launch_count() - launches0
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    timers = {k: [a.elapsed_time(b) for a, b in v] for k, v in block.timers.items()}
+    block.timers = None
+    total_ms = sum(step_ms)
+
+    # ---- timed end-to-end steps through the public API (host buffers, copies inside) ----
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.zero_()
+        ev2[i][0].record()
+        t_in = host_in.to(dev, non_blocking=True)[None]
+        out = block.step(t_in)
+        host_out.copy_(out[0], non_blocking=True)
+        ev2[i][1].record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
+
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+    if pkg.device_error_flags() != 0:
+        raise RuntimeError("device error flags set during the timed steps")
+
+    hbm_peak, tf_peak, peak_kind = _peaks()
+    frames_per_s = FRAMES * args.steps / (total_ms / 1e3)
+    # attention: compact queries of this rank over all merged keys
+    K_total = FRAMES * TOKENS_PER_FRAME // MERGE_FACTOR
+    K_local = K_total // world
+    attn_flops = 4.0 * K_local * K_total * 64 * HEADS
+    attn_ms = statistics.mean(timers["attention"])
+    attn_tflops = attn_flops / (attn_ms / 1e3) / 1e12
+    # projection compulsory bytes (bf16, C=1024): compact reads tokens of 3 tensors and writes
+    # merged rows; restore reads merged rows and writes tokens; plus index/weight/mass arrays
+    N_local = sh.token_end - sh.token_begin
+    S_local = N_local - K_local
+    meta = S_local * 4 * (4 + 4) + K_local * 4
+    compact_bytes = 3 * (N_local * DIM * 2 + K_local * DIM * 2 + meta)
+    restore_bytes = K_local * DIM * 2 + N_local * DIM * 2 + meta
+    compact_gbs = compact_bytes / (statistics.mean(timers["compact"]) / 1e3) / 1e9
+    restore_gbs = restore_bytes / (statistics.mean(timers["restore"]) / 1e3) / 1e9
+    phases = {k: round(statistics.mean(v), 4) for k, v in timers.items()}
+
+    line = {
+        "metric": METRIC, "value": frames_per_s, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config 2: single global-attention block, 32 frames x 1029 tokens, dim 1024, "
+                               "16x64 heads, merge 4x to 8232 keys (uniform convex top-4 plan), compact-query",
+                   "global_batch": 1, "tokens": FRAMES * TOKENS_PER_FRAME, "merged_keys": K_total,
+                   "parallelism": f"query-row shard x{world}" if world > 1 else "single GPU",
+                   "l2": "256 MB L2 flush between timed steps (outside the step events)"},
+        "components": {"attention_tflops": attn_tflops, "attention_ms": attn_ms,
+                       "compact_qkv_gbs": compact_gbs, "restore_gbs": restore_gbs, "phase_ms": phases},
+        "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": attn_tflops / tf_peak, "traffic": None,
+                     "kernel": "mass_bias_attention_tc_kernel",
+                     "peak_source": f"{peak_kind} bf16 dense (burst)"},
+        "clocks": clocks.summary(),
+        "e2e": {"value": FRAMES * args.steps / (e2e_ms / 1e3), "unit": "frames/s",
+                "h2d_bytes_per_step": FRAMES * TOKENS_PER_FRAME * DIM * 2,
+                "d2h_bytes_per_step": FRAMES * TOKENS_PER_FRAME * DIM * 2},
+        "gpu_launches": int(launches),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -44,6 +44,8 @@ extern "C" {
 /* ---- library ---------------------------------------------------------------------------- */
 VB200_API int vb200_version(void);
 VB200_API const char* vb200_last_error(void);
+/* Number of kernels this library has launched in the process (all devices, all threads). */
+VB200_API unsigned long long vb200_launch_count(void);
 /* OR of the error words that kernels write when a bounded wait runs out (bit 0) or an index
  * is out of range (bit 1).  Synchronises the current device; clears the words when clear!=0. */
 VB200_API int vb200_device_error_flags(unsigned* flags, int clear);
@@ -135,7 +137,9 @@ VB200_API int vb200_row_normalize_bf16(int dtype, const void* x, int64_t x_rows,
  * score[r, n] = bf16_round( <query[r], basis[n]> ) over D channels (fp32 accumulation on
  * tcgen05), ranked per row; ties keep the lower basis index.  With groups: query rows
  * [q_begin[g], q_begin[g+1]) are matched only against basis rows [b_begin[g], b_begin[g+1]);
- * groups == 1 with NULL tables means all rows against all basis rows.
+ * groups == 1 with NULL tables means all rows against all basis rows.  q_begin / b_begin are
+ * HOST arrays of groups+1 int64 entries (read before the launch).  Rows whose group has no
+ * basis row get values -inf and indices -1.
  * query: [R, D] bf16, row stride q_row_stride; basis: [Nb, D] bf16 (K-major, i.e. the rows
  * of the dictionary, row stride b_row_stride).  D % 64 == 0.  values [R, k] fp32,
  * indices [R, k] int64 (basis index, global), ordered best first.
@@ -146,6 +150,30 @@ VB200_API int vb200_sim_topk(const void* query, int64_t q_row_stride, const void
                    int64_t b_row_stride, int64_t R, int64_t Nb, int64_t D, int k,
                    const int64_t* q_begin, const int64_t* b_begin, int64_t groups,
                    float* values, int64_t* indices, void* stream);
+
+/* Ranking and keep / inverse maps of the FastVGGT merge (token_merging.py:1112-1121):
+ * the S sources are ordered by best score (stable, descending); the first `removed` are
+ * merged into destination dest_idx[target[s]]; keep [total-removed] lists the surviving
+ * token ids in order and inverse [total] maps every token to its compact index.
+ * best [S] fp32, target [S] int64 (index into dest_idx), source_idx [S], dest_idx [Dn] int64
+ * token ids.  workspace: vb200_merge_assign_workspace_size(S, total) bytes. */
+VB200_API size_t vb200_merge_assign_workspace_size(int64_t S, int64_t total);
+VB200_API int vb200_merge_assign(const float* best, const int64_t* target, const int64_t* source_idx,
+                                 const int64_t* dest_idx, int64_t S, int64_t Dn, int64_t total,
+                                 int64_t removed, int64_t* keep, int64_t* inverse, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* Support Gram and right-hand side of each source (sparse_convex.py:2314-2316):
+ * gram[s] = F[p] F[p]^T over its four support rows p = parent_rows[s, :], rhs[s] = F[p] x_s
+ * with x_s = F[src_rows[s]] (src_rows NULL: row s), fp32 accumulation.  With alpha != NULL
+ * the four-support projected-gradient solve (`steps` iterations, as
+ * vb200_four_support_projected_gradient) runs in the same kernel.  gram / rhs may be NULL.
+ * F: [rows, D] of `dtype` with row stride row_stride.  Rows outside [0, rows) set device
+ * error bit 1 and read row 0 instead. */
+VB200_API int vb200_support_fit(int dtype, const void* feat, int64_t rows, int64_t row_stride,
+                                const int64_t* src_rows, const int64_t* parent_rows, int64_t S,
+                                int64_t D, float* gram, float* rhs, float* alpha, int steps,
+                                void* stream);
 
 /* ---- next tier: 4-support simplex solvers ------------------------------------------------
  * Replaces four_support_projected_gradient (models/sparse_convex_kernels.py:283-296) and

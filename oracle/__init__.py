@@ -11,3 +11,4 @@ the script that made them live in ``tests/golden/``.
 """
 from .ref import *  # noqa: F401,F403
 from .synth import *  # noqa: F401,F403
+from . import pipeline  # noqa: F401

@@ -67,7 +67,7 @@ def mass_bias_attention(q, k, v, log_key_mass=None, dtype: str = "f32", round_p:
     k = np.asarray(k, dtype=np.float64)
     v = np.asarray(v, dtype=np.float64)
     d = q.shape[-1]
-    logits = np.einsum("bhqd,bhkd->bhqk", q, k) / math.sqrt(d)
+    logits = np.matmul(q, np.swapaxes(k, -1, -2)) / math.sqrt(d)
     if log_key_mass is not None:
         bias = round_to(np.asarray(log_key_mass, dtype=np.float32).reshape(-1), dtype).astype(np.float64)
         logits = logits + bias[None, None, None, :]
@@ -77,7 +77,7 @@ def mass_bias_attention(q, k, v, log_key_mass=None, dtype: str = "f32", round_p:
     denom = p.sum(axis=-1, keepdims=True)
     if round_p:
         p = round_to(p.astype(np.float32), dtype).astype(np.float64)
-    return np.einsum("bhqk,bhkd->bhqd", p, v) / denom
+    return np.matmul(p, v) / denom
 
 
 # ------------------------------------------------------------------------------------------
@@ -94,8 +94,7 @@ def normalizer(parent, weights, kept: int) -> np.ndarray:
     for c in range(parent.shape[1]):
         seg = np.zeros(kept, dtype=np.float32)
         order = np.argsort(parent[:, c], kind="stable")
-        for s in order:  # fp32 sequential segment sums
-            seg[parent[s, c]] = np.float32(seg[parent[s, c]] + weights[s, c])
+        np.add.at(seg, parent[order, c], weights[order, c])  # fp32, in source order
         mass = (mass + seg).astype(np.float32)
     return mass
 
@@ -106,11 +105,9 @@ def _segment_sums(x32, parent_c, weight_c, kept):
     out = np.zeros((kept, C), dtype=np.float32)
     order = np.argsort(parent_c, kind="stable")
     prod = (x32[order] * weight_c[order, None]).astype(np.float32)  # fp32 products
-    p_sorted = parent_c[order]
-    # sequential fp32 accumulation per segment, in order
-    for idx in range(len(order)):
-        j = p_sorted[idx]
-        out[j] = (out[j] + prod[idx]).astype(np.float32)
+    # sequential fp32 accumulation per segment, in order (np.add.at is unbuffered and
+    # applies the updates in array order)
+    np.add.at(out, parent_c[order], prod)
     return out
 
 
@@ -177,7 +174,8 @@ def layer_norm(x, weight, bias, eps: float = 1e-5) -> np.ndarray:
     return (x - mu) / np.sqrt(var + eps) * np.asarray(weight, np.float64) + np.asarray(bias, np.float64)
 
 
-def global_attention_forward(x, params: dict, plan: dict, heads: int, preserve_queries: bool) -> np.ndarray:
+def global_attention_forward(x, params: dict, plan: dict, heads: int, preserve_queries: bool,
+                             dense_special: bool = True) -> np.ndarray:
     """Restates SelfAttention.forward with a WeightedBilinearTokenPlan in fp32
     (vggt_omega/models/layers/attention.py:264-314, :328-439): qkv projection (k bias masked,
     :195-207), q/k LayerNorm over the head dim, compaction (compact-query plans compact Q, K
@@ -208,10 +206,11 @@ def global_attention_forward(x, params: dict, plan: dict, heads: int, preserve_q
     to_bh = lambda t: np.asarray(t, np.float64).reshape(1, -1, heads, hd).transpose(0, 2, 1, 3)
     log_mass = np.log(np.asarray(norm, np.float32)).astype(np.float32)
     o = mass_bias_attention(to_bh(qc), to_bh(kc), to_bh(vc), log_mass)  # [1,H,Nq,hd]
-    special = np.asarray(plan["special"], np.int64)
-    exact = mass_bias_attention(to_bh(flat(q)[special]), to_bh(flat(k)), to_bh(flat(v)), None)
-    out_index = special if preserve_queries else np.asarray(plan["special_compact"], np.int64)
-    o[:, :, out_index] = exact
+    if dense_special:
+        special = np.asarray(plan["special"], np.int64)
+        exact = mass_bias_attention(to_bh(flat(q)[special]), to_bh(flat(k)), to_bh(flat(v)), None)
+        out_index = special if preserve_queries else np.asarray(plan["special_compact"], np.int64)
+        o[:, :, out_index] = exact
     o = o.transpose(0, 2, 1, 3).reshape(-1, dim)
     y = o @ np.asarray(params["proj.weight"], np.float64).T + np.asarray(params["proj.bias"], np.float64)
     y = y.astype(np.float32)

@@ -1,0 +1,107 @@
+"""The global-attention call site end to end on the GPU: GlobalAttention.forward with a token
+plan against the reference's own SelfAttention.forward (golden vectors, fp32) and, in bf16
+under autocast, against the oracle; plus the device planners."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _module(pkg, golden, tag, dev):
+    params = {k[len(tag) + 3:]: v for k, v in golden.items() if k.startswith(f"{tag}_p_")}
+    dim = params["qkv.weight"].shape[1]
+    m = pkg.GlobalAttention(dim, 2, device=dev)
+    m.load_reference_state({k: torch.from_numpy(v).to(dev) for k, v in params.items()})
+    return m, params
+
+
+def _plan(pkg, golden, tag, dev, preserve):
+    t = lambda k, dt=torch.long: torch.from_numpy(golden[f"{tag}_{k}"]).to(dev, dt)
+    norm = t("normalizer", torch.float32).view(1, -1, 1)
+    return pkg.WeightedBilinearTokenPlan(
+        keep=t("keep")[None], source_original=t("source")[None], source_parent_compact=t("parent")[None],
+        source_pool_weights=t("weights", torch.float32)[None], source_restore_weights=t("weights", torch.float32)[None],
+        original_tokens=golden[f"{tag}_x"].shape[1], normalizer=norm, preserve_queries=preserve,
+        preserve_destination_keys=preserve, dense_special_queries=True, special_query_original=t("special"),
+        special_query_compact=t("special_compact"), key_log_mass=norm[..., 0].log())
+
+
+@pytest.mark.parametrize("tag,preserve", [("block_compact_q", False), ("block_preserve_q", True)])
+def test_block_fp32_matches_reference(pkg, golden, cuda_device, tag, preserve):
+    m, _ = _module(pkg, golden, tag, cuda_device)
+    plan = _plan(pkg, golden, tag, cuda_device, preserve)
+    x = torch.from_numpy(golden[f"{tag}_x"]).to(cuda_device)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    with torch.no_grad():
+        y = m(x, token_plan=plan)
+    assert_close(to_np(y), golden[f"{tag}_y"], "f32", tol=2e-5)
+
+
+@pytest.mark.parametrize("tag,preserve", [("block_compact_q", False), ("block_preserve_q", True)])
+def test_block_bf16_autocast(pkg, golden, oracle, cuda_device, tag, preserve):
+    m, params = _module(pkg, golden, tag, cuda_device)
+    plan = _plan(pkg, golden, tag, cuda_device, preserve)
+    x = torch.from_numpy(golden[f"{tag}_x"]).to(cuda_device)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        y = m(x, token_plan=plan)
+    assert y.dtype == torch.bfloat16
+    pd = {k: golden[f"{tag}_{k}"] for k in ("keep", "source", "parent", "weights", "normalizer", "special",
+                                            "special_compact")}
+    ref = oracle.global_attention_forward(golden[f"{tag}_x"][0], params, pd, heads=2, preserve_queries=preserve)
+    assert_close(to_np(y[0]), ref, "bf16")
+
+
+def test_fastvggt_plan_matches_reference(pkg, golden, cuda_device):
+    tokens = torch.from_numpy(golden["fast_tokens"]).to(cuda_device)
+    plan = pkg.build_fastvggt_plan(tokens, frames=3, tokens_per_frame=69, patch_token_start=5, patch_hw=(8, 8),
+                                   merge_ratio=0.5, protect_ratio=0.1, seed=3)
+    np.testing.assert_array_equal(plan.keep[0].cpu().numpy(), golden["fast_keep"])
+    np.testing.assert_array_equal(plan.inverse[0].cpu().numpy(), golden["fast_inverse"])
+    assert pkg.device_error_flags() == 0
+
+
+def test_fastvggt_plan_large(pkg, oracle, cuda_device):
+    """4 frames of 1029 tokens, D=1024 against the oracle restatement: the assignment of every
+    merged source equals the oracle's argmax up to exact bf16 ties."""
+    rng = np.random.default_rng(2)
+    frames, tpf, pts, hw = 4, 1029, 5, (32, 32)
+    tok = rng.standard_normal((frames * tpf, 1024)).astype(np.float32)
+    plan = pkg.build_fastvggt_plan(torch.from_numpy(tok)[None].to(cuda_device), frames=frames,
+                                   tokens_per_frame=tpf, patch_token_start=pts, patch_hw=hw, merge_ratio=0.5)
+    keep, inverse, best, target, src_idx, dst_idx = oracle.fastvggt_plan(
+        tok, frames=frames, tokens_per_frame=tpf, patch_token_start=pts, patch_hw=hw, merge_ratio=0.5)
+    got_keep = plan.keep[0].cpu().numpy()
+    got_inv = plan.inverse[0].cpu().numpy()
+    agree = np.mean(got_inv == inverse)
+    assert agree > 0.995, agree
+    assert got_keep.size == keep.size
+    # each merged token points at a destination whose oracle score equals the oracle's best
+    mapped = got_keep[got_inv]
+    assert np.all(np.isin(mapped, np.concatenate([dst_idx, keep])))
+
+
+def test_uniform_convex_plan(pkg, oracle, cuda_device):
+    rng = np.random.default_rng(4)
+    frames, tpf = 8, 1029
+    tok = torch.from_numpy(rng.standard_normal((1, frames * tpf, 1024)).astype(np.float32)).to(cuda_device)
+    plan = pkg.build_uniform_convex_plan(tok.bfloat16(), frames=frames, tokens_per_frame=tpf, patch_token_start=5,
+                                         merge_factor=4, group_frames=4)
+    N = frames * tpf
+    assert plan.kept_tokens == N // 4
+    w = plan.source_pool_weights[0]
+    assert torch.all(w >= 0) and torch.allclose(w.sum(-1), torch.ones_like(w[:, 0]), atol=1e-5)
+    mass = plan.normalizer[0, :, 0]
+    assert abs(float(mass.sum()) - N) < 1.0  # convex weights: masses sum to N
+    np.testing.assert_allclose(to_np(mass), oracle.normalizer(plan.source_parent_compact[0].cpu().numpy(),
+                                                              to_np(w), plan.kept_tokens), rtol=1e-5)
+    # supports stay inside the source's frame group
+    keep = plan.keep[0].cpu().numpy()
+    src = plan.source_original[0].cpu().numpy()
+    par = keep[plan.source_parent_compact[0].cpu().numpy()]
+    assert np.all(par // (4 * tpf) == (src // (4 * tpf))[:, None])
+    assert pkg.device_error_flags() == 0

@@ -1,0 +1,28 @@
+"""install() rebinds the reference's hot-path names to the B200 operators (CPU check: the
+reference is importable in the build container; nothing is computed)."""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import pytest
+
+REFERENCE = Path("/root/reference")
+
+
+@pytest.mark.skipif(not (REFERENCE / "vggt_omega").exists(), reason="reference checkout not present")
+def test_install_patches_reference(pkg):
+    patched = pkg.install(str(REFERENCE))
+    try:
+        mba = sys.modules["vggt_omega.models.mass_bias_attention"]
+        tm = sys.modules["vggt_omega.models.token_merging"]
+        sc = sys.modules["vggt_omega.models.sparse_convex"]
+        assert mba.mass_bias_attention is pkg.mass_bias_attention
+        assert tm.WeightedBilinearTokenPlan is pkg.WeightedBilinearTokenPlan
+        assert tm.build_fastvggt_plan is pkg.build_fastvggt_plan
+        assert sc.WeightedBilinearTokenPlan is pkg.WeightedBilinearTokenPlan
+        assert sc.four_support_projected_gradient is pkg.four_support_projected_gradient
+        assert "vggt_omega.models.sparse_convex_kernels.streaming_top4" in patched
+    finally:
+        pkg.uninstall()
+    assert sys.modules["vggt_omega.models.mass_bias_attention"].mass_bias_attention is not pkg.mass_bias_attention

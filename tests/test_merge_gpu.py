@@ -1,0 +1,97 @@
+"""Merge step on the GPU: tcgen05 similarity GEMM with fused top-1 / top-4 epilogue against
+the reference goldens and the oracle.  Indices must match bit-exactly up to exact ties: where
+an index differs, the oracle's score at our index equals its score at the reference index."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16(x, dev):
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(dev, torch.bfloat16)
+
+
+def _check_topk(oracle, q, b, got_v, got_i, k, groups=None):
+    """Compare against the oracle; allow a differing index only where the oracle score at our
+    index is within one bf16 ulp of the oracle's k-th best (fp32 accumulation-order ties)."""
+    scores = oracle.topk_scores(q, b)
+    if groups is not None:
+        mask = np.full(scores.shape, -np.inf, dtype=np.float32)
+        for (q0, q1), (b0, b1) in groups:
+            mask[q0:q1, b0:b1] = 0
+        scores = scores + mask
+    ref_order = np.argsort(-scores, axis=1, kind="stable")[:, :k]
+    ref_v = np.take_along_axis(scores, ref_order, 1)
+    rows = np.isfinite(ref_v[:, 0])
+    got_i = got_i.astype(np.int64)
+    assert np.all(got_i[rows] >= 0)
+    mine = np.take_along_axis(scores, np.where(got_i < 0, 0, got_i), 1)
+    exact = (got_i == ref_order) | (~rows[:, None])
+    assert exact.mean() > 0.995, f"only {exact.mean():.4f} of the indices match"
+    ulp = np.abs(ref_v) * 2 ** -7 + 1e-30
+    close = np.abs(mine - ref_v) <= ulp
+    assert np.all(close[rows]), "a differing index is not a tie within one bf16 ulp"
+    np.testing.assert_allclose(got_v[rows], ref_v[rows], rtol=2 ** -7, atol=0)
+    return exact.mean()
+
+
+def test_golden_top4_and_argmax(pkg, golden, oracle, cuda_device):
+    q, b = golden["topk_q"], golden["topk_b"]
+    v, i = pkg.similarity_topk(_bf16(q, cuda_device), _bf16(b, cuda_device), 4)
+    v, i = to_np(v), i.cpu().numpy()
+    scores = oracle.topk_scores(q, b)
+    ref_i = golden["topk_indices"].astype(np.int64)
+    np.testing.assert_array_equal(v, golden["topk_values"])
+    np.testing.assert_array_equal(np.take_along_axis(scores, i, 1), np.take_along_axis(scores, ref_i, 1))
+    assert np.mean(i == ref_i) > 0.95
+    best, target = pkg.merge_argmax(_bf16(q, cuda_device), _bf16(b, cuda_device))
+    np.testing.assert_array_equal(to_np(best), golden["topk_max_values"])
+    np.testing.assert_array_equal(scores[np.arange(len(q)), target.cpu().numpy()], golden["topk_max_values"])
+
+
+@pytest.mark.parametrize("k", [1, 4])
+@pytest.mark.parametrize("shape", [(1, 4, 64), (130, 300, 128), (1000, 2100, 1024), (257, 513, 192)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_against_oracle(pkg, oracle, cuda_device, k, shape):
+    R, Nb, D = shape
+    rng = np.random.default_rng(R + Nb + D)
+    q = rng.standard_normal((R, D)).astype(np.float32)
+    b = rng.standard_normal((Nb, D)).astype(np.float32)
+    q = oracle.round_bf16(q / np.linalg.norm(q, axis=1, keepdims=True))
+    b = oracle.round_bf16(b / np.linalg.norm(b, axis=1, keepdims=True))
+    v, i = pkg.similarity_topk(_bf16(q, cuda_device), _bf16(b, cuda_device), k)
+    _check_topk(oracle, q, b, to_np(v), i.cpu().numpy(), k)
+    assert pkg.device_error_flags() == 0
+
+
+def test_groups(pkg, oracle, cuda_device):
+    rng = np.random.default_rng(7)
+    D = 256
+    qb = [0, 300, 300, 700, 1000]   # group 1 has no query rows
+    bb = [0, 500, 600, 600, 1200]   # group 2 has no basis rows
+    q = oracle.round_bf16(rng.standard_normal((1000, D)).astype(np.float32) / 16)
+    b = oracle.round_bf16(rng.standard_normal((1200, D)).astype(np.float32) / 16)
+    v, i = pkg.similarity_topk(_bf16(q, cuda_device), _bf16(b, cuda_device), 4,
+                               query_begin=torch.tensor(qb), basis_begin=torch.tensor(bb))
+    v, i = to_np(v), i.cpu().numpy()
+    groups = [((qb[g], qb[g + 1]), (bb[g], bb[g + 1])) for g in range(4)]
+    _check_topk(oracle, q, b, v, i, 4, groups=groups)
+    # rows of the group without basis rows: -inf / -1
+    assert np.all(i[300:700] == -1) and np.all(np.isneginf(v[300:700]))
+
+
+def test_streaming_top4_transposed_basis(pkg, oracle, cuda_device):
+    rng = np.random.default_rng(3)
+    q = oracle.round_bf16(rng.standard_normal((200, 128)).astype(np.float32) / 11)
+    b = oracle.round_bf16(rng.standard_normal((64, 128)).astype(np.float32) / 11)
+    bt = _bf16(b, cuda_device).t()  # [D, N] view, as the reference passes it
+    v, i = pkg.streaming_top4(_bf16(q, cuda_device), bt)
+    assert i.dtype == torch.int64 and v.dtype == torch.float32
+    _check_topk(oracle, q, b, to_np(v), i.cpu().numpy(), 4)
+    with pytest.raises(ValueError, match="at least four"):
+        pkg.streaming_top4(_bf16(q, cuda_device), bt[:, :3])

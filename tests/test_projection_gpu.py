@@ -127,7 +127,8 @@ def test_row_ops(pkg, oracle, cuda_device):
     nb = pkg.row_normalize_bf16(xt, rows)
     ref = x[to_np(rows).astype(int)]
     ref = oracle.round_bf16(ref / np.maximum(np.linalg.norm(ref.astype(np.float64), axis=1, keepdims=True), 1e-12))
-    np.testing.assert_allclose(to_np(nb), ref, rtol=2 ** -8, atol=0)
-    assert np.mean(to_np(nb) == ref) > 0.99
+    # within one bf16 ulp (the fp32 norm may differ in its last bit), almost always exact
+    np.testing.assert_allclose(to_np(nb), ref, rtol=2 ** -7, atol=0)
+    assert np.mean(to_np(nb) == ref) > 0.999
     g = pkg.row_gather(xt.bfloat16(), rows)
     assert torch.equal(g, xt.bfloat16()[rows])
