@@ -37,6 +37,11 @@ _SIGNATURES = {
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
          _p_i64, _p_i64, _p_i64, _p_i64, _c_vp, _c_size, _c_vp],
     ),
+    "vb200_mass_bias_attention_noalloc": (
+        _c_int,
+        [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+         _p_i64, _p_i64, _p_i64, _p_i64, _c_vp],
+    ),
     "vb200_plan_csr_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "vb200_plan_csr_build": (
         _c_int,

@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -576,4 +577,62 @@ extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k
   }
   VB200_CHECK_LAUNCH("mass_bias_attention_tc_kernel");
   return VB200_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// No-allocation variant.
+//
+// Some callers of this library cannot call cudaMalloc or any allocator: code that only
+// receives raw device pointers from another runtime's memory arena (with no allocator handle
+// to obtain scratch from), and latency-critical serving loops that must not call cudaMalloc /
+// cudaFree because those calls synchronise the device.  For them the attention's only scratch
+// buffer — the padded log2-domain bias — lives in a fixed file-scope device array instead of a
+// caller workspace.  Every GPU that loads this library holds the array (1 MiB) until exit.
+// ------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kNoAllocMaxKeys = 262144;  // keys per call; a multiple of the 128-key tile
+static __device__ __align__(256) float g_noalloc_bias[kNoAllocMaxKeys];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_bias on the current device.  In host code the symbol is a
+// host-side stand-in, so its address is resolved once per device (with that device current)
+// through cudaGetSymbolAddress and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  VB200_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(VB200_EUNSUPPORTED, "device ordinal %d exceeds %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    VB200_CHECK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_bias), "cudaGetSymbolAddress(g_noalloc_bias)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return VB200_OK;
+}
+
+}  // namespace
+
+extern "C" int vb200_mass_bias_attention_noalloc(int dtype, const void* q, const void* k, const void* v,
+                                                 const void* log_key_mass, int bias_dtype, void* out,
+                                                 int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t D,
+                                                 const int64_t* qs, const int64_t* ks, const int64_t* vs,
+                                                 const int64_t* os, void* stream) {
+  if (Nk > kNoAllocMaxKeys)
+    return set_error(VB200_EINVAL,
+                     "mass_bias_attention_noalloc: %lld keys exceed the fixed scratch of %lld keys; "
+                     "use vb200_mass_bias_attention with a caller workspace",
+                     (long long)Nk, (long long)kNoAllocMaxKeys);
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != VB200_OK) return rc;
+  // The bias kernel rewrites every scratch entry the attention kernel reads (real keys and the
+  // -inf padding of the last tile), so nothing carries over from a previous call.
+  return vb200_mass_bias_attention(dtype, q, k, v, log_key_mass, bias_dtype, out, B, H, Nq, Nk, D, qs, ks,
+                                   vs, os, scratch, sizeof(float) * kNoAllocMaxKeys, stream);
 }

@@ -70,6 +70,24 @@ VB200_API int vb200_mass_bias_attention(int dtype, const void* q, const void* k,
                               const int64_t* v_strides, const int64_t* o_strides,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same computation as vb200_mass_bias_attention, for callers that cannot allocate device
+ * memory: code that only holds raw device pointers handed over by another runtime (no
+ * allocator to get a workspace from) and latency-critical loops that must not call
+ * cudaMalloc / cudaFree, which synchronise the device.  It allocates nothing: its scratch (the
+ * padded bias) is a fixed 1 MiB array inside the library, present on every GPU that loads it
+ * until the process exits, so Nk is limited to 262,144 keys (larger Nk returns VB200_EINVAL).
+ * The first call on a device resolves that array's device address (cudaGetSymbolAddress) with
+ * the device current; make that first call before any stream capture.  All calls share the
+ * array: calls that may overlap on the GPU (different streams, or different host threads on one
+ * device) race on it.  Nothing carries over between calls: each call rewrites every entry it
+ * reads.  This entry point has no counterpart in the reference. */
+VB200_API int vb200_mass_bias_attention_noalloc(int dtype, const void* q, const void* k, const void* v,
+                                                const void* log_key_mass, int bias_dtype, void* out,
+                                                int64_t B, int64_t H, int64_t Nq, int64_t Nk, int64_t D,
+                                                const int64_t* q_strides, const int64_t* k_strides,
+                                                const int64_t* v_strides, const int64_t* o_strides,
+                                                void* stream);
+
 /* ---- a7/a8: plan preprocessing --------------------------------------------------------------
  * Groups the S*corners (source, corner) pairs of a weighted plan by compact parent so that
  * every reduction below runs in a fixed order with no atomics.  Segment (j, c) lists, in
