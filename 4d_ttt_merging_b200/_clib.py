@@ -53,6 +53,14 @@ _SIGNATURES = {
         [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
          _c_i64, _c_i64, _c_vp],
     ),
+    "vb200_compact_qkv": (
+        _c_int,
+        [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_float, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp,
+         _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_vp],
+    ),
+    "vb200_head_layernorm": (
+        _c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_float, _c_vp, _c_i64, _c_vp],
+    ),
     "vb200_proj_gather": (
         _c_int,
         [_c_int, _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64,

@@ -23,7 +23,8 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .ops import mass_bias_attention
+from .ops import head_layernorm, mass_bias_attention, row_gather
+from .token_plan import WeightedBilinearTokenPlan
 
 __all__ = ["GlobalAttention", "compute_attention"]
 
@@ -34,10 +35,71 @@ def _bhtd(x: torch.Tensor, heads: int) -> torch.Tensor:
     return x.view(B, T, heads, C // heads).transpose(1, 2)
 
 
+def _ln_params(q_norm, k_norm):
+    if q_norm is None or k_norm is None:
+        return None, None, 1e-5
+    w = torch.stack([q_norm.weight.detach(), k_norm.weight.detach()]).float()
+    b = torch.stack([q_norm.bias.detach(), k_norm.bias.detach()]).float()
+    return w, b, float(q_norm.eps)
+
+
+def _fused_ok(qkv: torch.Tensor, token_plan, q_norm, k_norm) -> bool:
+    """The one-kernel LayerNorm + Q||K||V compaction applies to 16-bit qkv buffers with a
+    WeightedBilinearTokenPlan without a separate query plan."""
+    if not isinstance(token_plan, WeightedBilinearTokenPlan) or token_plan.query_keep is not None:
+        return False
+    if qkv.dtype not in (torch.bfloat16, torch.float16) or qkv.shape[0] != 1 or (qkv.shape[2] // 3) % 256:
+        return False
+    if (q_norm is None) != (k_norm is None):
+        return False
+    return q_norm is None or (q_norm.elementwise_affine and tuple(q_norm.normalized_shape) == (64,))
+
+
+def _compute_attention_fused(qkv, num_heads, plan, q_norm, k_norm):
+    B, N, C3 = qkv.shape
+    C = C3 // 3
+    x = qkv[0]
+    lw, lb, eps = _ln_params(q_norm, k_norm)
+    preserve = plan.preserve_queries
+    if preserve:
+        mask = 0b100 | (0 if plan.preserve_destination_keys else 0b010)
+    else:
+        mask = 0b111
+    packed = plan.compact_qkv(x, lw, lb, eps, pool_mask=mask)  # [M, 3C]
+    M = packed.shape[0]
+    view = lambda t, T: t.view(1, T, num_heads, C // num_heads).transpose(1, 2)
+    if preserve:
+        q = head_layernorm(x[:, :C], lw[0], lb[0], eps) if lw is not None else x[:, :C]
+        qv = view(q, N)
+    else:
+        qv = view(packed[:, :C], M)
+    o = mass_bias_attention(qv, view(packed[:, C:2 * C], M), view(packed[:, 2 * C:], M), plan.key_log_mass)
+    if plan.dense_special_queries:
+        original, out_index = plan.special_query_original, (
+            plan.special_query_original if preserve else plan.special_query_compact)
+        if original is None or out_index is None:
+            raise RuntimeError("dense-special attention plan has no special-token mapping")
+        qs = row_gather(x[:, :C], original)
+        if lw is not None:
+            qs = head_layernorm(qs, lw[0], lb[0], eps)
+            kd = head_layernorm(x[:, C:2 * C], lw[1], lb[1], eps)
+        else:
+            kd = x[:, C:2 * C]
+        exact = mass_bias_attention(view(qs, qs.shape[0]), view(kd, N), view(x[:, 2 * C:], N), None)
+        o.index_copy_(2, out_index, exact)
+    return o.transpose(1, 2).reshape(B, o.shape[2], C)
+
+
 def compute_attention(qkv: torch.Tensor, num_heads: int, token_plan, q_norm: nn.Module | None = None,
                       k_norm: nn.Module | None = None) -> torch.Tensor:
     """Attention part of SelfAttention.compute_attention (attention.py:328-439) for a global
-    block with a token plan; returns [B, Nq, C] (Nq = compact query count or N)."""
+    block with a token plan; returns [B, Nq, C] (Nq = compact query count or N).
+
+    16-bit qkv buffers with a WeightedBilinearTokenPlan take the fused path: one kernel
+    LayerNorms q/k per head and compacts Q||K||V (``vb200_compact_qkv``).  Other inputs
+    (fp32, hard-merge TokenPlan, separate query plans) compose the individual operators."""
+    if token_plan is not None and _fused_ok(qkv, token_plan, q_norm, k_norm):
+        return _compute_attention_fused(qkv, num_heads, token_plan, q_norm, k_norm)
     B, N, C3 = qkv.shape
     C = C3 // 3
     hd = C // num_heads

@@ -267,6 +267,168 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 }
 
 // ------------------------------------------------------------------------------------------
+// fused q/k LayerNorm + Q||K||V compaction
+//
+// The qkv row of a token is [q | k | v], each C = heads * 64 channels.  One warp per compact
+// row j; lane l holds 16-byte vector l of every 256-channel chunk, i.e. channels [8l, 8l+8),
+// so one head's 64 channels sit on 8 consecutive lanes and the LayerNorm statistics of a head
+// are two 3-step shuffle reductions inside that lane octet.  For q and k every loaded row is
+// normalised (fp32, biased variance, as nn.LayerNorm) before it is weighted, which is the
+// reference order: q_norm / k_norm on every token, then compaction
+// (vggt_omega/models/layers/attention.py:337-339, 354-374).  Tensor t is pooled (keep row +
+// corner partial sums, divided by the normaliser) when bit t of pool_mask is set, otherwise
+// it is the (normalised) keep row alone, as compact_key (token_merging.py:372-376).
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void layer_norm_octet(float (&x)[8], const float (&w)[8], const float (&b)[8],
+                                                 float eps) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += x[i];
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  s += __shfl_xor_sync(0xffffffffu, s, 4);
+  const float mean = s * (1.f / 64.f);
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float d = x[i] - mean;
+    var = fmaf(d, d, var);
+  }
+  var += __shfl_xor_sync(0xffffffffu, var, 1);
+  var += __shfl_xor_sync(0xffffffffu, var, 2);
+  var += __shfl_xor_sync(0xffffffffu, var, 4);
+  const float rstd = rsqrtf(var * (1.f / 64.f) + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = fmaf((x[i] - mean) * rstd, w[i], b[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    compact_qkv_kernel(const T* __restrict__ qkv, long long rows, long long xs, int C,
+                       const float* __restrict__ ln_w, const float* __restrict__ ln_b, float eps,
+                       const int64_t* __restrict__ keep, long long M, int corners,
+                       const int32_t* __restrict__ seg_offsets, const int32_t* __restrict__ entry_src,
+                       const float* __restrict__ entry_w, const float* __restrict__ normalizer,
+                       int pool_mask, T* __restrict__ out, long long os) {
+  constexpr int V = 8;
+  constexpr int kCB = 4;  // 16-byte vectors per lane per pass: 1024 channels
+  const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= M) return;
+  const int oct = lane & 7;
+  float lw[2][8], lb[2][8];
+  if (ln_w != nullptr) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        lw[t][i] = ln_w[t * 64 + oct * 8 + i];
+        lb[t][i] = ln_b[t * 64 + oct * 8 + i];
+      }
+  }
+  int64_t kr = keep[j];
+  if (kr < 0 || kr >= rows) {
+    if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+    kr = 0;
+  }
+  const float norm = normalizer[j];
+  const int32_t* seg = seg_offsets + j * corners;
+  T* orow = out + j * os;
+
+  for (int t = 0; t < 3; ++t) {
+    const bool ln = ln_w != nullptr && t < 2;
+    const bool pooled = (pool_mask >> t) & 1;
+    const int tb = t * C;
+    for (int base = 0; base < C; base += kCB * 32 * V) {
+      float acc[kCB][V];
+#pragma unroll
+      for (int cb = 0; cb < kCB; ++cb) {
+        const int col = base + (cb * 32 + lane) * V;
+        if (col < C) {
+          load_vec<T>(qkv + kr * xs + tb + col, acc[cb]);
+          if (ln) layer_norm_octet(acc[cb], lw[t], lb[t], eps);
+        }
+      }
+      if (pooled) {
+        for (int c = 0; c < corners; ++c) {
+          const int e0 = seg[c], e1 = seg[c + 1];
+          if (e0 == e1) continue;
+          float part[kCB][V];
+#pragma unroll
+          for (int cb = 0; cb < kCB; ++cb)
+#pragma unroll
+            for (int q = 0; q < V; ++q) part[cb][q] = 0.f;
+          for (int e = e0; e < e1; ++e) {
+            int s = __ldg(entry_src + e);
+            float w = __ldg(entry_w + e);
+            if (s < 0 || s >= rows) {
+              if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+              s = 0;
+              w = 0.f;
+            }
+            float x[kCB][V];
+#pragma unroll
+            for (int cb = 0; cb < kCB; ++cb) {
+              const int col = base + (cb * 32 + lane) * V;
+              if (col < C) load_vec<T>(qkv + static_cast<long long>(s) * xs + tb + col, x[cb]);
+            }
+#pragma unroll
+            for (int cb = 0; cb < kCB; ++cb) {
+              const int col = base + (cb * 32 + lane) * V;
+              if (col < C) {
+                if (ln) layer_norm_octet(x[cb], lw[t], lb[t], eps);
+#pragma unroll
+                for (int q = 0; q < V; ++q) part[cb][q] = fmaf(w, x[cb][q], part[cb][q]);
+              }
+            }
+          }
+#pragma unroll
+          for (int cb = 0; cb < kCB; ++cb)
+#pragma unroll
+            for (int q = 0; q < V; ++q) acc[cb][q] += part[cb][q];
+        }
+      }
+#pragma unroll
+      for (int cb = 0; cb < kCB; ++cb) {
+        const int col = base + (cb * 32 + lane) * V;
+        if (col < C) {
+          if (pooled) {
+#pragma unroll
+            for (int q = 0; q < V; ++q) acc[cb][q] = __fdiv_rn(acc[cb][q], norm);
+          }
+          store_vec<T>(orow + tb + col, acc[cb]);
+        }
+      }
+    }
+  }
+}
+
+// Per-head LayerNorm of the q block of qkv rows (query-preserving plans keep every query).
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    head_layernorm_kernel(const T* __restrict__ x, long long rows, long long xs, int C,
+                          const float* __restrict__ w, const float* __restrict__ b, float eps,
+                          T* __restrict__ out, long long os) {
+  constexpr int V = 8;
+  const long long r = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int oct = lane & 7;
+  float lw[8], lb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    lw[i] = w[oct * 8 + i];
+    lb[i] = b[oct * 8 + i];
+  }
+  for (int col = lane * V; col < C; col += 32 * V) {
+    float v[V];
+    load_vec<T>(x + r * xs + col, v);
+    layer_norm_octet(v, lw, lb, eps);
+    store_vec<T>(out + r * os + col, v);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // plan CSR
 // ------------------------------------------------------------------------------------------
 __global__ void csr_keys_kernel(const int64_t* __restrict__ parent, long long n, int corners,
@@ -602,5 +764,56 @@ extern "C" int vb200_row_normalize_bf16(int dtype, const void* x, int64_t x_rows
   else VB200_NORM(__half);
 #undef VB200_NORM
   VB200_CHECK_LAUNCH("row_normalize_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C,
+                                 const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
+                                 int64_t M, int64_t corners, const int32_t* seg_offsets,
+                                 const int32_t* entry_src, const float* entry_w, const float* normalizer,
+                                 int pool_mask, void* out, int64_t os, void* stream) {
+  VB200_REQUIRE(dtype == VB200_BF16 || dtype == VB200_F16, "compact_qkv: dtype must be bf16 or fp16 (got %d)", dtype);
+  VB200_REQUIRE(C > 0 && C % 256 == 0, "compact_qkv: channels per tensor must be a multiple of 256 (got %lld)",
+                (long long)C);
+  VB200_REQUIRE(M >= 0 && rows > 0 && corners >= 1, "compact_qkv: bad sizes");
+  VB200_REQUIRE((ln_weight == nullptr) == (ln_bias == nullptr), "compact_qkv: pass both LayerNorm tensors or neither");
+  if (M == 0) return VB200_OK;
+  VB200_REQUIRE(qkv && keep && out && normalizer && (pool_mask == 0 || seg_offsets),
+                "compact_qkv: null pointer");
+  int rc;
+  if ((rc = check_rows(dtype, qkv, xs, 3 * C, "compact_qkv input")) != VB200_OK) return rc;
+  if ((rc = check_rows(dtype, out, os, 3 * C, "compact_qkv output")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_CQKV(T)                                                                                     \
+  compact_qkv_kernel<T><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                                   \
+      static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, eps, keep, M,        \
+      static_cast<int>(corners), seg_offsets, entry_src, entry_w, normalizer, pool_mask, static_cast<T*>(out), os)
+  if (dtype == VB200_BF16) VB200_CQKV(__nv_bfloat16);
+  else VB200_CQKV(__half);
+#undef VB200_CQKV
+  VB200_CHECK_LAUNCH("compact_qkv_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_head_layernorm(int dtype, const void* x, int64_t rows, int64_t xs, int64_t C,
+                                    const float* weight, const float* bias, float eps, void* out, int64_t os,
+                                    void* stream) {
+  VB200_REQUIRE(dtype == VB200_BF16 || dtype == VB200_F16, "head_layernorm: dtype must be bf16 or fp16");
+  VB200_REQUIRE(C > 0 && C % 64 == 0 && rows >= 0, "head_layernorm: channels must be a multiple of 64");
+  if (rows == 0) return VB200_OK;
+  VB200_REQUIRE(x && out && weight && bias, "head_layernorm: null pointer");
+  VB200_REQUIRE(C % 256 == 0, "head_layernorm: channels must be a multiple of 256");
+  int rc;
+  if ((rc = check_rows(dtype, x, xs, C, "head_layernorm input")) != VB200_OK) return rc;
+  if ((rc = check_rows(dtype, out, os, C, "head_layernorm output")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == VB200_BF16)
+    head_layernorm_kernel<__nv_bfloat16><<<row_blocks(rows), kWarpsPerBlock * 32, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), rows, xs, static_cast<int>(C), weight, bias, eps,
+        static_cast<__nv_bfloat16*>(out), os);
+  else
+    head_layernorm_kernel<__half><<<row_blocks(rows), kWarpsPerBlock * 32, 0, st>>>(
+        static_cast<const __half*>(x), rows, xs, static_cast<int>(C), weight, bias, eps, static_cast<__half*>(out), os);
+  VB200_CHECK_LAUNCH("head_layernorm_kernel");
   return VB200_OK;
 }

@@ -34,6 +34,7 @@ __all__ = [
     "deterministic_weighted_normalizer",
     "row_normalize_bf16",
     "row_gather",
+    "head_layernorm",
     "PlanCSR",
     "build_plan_csr",
 ]
@@ -279,6 +280,22 @@ def row_normalize_bf16(x: torch.Tensor, rows: torch.Tensor | None = None, eps: f
         C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), C.ptr(rows), R, x.shape[1], float(eps),
         out.data_ptr(), out.stride(0), C.stream_of(x.device))
     C.check(rc, "row_normalize_bf16")
+    return out
+
+
+def head_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """LayerNorm over every 64-channel head of the rows of a 2-D bf16 / fp16 tensor
+    (nn.LayerNorm(64) applied to [N, H, 64]); weight / bias [64]."""
+    C.require_cuda(x, "head_layernorm")
+    if x.stride(-1) != 1 or x.data_ptr() % 16 or (x.stride(0) * x.element_size()) % 16:
+        x = x.contiguous()
+    w = weight.reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
+    b = bias.reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
+    out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+    rc = C.lib().vb200_head_layernorm(C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), x.shape[1],
+                                      w.data_ptr(), b.data_ptr(), float(eps), out.data_ptr(), out.stride(0),
+                                      C.stream_of(x.device))
+    C.check(rc, "head_layernorm")
     return out
 
 

@@ -87,6 +87,7 @@ class ShardedGlobalBlock:
         self.group = group
         self.world = world
         self.timers = None  # optional dict name -> list of (start, end) CUDA events
+        self._ln = None     # fp32 q/k LayerNorm parameters, [2, 64] each
 
     def _ev(self, name):
         if self.timers is None:
@@ -120,29 +121,26 @@ class ShardedGlobalBlock:
         self._end(e)
         B, N, C3 = qkv.shape
         C = C3 // 3
-        e = self._ev("qk_norm")
-        q, k, v = qkv.view(B, N, 3, H, C // H).unbind(2)
-        if attn.q_norm is not None:
-            q = attn.q_norm(q)
-            k = attn.k_norm(k)
-        self._end(e)
         e = self._ev("compact")
-        qc = plan.compact(q.reshape(B, N, C).to(qkv.dtype))
-        kc = plan.compact(k.reshape(B, N, C).to(qkv.dtype))
-        vc = plan.compact(v.reshape(B, N, C))
+        if self._ln is None and attn.q_norm is not None:
+            from .attention_block import _ln_params
+            self._ln = _ln_params(attn.q_norm, attn.k_norm)
+        lw, lb, eps = self._ln if self._ln is not None else (None, None, 1e-5)
+        packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111)  # [K_local, 3C]: q | k | v
         self._end(e)
         log_mass = plan.key_log_mass.reshape(-1)
+        K_local = packed.shape[0]
+        kv = packed[:, C:]
         if self.world > 1:
             e = self._ev("all_gather")
-            kc2, vc2, log_mass = gather_merged([kc[0], vc[0], log_mass], self.group)
-            kc, vc = kc2[None], vc2[None]
+            kv, log_mass = gather_merged([kv, log_mass], self.group)
             self._end(e)
         e = self._ev("attention")
-        split = lambda x: x.view(B, x.shape[1], H, C // H).transpose(1, 2)
-        o = mass_bias_attention(split(qc), split(kc), split(vc), log_mass)
+        view = lambda t: t.view(1, t.shape[0], H, C // H).transpose(1, 2)
+        o = mass_bias_attention(view(packed[:, :C]), view(kv[:, :C]), view(kv[:, C:]), log_mass)
         self._end(e)
         e = self._ev("proj_gemm")
-        y = attn.proj(o.transpose(1, 2).reshape(B, qc.shape[1], C))
+        y = attn.proj(o.transpose(1, 2).reshape(B, K_local, C))
         self._end(e)
         e = self._ev("restore")
         out = plan.restore(y)

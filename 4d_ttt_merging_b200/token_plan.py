@@ -205,6 +205,32 @@ class WeightedBilinearTokenPlan:
             return row_gather(x, self._keep_flat).unsqueeze(0)
         return _scatter(x, self._keep_flat, self.csr, self._normalizer_flat, self.kept_tokens).unsqueeze(0)
 
+    def compact_qkv(self, qkv: torch.Tensor, ln_weight: torch.Tensor | None = None,
+                    ln_bias: torch.Tensor | None = None, eps: float = 1e-5,
+                    pool_mask: int = 0b111) -> torch.Tensor:
+        """Fused q/k LayerNorm + Q||K||V compaction of a [N, 3C] (or [1, N, 3C]) qkv buffer in
+        one kernel (``vb200_compact_qkv``); returns [M, 3C].  ``ln_weight`` / ``ln_bias`` are
+        [2, 64] fp32 (q then k) or None.  Bit t of ``pool_mask`` pools tensor t (q, k, v);
+        a clear bit keeps the physical row only (compact_key semantics)."""
+        x = qkv[0] if qkv.ndim == 3 else qkv
+        C.require_cuda(x, "compact_qkv")
+        if x.stride(-1) != 1 or x.data_ptr() % 16 or (x.stride(0) * x.element_size()) % 16:
+            x = x.contiguous()
+        c = x.shape[1] // 3
+        out = torch.empty((self.kept_tokens, 3 * c), device=x.device, dtype=x.dtype)
+        if not self.pool_source_content or self.source_original.shape[1] == 0:
+            pool_mask = 0
+        lw = None if ln_weight is None else ln_weight.reshape(-1).to(torch.float32).contiguous()
+        lb = None if ln_bias is None else ln_bias.reshape(-1).to(torch.float32).contiguous()
+        csr = self.csr
+        rc = C.lib().vb200_compact_qkv(
+            C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), c, C.ptr(lw), C.ptr(lb), float(eps),
+            self._keep_flat.data_ptr(), self.kept_tokens, csr.corners, csr.seg_offsets.data_ptr(),
+            csr.entry_src.data_ptr(), csr.entry_w.data_ptr(), self._normalizer_flat.data_ptr(), int(pool_mask),
+            out.data_ptr(), out.stride(0), C.stream_of(x.device))
+        C.check(rc, "compact_qkv")
+        return out
+
     def compact_key(self, value: torch.Tensor) -> torch.Tensor:
         """Keep physical keys unchanged for the Q-preserving KV-only path."""
         if not self.preserve_destination_keys:

@@ -124,6 +124,26 @@ VB200_API int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64
                        const float* entry_w, const float* normalizer, void* out,
                        int64_t out_row_stride, int64_t C, void* stream);
 
+/* ---- a4 + q/k norm fused: Q||K||V compaction of the qkv projection ---------------------------
+ * qkv: [rows, 3C] rows of [q | k | v] (C = heads * 64, C % 256 == 0), bf16 or fp16.  q and k
+ * are LayerNorm-ed per 64-channel head (weights ln_weight[0:64] / ln_bias[0:64] for q,
+ * [64:128] for k, fp32, biased variance, `eps`) on every row they are read from, then for
+ * tensor t in {q, k, v}: out[j, t] = (keep row + sum_c corner partial sums) / normalizer[j]
+ * when bit t of pool_mask is set, else the keep row alone (compact_key).  fp32 accumulation,
+ * one rounding to `dtype`.  out: [M, 3C].  ln_weight / ln_bias NULL: no normalisation.
+ * Replaces the q_norm / k_norm + compact / compact_key sequence of
+ * vggt_omega/models/layers/attention.py:337-374 (token_merging.py:343-376). */
+VB200_API int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t row_stride, int64_t C,
+                                const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
+                                int64_t M, int64_t corners, const int32_t* seg_offsets,
+                                const int32_t* entry_src, const float* entry_w, const float* normalizer,
+                                int pool_mask, void* out, int64_t out_row_stride, void* stream);
+/* Per-64-channel-head LayerNorm of rows (the dense queries of query-preserving plans and the
+ * special queries): out[r] = LN(x[r]).  C % 256 == 0. */
+VB200_API int vb200_head_layernorm(int dtype, const void* x, int64_t rows, int64_t row_stride, int64_t C,
+                                   const float* weight, const float* bias, float eps, void* out,
+                                   int64_t out_row_stride, void* stream);
+
 /* ---- a6: top-4 gather (merged -> tokens) ----------------------------------------------------
  * out[keep[k]] = y[k];  out[src[s]] = sum_c w[s,c] * y[parent[s,c]]
  * For 16-bit dtypes the weights are rounded to `dtype` and each product is rounded to

@@ -105,3 +105,44 @@ def test_uniform_convex_plan(pkg, oracle, cuda_device):
     par = keep[plan.source_parent_compact[0].cpu().numpy()]
     assert np.all(par // (4 * tpf) == (src // (4 * tpf))[:, None])
     assert pkg.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("preserve,special", [(False, False), (False, True), (True, True), (True, False)])
+def test_fused_qkv_path_bf16(pkg, oracle, cuda_device, preserve, special):
+    """dim 256 / 4 heads in bf16: compute_attention takes the fused LayerNorm + Q||K||V
+    compaction kernel; compared with the oracle restatement of the reference call site."""
+    rng = np.random.default_rng(5 + 2 * preserve + special)
+    dim, heads, frames, tpf, n_special = 256, 4, 3, 90, 5
+    N = frames * tpf
+    K = 80
+    m = pkg.GlobalAttention(dim, heads, device=cuda_device, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(torch.from_numpy(rng.standard_normal(p.shape).astype(np.float32) * (0.1 if p.ndim > 1 else 0.5)))
+    params = {k: to_np(v) for k, v in m.state_dict().items()}
+    params["qkv.bias_mask"] = params.pop("bias_mask")
+    special_ids = np.concatenate([np.arange(f * tpf, f * tpf + n_special) for f in range(frames)])
+    others = np.setdiff1d(np.arange(N), special_ids)
+    keep = np.sort(np.concatenate([special_ids, rng.choice(others, K - special_ids.size, replace=False)]))
+    src = np.setdiff1d(np.arange(N), keep)
+    parent = np.stack([rng.choice(K, 4, replace=False) for _ in src])
+    w = rng.dirichlet(np.ones(4), size=src.size).astype(np.float32)
+    norm = oracle.normalizer(parent, w, K)
+    o2c = np.full(N, -1)
+    o2c[keep] = np.arange(K)
+    t = lambda a, dt=torch.long: torch.as_tensor(a, device=cuda_device, dtype=dt)
+    nt = t(norm, torch.float32).view(1, -1, 1)
+    plan = pkg.WeightedBilinearTokenPlan(
+        keep=t(keep)[None], source_original=t(src)[None], source_parent_compact=t(parent)[None],
+        source_pool_weights=t(w, torch.float32)[None], source_restore_weights=t(w, torch.float32)[None],
+        original_tokens=N, normalizer=nt, preserve_queries=preserve, preserve_destination_keys=preserve,
+        dense_special_queries=special, special_query_original=t(special_ids), special_query_compact=t(o2c[special_ids]),
+        key_log_mass=nt[..., 0].log())
+    x = oracle.round_bf16(rng.standard_normal((N, dim)).astype(np.float32))
+    with torch.no_grad():
+        y = m(t(x, torch.bfloat16)[None], token_plan=plan)
+    pd = dict(keep=keep, source=src, parent=parent, weights=w, normalizer=norm, special=special_ids,
+              special_compact=o2c[special_ids])
+    ref = oracle.global_attention_forward(x, params, pd, heads=heads, preserve_queries=preserve, dense_special=special)
+    assert_close(to_np(y[0]), ref, "bf16")
+    assert pkg.device_error_flags() == 0
