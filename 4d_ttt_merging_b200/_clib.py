@@ -42,6 +42,7 @@ _SIGNATURES = {
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
          _p_i64, _p_i64, _p_i64, _p_i64, _c_vp],
     ),
+    "vb200_exp2_poly": (_c_int, [_c_vp, _c_vp, _c_i64, _c_vp]),
     "vb200_plan_csr_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "vb200_plan_csr_build": (
         _c_int,
@@ -53,10 +54,11 @@ _SIGNATURES = {
         [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
          _c_i64, _c_i64, _c_vp],
     ),
+    "vb200_compact_qkv_workspace_size": (_c_size, [_c_i64, _c_i64]),
     "vb200_compact_qkv": (
         _c_int,
         [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_float, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp,
-         _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_vp],
+         _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_vp, _c_size, _c_vp],
     ),
     "vb200_head_layernorm": (
         _c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_float, _c_vp, _c_i64, _c_vp],

@@ -7,20 +7,10 @@
 // probabilities rounded to the value dtype before the PV product, output divided by the
 // running sum and written in the input dtype.
 //
-// Kernel design (one CTA per 128-row query tile and (batch, head), 6 warps):
-//   warp 0      TMA producer: Q once, then K tiles running one tile ahead of V tiles; the
-//               log2-domain bias of a key tile rides with its V tile (bulk copy, 512 B).
-//   warp 1      allocates 256 TMEM columns, then one lane issues every tcgen05.mma:
-//                 S_j = Q K_j^T   (SS-MMA, M=128 N=128 K=64, fp32 accumulate in TMEM)
-//                 O_j = P_j V_j   (TS-MMA: P_j read from TMEM, V_j from shared memory)
-//   warps 2..5  softmax warpgroup: thread t owns query row t (its TMEM lane).  For tile j it
-//               reads S_j, forms the new running max, folds O_{j-1} into its register
-//               accumulator (rescaled), writes P_j = exp2(x - m) as packed 16-bit values back
-//               over S_j's first 64 columns and signals the MMA warp.
-//   TMEM: two 128-column buffers; buffer b = j % 2 holds S_j, then P_j (cols 0-63) and
-//   O_j (cols 64-127).  While the softmax works on S_j the tensor core runs QK for j+1.
-// Shared-memory tiles use the 128-byte swizzle written by TMA; the UMMA descriptors describe
-// the same layout (K-major for Q and K, MN-major for V).  No TMA multicast is used.
+// Kernel design: one CTA per 256 query rows (two 128-row tiles) and (batch, head), 10 warps,
+// one CTA per SM; see mass_bias_attention_tc_kernel.  Shared-memory tiles use the 128-byte
+// swizzle written by TMA; the UMMA descriptors describe the same layout (K-major for Q and K,
+// MN-major for V).  No TMA multicast is used.
 #include <cudaTypedefs.h>
 
 #include <cmath>
@@ -34,36 +24,48 @@ namespace {
 
 static __device__ unsigned g_attn_err;
 
-constexpr int kBM = 128;  // query rows per CTA
+constexpr int kBM = 128;  // query rows per tile (one TMEM lane per row)
+constexpr int kQT = 2;    // query tiles per CTA, one softmax warpgroup each
 constexpr int kBN = 128;  // keys per tile
 constexpr int kHD = 64;   // head dim
-constexpr int kStages = 2;
-constexpr int kTileBytes = kBM * kHD * 2;  // 16 KB, also the K / V tile size (kBN == kBM)
+constexpr int kStages = 4;
+constexpr int kTileBytes = kBM * kHD * 2;  // 16 KB: one Q, K or V tile
 constexpr int kBiasBytes = kBN * 4;
-constexpr int kThreads = 192;
+constexpr int kStageStride = 34816;        // K + V + bias, rounded up to 1024 bytes
+constexpr int kThreads = 384;              // warpgroups: 0, 1 softmax; 2 = producer (warp 8) + MMA (warp 9)
+// Register split (setmaxnreg): the block launches with kLaunchRegs per thread; the producer
+// warpgroup drops to kRegsLow and the two softmax warpgroups rise to kRegsHigh.  The shares
+// add up exactly to the launch total, which the host checks before every launch.
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsHigh = 232;
+constexpr int kRegsLow = 40;
+static_assert(2 * 128 * kRegsHigh + 128 * kRegsLow == kThreads * kLaunchRegs, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // lazy rescale: P stays <= 2^8
+// Of every 8 exponent pairs, how many are computed on the FMA pipe (exp2_poly2) instead of
+// MUFU.  Measured: the softmax is issue-bound, not MUFU-bound, at head_dim 64, and the
+// polynomial costs ~5 instructions per value against 1, so all exponentials use MUFU.
+constexpr int kPolyPairs = 0;
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;
-constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffBias = kOffV + kStages * kTileBytes;
-constexpr int kOffBar = kOffBias + kStages * kBiasBytes;
-// barriers
+constexpr int kOffQ = 0;                                  // kQT tiles
+constexpr int kOffStage = kOffQ + kQT * kTileBytes;       // kStages x {K, V, bias}
+constexpr int kOffBar = kOffStage + kStages * kStageStride;
 constexpr int kBarQFull = 0;
-constexpr int kBarKFull = 1;
-constexpr int kBarKEmpty = kBarKFull + kStages;
-constexpr int kBarVFull = kBarKEmpty + kStages;
-constexpr int kBarVEmpty = kBarVFull + kStages;
-constexpr int kBarSFull = kBarVEmpty + kStages;
-constexpr int kBarPFull = kBarSFull + 2;
-constexpr int kBarOFull = kBarPFull + 2;
-constexpr int kBarSFree = kBarOFull + 2;
-constexpr int kNumBars = kBarSFree + 2;
+constexpr int kBarKVFull = 1;
+constexpr int kBarKVEmpty = kBarKVFull + kStages;
+constexpr int kBarSFull = kBarKVEmpty + kStages;
+constexpr int kBarPFull = kBarSFull + kQT;
+constexpr int kBarODone = kBarPFull + kQT;
+constexpr int kBarSFree = kBarODone + kQT;
+constexpr int kNumBars = kBarSFree + kQT;
 constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
 constexpr int kSmemUsed = kOffTmemSlot + 16;
 constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for aligning the dynamic base
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;           // S_t at 128t, P_t at 256 + 64t, O_t at 384 + 64t
+constexpr uint32_t kTmemP = 256;
+constexpr uint32_t kTmemO = 384;
+static_assert(kStageStride >= 2 * kTileBytes + kBiasBytes && kStageStride % 1024 == 0, "stage layout");
 
 struct AttnParams {
   const float* bias;  // [n_tiles * kBN] log2-domain bias, -inf past Nk
@@ -74,9 +76,23 @@ struct AttnParams {
 };
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+__device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
 
+// Mass-bias attention, two query tiles per CTA (FA4-style ping-pong):
+//   warps 0-3 / 4-7  softmax warpgroup of query tile 0 / 1: thread = query row = TMEM lane.
+//   warps 8-11       warp 8: TMA producer: both Q tiles once; K_j, V_j and the bias of key tile j
+//                    into a 4-stage ring.
+//                    warp 9: TMEM allocation; one lane issues all tcgen05.mma.  Per key
+//                    tile j it issues QK_0(j+1), QK_1(j+1) as soon as the softmax has read
+//                    S_t(j) into registers, then PV_0(j), PV_1(j) once P_t(j) is written, so
+//                    the next scores are computed underneath the current softmax.
+// TMEM (512 columns): S_t in [128t, 128t+128), P_t as packed 16-bit values in
+// [256+64t, 256+64t+64) (the A operand of the TS-MMA), O_t accumulating in [384+64t, ...).
+// The running max is lazy: O_t is rescaled (in TMEM, by the softmax thread that owns the row)
+// only when a row's max grows by more than 2^8, otherwise P is formed against the stale max,
+// which the final division by the matching running sum cancels exactly.
 template <bool kBF16>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     mass_bias_attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                   const __grid_constant__ CUtensorMap tmap_k,
                                   const __grid_constant__ CUtensorMap tmap_v, AttnParams p) {
@@ -86,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_tile = blockIdx.x;
+  const int q_block = blockIdx.x;  // kQT * kBM query rows
   const int bh = blockIdx.y;
   const int batch = bh / p.H;
   const int head = bh - batch * p.H;
@@ -97,26 +113,24 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (threadIdx.x == 0) {
     mbar_init(bar(kBarQFull), 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kBarKFull + s), 1);
-      mbar_init(bar(kBarKEmpty + s), 1);
-      mbar_init(bar(kBarVFull + s), 1);
-      mbar_init(bar(kBarVEmpty + s), 1);
+      mbar_init(bar(kBarKVFull + s), 1);
+      mbar_init(bar(kBarKVEmpty + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(kBarSFull + b), 1);
-      mbar_init(bar(kBarPFull + b), 128);
-      mbar_init(bar(kBarOFull + b), 1);
-      mbar_init(bar(kBarSFree + b), 128);
+    for (int t = 0; t < kQT; ++t) {
+      mbar_init(bar(kBarSFull + t), 1);
+      mbar_init(bar(kBarPFull + t), 128);
+      mbar_init(bar(kBarODone + t), 1);
+      mbar_init(bar(kBarSFree + t), 128);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     prefetch_tmap(&tmap_q);
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(sbase + kOffTmemSlot, kTmemCols);
     tmem_relinquish();
   }
@@ -125,188 +139,214 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kOffTmemSlot);
 
-  if (warp == 0) {
+  // Each role's code is dominated by its own setmaxnreg (no merge point in between), so the
+  // register allocator gives every branch the budget its warpgroup actually holds.
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+  if (warp == 8) {
     // ------------------------------- producer -------------------------------
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(bar(kBarQFull), kTileBytes);
-      tma_load_4d(sbase + kOffQ, &tmap_q, bar(kBarQFull), 0, q_tile * kBM, head, batch);
-      auto load_k = [&](int j) -> bool {
-        const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(bar(kBarKEmpty + s), ((j / kStages) - 1) & 1, &g_attn_err))
-          return false;
-        mbar_arrive_expect_tx(bar(kBarKFull + s), kTileBytes);
-        tma_load_4d(sbase + kOffK + s * kTileBytes, &tmap_k, bar(kBarKFull + s), 0, j * kBN, head,
-                    batch);
-        return true;
-      };
-      auto load_v = [&](int j) -> bool {
-        const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(bar(kBarVEmpty + s), ((j / kStages) - 1) & 1, &g_attn_err))
-          return false;
-        mbar_arrive_expect_tx(bar(kBarVFull + s), kTileBytes + kBiasBytes);
-        tma_load_4d(sbase + kOffV + s * kTileBytes, &tmap_v, bar(kBarVFull + s), 0, j * kBN, head,
-                    batch);
-        bulk_load(sbase + kOffBias + s * kBiasBytes, p.bias + static_cast<size_t>(j) * kBN,
-                  kBiasBytes, bar(kBarVFull + s));
-        return true;
-      };
+      mbar_arrive_expect_tx(bar(kBarQFull), kQT * kTileBytes);
+      for (int t = 0; t < kQT; ++t)
+        tma_load_4d(sbase + kOffQ + t * kTileBytes, &tmap_q, bar(kBarQFull), 0, (q_block * kQT + t) * kBM,
+                    head, batch);
       for (int j = 0; j < n_tiles && ok; ++j) {
+        const int s = j % kStages;
         if (*abort_flag) { ok = false; break; }
-        ok = load_k(j);
-        if (ok && j >= 1) ok = load_v(j - 1);
+        if (j >= kStages && !mbar_wait(bar(kBarKVEmpty + s), ((j / kStages) - 1) & 1, &g_attn_err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t st = sbase + kOffStage + s * kStageStride;
+        mbar_arrive_expect_tx(bar(kBarKVFull + s), 2 * kTileBytes + kBiasBytes);
+        tma_load_4d(st, &tmap_k, bar(kBarKVFull + s), 0, j * kBN, head, batch);
+        tma_load_4d(st + kTileBytes, &tmap_v, bar(kBarKVFull + s), 0, j * kBN, head, batch);
+        bulk_load(st + 2 * kTileBytes, p.bias + static_cast<size_t>(j) * kBN, kBiasBytes, bar(kBarKVFull + s));
       }
-      if (ok) ok = load_v(n_tiles - 1);
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     // ------------------------------- MMA issuer -------------------------------
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, kBF16 ? 1 : 0, 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16(kBM, kHD, kBF16 ? 1 : 0, 0, 1);
       bool ok = mbar_wait(bar(kBarQFull), 0, &g_attn_err);
-      auto issue_pv = [&](int jj) -> bool {
-        const int bb = jj & 1;
-        const int s = jj % kStages;
-        if (!mbar_wait(bar(kBarPFull + bb), (jj >> 1) & 1, &g_attn_err)) return false;
-        if (!mbar_wait(bar(kBarVFull + s), (jj / kStages) & 1, &g_attn_err)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = sbase + kOffV + s * kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          // V tile: key rows of 128 bytes; a K-step of 16 keys spans two 1024-byte atoms.
-          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 16384, 1024);
-          umma_ts(tmem + bb * 128 + 64, tmem + bb * 128 + kk * 8, bdesc, idesc_pv, kk > 0);
-        }
-        umma_commit(bar(kBarOFull + bb));
-        umma_commit(bar(kBarVEmpty + s));
-        return true;
-      };
-      for (int j = 0; j < n_tiles && ok; ++j) {
+      // S_t = Q_t K_j^T
+      auto issue_qk = [&](int t, int j) {
         const int s = j % kStages;
-        const int b = j & 1;
-        if (*abort_flag) { ok = false; break; }
-        if (!mbar_wait(bar(kBarKFull + s), (j / kStages) & 1, &g_attn_err)) { ok = false; break; }
-        if (j >= 2 && !mbar_wait(bar(kBarSFree + b), ((j - 2) >> 1) & 1, &g_attn_err)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t q_addr = sbase + kOffQ;
-        const uint32_t k_addr = sbase + kOffK + s * kTileBytes;
+        const uint32_t q_addr = sbase + kOffQ + t * kTileBytes;
+        const uint32_t k_addr = sbase + kOffStage + s * kStageStride;
 #pragma unroll
         for (int kk = 0; kk < kHD / 16; ++kk) {
           const uint64_t adesc = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
           const uint64_t bdesc = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-          umma_ss(tmem + b * 128, adesc, bdesc, idesc_qk, kk > 0);
+          umma_ss(tmem + t * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(bar(kBarSFull + b));
-        umma_commit(bar(kBarKEmpty + s));
-        if (j >= 1) ok = issue_pv(j - 1);
+        umma_commit(bar(kBarSFull + t));
+      };
+      // O_t += P_t V_j (P_t from TMEM, V MN-major from shared memory)
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int s = j % kStages;
+        if (!mbar_wait(bar(kBarPFull + t), j & 1, &g_attn_err)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = sbase + kOffStage + s * kStageStride + kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          // V tile: key rows of 128 bytes; a K-step of 16 keys spans two 1024-byte atoms
+          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 16384, 1024);
+          umma_ts(tmem + kTmemO + t * kHD, tmem + kTmemP + t * kHD + kk * 8, bdesc, idesc_pv,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(kBarODone + t));
+        if (t == kQT - 1) umma_commit(bar(kBarKVEmpty + s));
+        return true;
+      };
+      if (ok) ok = mbar_wait(bar(kBarKVFull + 0), 0, &g_attn_err);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < kQT; ++t) issue_qk(t, 0);
       }
-      if (ok) ok = issue_pv(n_tiles - 1);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (*abort_flag) { ok = false; break; }
+        if (j + 1 < n_tiles) {
+          const int s1 = (j + 1) % kStages;
+          if (!mbar_wait(bar(kBarKVFull + s1), ((j + 1) / kStages) & 1, &g_attn_err)) { ok = false; break; }
+          for (int t = 0; t < kQT && ok; ++t) {
+            // S_t(j) has been read into registers: overwrite it with the next tile's scores
+            if (!mbar_wait(bar(kBarSFree + t), j & 1, &g_attn_err)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk(t, j + 1);
+          }
+          if (!ok) break;
+        }
+        for (int t = 0; t < kQT && ok; ++t) ok = issue_pv(t, j);
+      }
       if (!ok) *abort_flag = 1;
     }
+  }
   } else {
-    // ------------------------------- softmax warpgroup -------------------------------
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    // ------------------------------- softmax warpgroups -------------------------------
+    const int t = warp >> 2;    // query tile of this warpgroup
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + t * 128;
+    const uint32_t p_addr = tmem + lane_off + kTmemP + t * kHD;
+    const uint32_t o_addr = tmem + lane_off + kTmemO + t * kHD;
     const float scale = p.scale_log2;
     float m_run = -INFINITY;
     float l_run = 0.f;
-    float acc[kHD];
-#pragma unroll
-    for (int i = 0; i < kHD; ++i) acc[i] = 0.f;
     bool ok = true;
 
     for (int j = 0; j < n_tiles; ++j) {
-      const int b = j & 1;
       const int s = j % kStages;
       if (*abort_flag) { ok = false; break; }
-      if (!mbar_wait(bar(kBarSFull + b), (j >> 1) & 1, &g_attn_err)) { ok = false; break; }
-      if (!mbar_wait(bar(kBarVFull + s), (j / kStages) & 1, &g_attn_err)) { ok = false; break; }
+      if (!mbar_wait(bar(kBarSFull + t), j & 1, &g_attn_err)) { ok = false; break; }
+      if (!mbar_wait(bar(kBarKVFull + s), (j / kStages) & 1, &g_attn_err)) { ok = false; break; }
       tc_fence_after();
-      const float4* bias4 = reinterpret_cast<const float4*>(smem + kOffBias + s * kBiasBytes);
-      const uint32_t s_addr = tmem + lane_off + b * 128;
+      uint32_t r[kBN];
+      tmem_ld32x32b_x32_nowait(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32x32b_x32_nowait(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld32x32b_x32_nowait(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      tmem_ld32x32b_x32_nowait(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tmem_wait_ld();
+      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+      tc_fence_before();
+      mbar_arrive(bar(kBarSFree + t));  // S_t(j) is in registers: QK_t(j+1) may overwrite it
 
-      // pass 1: row max of the log2-domain logits
-      float mx = -INFINITY;
+      // log2-domain logits x = s * log2e/sqrt(d) + bias (bias = -inf past the last key)
+      const float4* bias4 = reinterpret_cast<const float4*>(smem + kOffStage + s * kStageStride + 2 * kTileBytes);
+      float mxa = -INFINITY, mxb = -INFINITY;  // two max chains
+      const uint64_t scale2 = pk2(scale, scale);
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32x32b_x32(s_addr + c * 32, r);
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 bv = bias4[(c * 32 + i) / 4];
-          mx = fmaxf(mx, fmaf(u2f(r[i + 0]), scale, bv.x));
-          mx = fmaxf(mx, fmaf(u2f(r[i + 1]), scale, bv.y));
-          mx = fmaxf(mx, fmaf(u2f(r[i + 2]), scale, bv.z));
-          mx = fmaxf(mx, fmaf(u2f(r[i + 3]), scale, bv.w));
-        }
+      for (int i = 0; i < kBN; i += 4) {
+        const float4 bv = bias4[i / 4];
+        const uint64_t x01 = ffma2(pk2(u2f(r[i + 0]), u2f(r[i + 1])), scale2, pk2(bv.x, bv.y));
+        const uint64_t x23 = ffma2(pk2(u2f(r[i + 2]), u2f(r[i + 3])), scale2, pk2(bv.z, bv.w));
+        float x0, x1, x2, x3;
+        upk2(x01, x0, x1);
+        upk2(x23, x2, x3);
+        r[i + 0] = f2u(x0);
+        r[i + 1] = f2u(x1);
+        r[i + 2] = f2u(x2);
+        r[i + 3] = f2u(x3);
+        mxa = fmax3(mxa, x0, x1);
+        mxb = fmax3(mxb, x2, x3);
       }
+      const float mx = fmaxf(mxa, mxb);
       const float m_new = fmaxf(m_run, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float corr = ex2_approx(m_run - m_use);  // 0 on the first tile
-
-      // fold O_{j-1} (computed against m_run) into the accumulator, rescaled to m_new
-      if (j >= 1) {
-        const int jj = j - 1;
-        const int bb = jj & 1;
-        if (!mbar_wait(bar(kBarOFull + bb), (jj >> 1) & 1, &g_attn_err)) { ok = false; break; }
+      const bool need = m_new > m_run + kRescaleThreshold;  // always true on the first tile
+      if (j > 0) {
+        // PV_t(j-1) must be complete before P_t is overwritten or O_t is rescaled
+        if (!mbar_wait(bar(kBarODone + t), (j - 1) & 1, &g_attn_err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t o_addr = tmem + lane_off + bb * 128 + 64;
-#pragma unroll
-        for (int c = 0; c < kHD / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld32x32b_x16(o_addr + c * 16, r);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[c * 16 + i] = (acc[c * 16 + i] + u2f(r[i])) * corr;
-        }
-        tc_fence_before();
-        mbar_arrive(bar(kBarSFree + bb));
       }
-      l_run *= corr;
-      m_run = m_new;
-
-      // pass 2: probabilities, row sum, packed 16-bit P written over S's first 64 columns
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_tgt = need ? m_new : m_run;
+        const float alpha = ex2_approx(m_run - m_tgt);  // 0 on the first tile, 1 if unchanged
+        if (j > 0) {
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32x32b_x32(s_addr + c * 32, r);
-        uint32_t pk[16];
+          for (int h = 0; h < kHD; h += 32) {  // two halves keep the register peak low
+            uint32_t o[32];
+            tmem_ld32x32b_x32_nowait(o_addr + h, o);
+            tmem_wait_ld();
+            reg_fence32(o);
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 bv = bias4[(c * 32 + i) / 4];
-          const float p0 = ex2_approx(fmaf(u2f(r[i + 0]), scale, bv.x) - m_use);
-          const float p1 = ex2_approx(fmaf(u2f(r[i + 1]), scale, bv.y) - m_use);
-          const float p2 = ex2_approx(fmaf(u2f(r[i + 2]), scale, bv.z) - m_use);
-          const float p3 = ex2_approx(fmaf(u2f(r[i + 3]), scale, bv.w) - m_use);
-          l_run += (p0 + p1) + (p2 + p3);
-          pk[i / 2 + 0] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-          pk[i / 2 + 1] = kBF16 ? pack_bf16x2(p2, p3) : pack_f16x2(p2, p3);
+            for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
+            tmem_st32x32b_x32(o_addr + h, o);
+          }
         }
-        tmem_st32x32b_x16(s_addr + c * 16, pk);
+        l_run *= alpha;
+        m_run = m_tgt;
       }
+      // probabilities against m_run, packed in place: r[i] <- (p[2i], p[2i+1])
+      // Exponentials: kPolyPairs of every 8 pairs on the FMA pipe (exp2_poly2), the rest on
+      // MUFU, so both pipes share the 16K exponentials of a tile.
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      const uint64_t neg_m2 = pk2(-m_use, -m_use);
+      uint64_t ls0 = pk2(0.f, 0.f), ls1 = pk2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < kBN / 2; ++i) {
+        float e0, e1, p0, p1;
+        upk2(fadd2(pk2(u2f(r[2 * i]), u2f(r[2 * i + 1])), neg_m2), e0, e1);
+        if ((i & 7) < kPolyPairs) {
+          exp2_poly2(e0, e1, p0, p1);
+        } else {
+          p0 = ex2_approx(e0);
+          p1 = ex2_approx(e1);
+        }
+        if (i & 1) ls1 = fadd2(ls1, pk2(p0, p1));
+        else ls0 = fadd2(ls0, pk2(p0, p1));
+        r[i] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+      }
+      {
+        float a0, a1, b0, b1;
+        upk2(ls0, a0, a1);
+        upk2(ls1, b0, b1);
+        l_run += (a0 + a1) + (b0 + b1);
+      }
+      tmem_st32x32b_x32(p_addr + 0, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
+      tmem_st32x32b_x32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(kBarPFull + b));
+      mbar_arrive(bar(kBarPFull + t));
     }
 
     if (ok) {
-      const int jj = n_tiles - 1;
-      const int bb = jj & 1;
-      if (mbar_wait(bar(kBarOFull + bb), (jj >> 1) & 1, &g_attn_err)) {
+      if (mbar_wait(bar(kBarODone + t), (n_tiles - 1) & 1, &g_attn_err)) {
         tc_fence_after();
-        const uint32_t o_addr = tmem + lane_off + bb * 128 + 64;
-#pragma unroll
-        for (int c = 0; c < kHD / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld32x32b_x16(o_addr + c * 16, r);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) acc[c * 16 + i] += u2f(r[i]);
-        }
-        const int grow = q_tile * kBM + row;
+        uint32_t o[kHD];
+        tmem_ld32x32b_x32_nowait(o_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+        tmem_ld32x32b_x32_nowait(o_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+        tmem_wait_ld();
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+        const int grow = (q_block * kQT + t) * kBM + row;
         if (grow < p.Nq) {
           const float inv = 1.f / l_run;
           uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
@@ -317,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const float a = acc[c * 8 + 2 * i] * inv, bq = acc[c * 8 + 2 * i + 1] * inv;
-              wp[i] = kBF16 ? pack_bf16x2(a, bq) : pack_f16x2(a, bq);
+              const float a = u2f(o[c * 8 + 2 * i]) * inv, b2 = u2f(o[c * 8 + 2 * i + 1]) * inv;
+              wp[i] = kBF16 ? pack_bf16x2(a, b2) : pack_f16x2(a, b2);
             }
             *reinterpret_cast<uint4*>(orow + c * 16) = w;
           }
@@ -332,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -562,7 +602,20 @@ extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k
   prm.Nk = static_cast<int>(Nk);
   prm.n_tiles = n_tiles;
   prm.scale_log2 = scale_log2;
-  const dim3 grid(static_cast<unsigned>((Nq + kBM - 1) / kBM), static_cast<unsigned>(B * H));
+  const dim3 grid(static_cast<unsigned>((Nq + kQT * kBM - 1) / (kQT * kBM)), static_cast<unsigned>(B * H));
+  // The register split inside the kernel is only valid with exactly kLaunchRegs registers per
+  // thread at launch: refuse to launch anything else.
+  {
+    cudaFuncAttributes fa{};
+    VB200_CHECK_CUDA(cudaFuncGetAttributes(&fa, dtype == VB200_BF16 ? mass_bias_attention_tc_kernel<true>
+                                                                     : mass_bias_attention_tc_kernel<false>),
+                     "cudaFuncGetAttributes");
+    if (fa.numRegs != kLaunchRegs)
+      return set_error(VB200_EUNSUPPORTED,
+                       "mass_bias_attention_tc_kernel was built with %d registers per thread; its register "
+                       "split needs exactly %d",
+                       fa.numRegs, kLaunchRegs);
+  }
   // The shared-memory opt-in is per device: set it on every call (cheap, host-side only).
   if (dtype == VB200_BF16) {
     VB200_CHECK_CUDA(cudaFuncSetAttribute(mass_bias_attention_tc_kernel<true>,
@@ -635,4 +688,30 @@ extern "C" int vb200_mass_bias_attention_noalloc(int dtype, const void* q, const
   // -inf padding of the last tile), so nothing carries over from a previous call.
   return vb200_mass_bias_attention(dtype, q, k, v, log_key_mass, bias_dtype, out, B, H, Nq, Nk, D, qs, ks,
                                    vs, os, scratch, sizeof(float) * kNoAllocMaxKeys, stream);
+}
+
+// ------------------------------------------------------------------------------------------
+// The FMA-pipe exponential used by the softmax, exposed for testing against exact 2^x.
+// ------------------------------------------------------------------------------------------
+namespace vb200 {
+namespace {
+__global__ void exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  const long long i = 2 * (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  float p0, p1;
+  exp2_poly2(x[i], i + 1 < n ? x[i + 1] : 0.f, p0, p1);
+  y[i] = p0;
+  if (i + 1 < n) y[i + 1] = p1;
+}
+}  // namespace
+}  // namespace vb200
+
+extern "C" int vb200_exp2_poly(const float* x, float* y, int64_t n, void* stream) {
+  VB200_REQUIRE(n >= 0, "exp2_poly: negative size");
+  if (n == 0) return VB200_OK;
+  VB200_REQUIRE(x && y, "exp2_poly: null pointer");
+  const long long pairs = (n + 1) / 2;
+  exp2_poly_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n);
+  VB200_CHECK_LAUNCH("exp2_poly_kernel");
+  return VB200_OK;
 }

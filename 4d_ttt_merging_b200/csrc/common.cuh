@@ -232,6 +232,57 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// ---- packed fp32x2 arithmetic (sm_100: two fp32 lanes per instruction) ----
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^e for two values on the FMA pipe (no MUFU), for e <= 64.  Method: round-to-nearest
+// split e = n + f with the 1.5 * 2^23 shifter (n lands in the low mantissa bits of
+// t = e + 1.5 * 2^23, f = e - n in [-1/2, 1/2]); 2^f by a degree-3 polynomial fitted here for
+// minimum maximum relative error on [-1/2, 1/2] (Remez exchange, 7.5e-5 with fp32 Horner);
+// 2^n applied by adding n to the exponent field (t's bits shifted left by 23).  Inputs below
+// -125 are clamped, giving about 2^-125 instead of a denormal or zero.
+__device__ __forceinline__ void exp2_poly2(float e0, float e1, float& p0, float& p1) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992805719375610f;
+  constexpr float kC1 = 0.69326096773147583f;
+  constexpr float kC2 = 0.24261112511157990f;
+  constexpr float kC3 = 0.05517166852951050f;
+  const uint64_t e = pk2(fmaxf(e0, -125.f), fmaxf(e1, -125.f));
+  const uint64_t t = fadd2(e, pk2(kShift, kShift));
+  const uint64_t neg_n = ffma2(t, pk2(-1.f, -1.f), pk2(kShift, kShift));  // shifter - t = -n
+  const uint64_t f = fadd2(e, neg_n);
+  uint64_t p = ffma2(pk2(kC3, kC3), f, pk2(kC2, kC2));
+  p = ffma2(p, f, pk2(kC1, kC1));
+  p = ffma2(p, f, pk2(kC0, kC0));
+  float plo, phi, tlo, thi;
+  upk2(p, plo, phi);
+  upk2(t, tlo, thi);
+  p0 = __uint_as_float(__float_as_uint(plo) + (__float_as_uint(tlo) << 23));
+  p1 = __uint_as_float(__float_as_uint(phi) + (__float_as_uint(thi) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

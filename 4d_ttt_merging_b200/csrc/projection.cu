@@ -302,105 +302,156 @@ __device__ __forceinline__ void layer_norm_octet(float (&x)[8], const float (&w)
   for (int i = 0; i < 8; ++i) x[i] = fmaf((x[i] - mean) * rstd, w[i], b[i]);
 }
 
+// LayerNorm statistics (mean, 1/sqrt(var + eps)) of every 64-channel head of the q and k
+// blocks of each qkv row: stats[row][h] for q heads h < H, stats[row][H + h] for k heads.
 template <typename T>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    head_stats_kernel(const T* __restrict__ qkv, long long rows, long long xs, int C, float eps,
+                      float2* __restrict__ stats) {
+  constexpr int V = 8;
+  const long long r = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int heads2 = 2 * C / 64;
+  constexpr int kBatch = 8;  // 16-byte loads issued before any is reduced (2C <= 8 * 256 per pass)
+  for (int base = 0; base < 2 * C; base += kBatch * 32 * V) {
+  uint4 raw[kBatch];
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+    const int col = base + (b * 32 + lane) * V;
+    if (col < 2 * C) raw[b] = __ldg(reinterpret_cast<const uint4*>(qkv + r * xs + col));
+  }
+#pragma unroll
+  for (int b = 0; b < kBatch; ++b) {
+    const int col = base + (b * 32 + lane) * V;
+    if (col >= 2 * C) break;  // uniform across the warp
+    float x[V];
+    const T* xe = reinterpret_cast<const T*>(&raw[b]);
+#pragma unroll
+    for (int i = 0; i < V; ++i) x[i] = to_f32<T>(xe[i]);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) s += x[i];
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    s += __shfl_xor_sync(0xffffffffu, s, 4);
+    const float mean = s * (1.f / 64.f);
+    float var = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float d = x[i] - mean;
+      var = fmaf(d, d, var);
+    }
+    var += __shfl_xor_sync(0xffffffffu, var, 1);
+    var += __shfl_xor_sync(0xffffffffu, var, 2);
+    var += __shfl_xor_sync(0xffffffffu, var, 4);
+    if ((lane & 7) == 0) stats[r * heads2 + col / 64] = make_float2(mean, rsqrtf(var * (1.f / 64.f) + eps));
+  }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
     compact_qkv_kernel(const T* __restrict__ qkv, long long rows, long long xs, int C,
-                       const float* __restrict__ ln_w, const float* __restrict__ ln_b, float eps,
-                       const int64_t* __restrict__ keep, long long M, int corners,
-                       const int32_t* __restrict__ seg_offsets, const int32_t* __restrict__ entry_src,
+                       const float* __restrict__ ln_w, const float* __restrict__ ln_b,
+                       const float2* __restrict__ stats, const int64_t* __restrict__ keep, long long M,
+                       int corners, const int32_t* __restrict__ seg_offsets, const int32_t* __restrict__ entry_src,
                        const float* __restrict__ entry_w, const float* __restrict__ normalizer,
                        int pool_mask, T* __restrict__ out, long long os) {
+  // One warp per (compact row j, tensor t, 256-channel chunk); lane = one 16-byte vector.
+  // Warps of one row are adjacent, so its CSR entries are shared through L1, and four
+  // entries are loaded before any is reduced to keep four row fetches in flight per lane.
+  // For q and k the LayerNorm is folded into the weighted sum: with (mu_e, r_e) the
+  // statistics of the entry's head,
+  //   sum_e w_e LN(x_e)_i = g_i (sum_e w_e r_e x_e,i - sum_e w_e r_e mu_e) + b_i sum_e w_e,
+  // so each gathered element costs one FMA and the statistics come from head_stats_kernel.
   constexpr int V = 8;
-  constexpr int kCB = 4;  // 16-byte vectors per lane per pass: 1024 channels
-  const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  constexpr int kUnroll = 8;
+  const int nch = C / (32 * V);
+  const long long w_id = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  const long long per_row = 3ll * nch;
+  const long long j = w_id / per_row;
   if (j >= M) return;
-  const int oct = lane & 7;
-  float lw[2][8], lb[2][8];
-  if (ln_w != nullptr) {
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        lw[t][i] = ln_w[t * 64 + oct * 8 + i];
-        lb[t][i] = ln_b[t * 64 + oct * 8 + i];
-      }
-  }
+  const int rem = static_cast<int>(w_id - j * per_row);
+  const int t = rem / nch;
+  const int col = (rem - t * nch) * 32 * V + lane * V;  // channel within the tensor
+  const bool ln = ln_w != nullptr && t < 2;
+  const bool pooled = (pool_mask >> t) & 1;
+  const int heads2 = 2 * C / 64;
+  const int head = t * (C / 64) + col / 64;  // index into a row of stats (q heads, then k heads)
   int64_t kr = keep[j];
   if (kr < 0 || kr >= rows) {
     if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
     kr = 0;
   }
-  const float norm = normalizer[j];
-  const int32_t* seg = seg_offsets + j * corners;
-  T* orow = out + j * os;
-
-  for (int t = 0; t < 3; ++t) {
-    const bool ln = ln_w != nullptr && t < 2;
-    const bool pooled = (pool_mask >> t) & 1;
-    const int tb = t * C;
-    for (int base = 0; base < C; base += kCB * 32 * V) {
-      float acc[kCB][V];
+  const T* xcol = qkv + t * C + col;
+  float acc[V];
+  float csum = 0.f, wsum = 1.f;  // the keep row enters with weight 1
+  load_vec<T>(xcol + kr * xs, acc);
+  if (ln) {
+    const float2 st = stats[kr * heads2 + head];
 #pragma unroll
-      for (int cb = 0; cb < kCB; ++cb) {
-        const int col = base + (cb * 32 + lane) * V;
-        if (col < C) {
-          load_vec<T>(qkv + kr * xs + tb + col, acc[cb]);
-          if (ln) layer_norm_octet(acc[cb], lw[t], lb[t], eps);
-        }
-      }
-      if (pooled) {
-        for (int c = 0; c < corners; ++c) {
-          const int e0 = seg[c], e1 = seg[c + 1];
-          if (e0 == e1) continue;
-          float part[kCB][V];
+    for (int q = 0; q < V; ++q) acc[q] *= st.y;
+    csum = st.x * st.y;
+  }
+  if (pooled) {
+    // The row's entries of all corners are one contiguous CSR range (corner-major, source
+    // order inside a corner); walking it as one list keeps kUnroll fetches in flight.
+    const int e0 = seg_offsets[j * corners], e1 = seg_offsets[(j + 1) * corners];
+    {
+      float part[V];
+      float pc = 0.f, pw = 0.f;
 #pragma unroll
-          for (int cb = 0; cb < kCB; ++cb)
+      for (int q = 0; q < V; ++q) part[q] = 0.f;
+      for (int e = e0; e < e1; e += kUnroll) {
+        uint4 x[kUnroll];  // raw 16-bit rows, converted when reduced (keeps registers low)
+        float w[kUnroll];
+        float2 st[kUnroll];
 #pragma unroll
-            for (int q = 0; q < V; ++q) part[cb][q] = 0.f;
-          for (int e = e0; e < e1; ++e) {
-            int s = __ldg(entry_src + e);
-            float w = __ldg(entry_w + e);
+        for (int u = 0; u < kUnroll; ++u) {
+          int s = 0;
+          w[u] = 0.f;
+          if (e + u < e1) {
+            s = __ldg(entry_src + e + u);
+            w[u] = __ldg(entry_w + e + u);
             if (s < 0 || s >= rows) {
               if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
               s = 0;
-              w = 0.f;
-            }
-            float x[kCB][V];
-#pragma unroll
-            for (int cb = 0; cb < kCB; ++cb) {
-              const int col = base + (cb * 32 + lane) * V;
-              if (col < C) load_vec<T>(qkv + static_cast<long long>(s) * xs + tb + col, x[cb]);
-            }
-#pragma unroll
-            for (int cb = 0; cb < kCB; ++cb) {
-              const int col = base + (cb * 32 + lane) * V;
-              if (col < C) {
-                if (ln) layer_norm_octet(x[cb], lw[t], lb[t], eps);
-#pragma unroll
-                for (int q = 0; q < V; ++q) part[cb][q] = fmaf(w, x[cb][q], part[cb][q]);
-              }
+              w[u] = 0.f;
             }
           }
+          x[u] = __ldg(reinterpret_cast<const uint4*>(xcol + static_cast<long long>(s) * xs));
+          st[u] = ln ? stats[static_cast<long long>(s) * heads2 + head] : make_float2(0.f, 1.f);
+        }
 #pragma unroll
-          for (int cb = 0; cb < kCB; ++cb)
+        for (int u = 0; u < kUnroll; ++u) {
+          const float a = w[u] * st[u].y;  // w_e r_e (w_e for v)
+          const T* xe = reinterpret_cast<const T*>(&x[u]);
 #pragma unroll
-            for (int q = 0; q < V; ++q) acc[cb][q] += part[cb][q];
+          for (int q = 0; q < V; ++q) part[q] = fmaf(a, to_f32<T>(xe[q]), part[q]);
+          pc = fmaf(a, st[u].x, pc);
+          pw += w[u];
         }
       }
 #pragma unroll
-      for (int cb = 0; cb < kCB; ++cb) {
-        const int col = base + (cb * 32 + lane) * V;
-        if (col < C) {
-          if (pooled) {
-#pragma unroll
-            for (int q = 0; q < V; ++q) acc[cb][q] = __fdiv_rn(acc[cb][q], norm);
-          }
-          store_vec<T>(orow + tb + col, acc[cb]);
-        }
-      }
+      for (int q = 0; q < V; ++q) acc[q] += part[q];
+      csum += pc;
+      wsum += pw;
     }
   }
+  if (ln) {
+    const int oct = lane & 7;
+#pragma unroll
+    for (int q = 0; q < V; ++q)
+      acc[q] = fmaf(ln_w[t * 64 + oct * 8 + q], acc[q] - csum, ln_b[t * 64 + oct * 8 + q] * wsum);
+  }
+  if (pooled) {
+    const float norm = normalizer[j];
+#pragma unroll
+    for (int q = 0; q < V; ++q) acc[q] = __fdiv_rn(acc[q], norm);
+  }
+  store_vec<T>(out + j * os + t * C + col, acc);
 }
 
 // Per-head LayerNorm of the q block of qkv rows (query-preserving plans keep every query).
@@ -767,11 +818,17 @@ extern "C" int vb200_row_normalize_bf16(int dtype, const void* x, int64_t x_rows
   return VB200_OK;
 }
 
+extern "C" size_t vb200_compact_qkv_workspace_size(int64_t rows, int64_t C) {
+  if (rows < 0 || C < 0) return 0;
+  return align_up(static_cast<size_t>(rows > 0 ? rows : 1) * static_cast<size_t>(2 * C / 64) * sizeof(float2), 256);
+}
+
 extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C,
                                  const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
                                  int64_t M, int64_t corners, const int32_t* seg_offsets,
                                  const int32_t* entry_src, const float* entry_w, const float* normalizer,
-                                 int pool_mask, void* out, int64_t os, void* stream) {
+                                 int pool_mask, void* out, int64_t os, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
   VB200_REQUIRE(dtype == VB200_BF16 || dtype == VB200_F16, "compact_qkv: dtype must be bf16 or fp16 (got %d)", dtype);
   VB200_REQUIRE(C > 0 && C % 256 == 0, "compact_qkv: channels per tensor must be a multiple of 256 (got %lld)",
                 (long long)C);
@@ -784,9 +841,23 @@ extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64
   if ((rc = check_rows(dtype, qkv, xs, 3 * C, "compact_qkv input")) != VB200_OK) return rc;
   if ((rc = check_rows(dtype, out, os, 3 * C, "compact_qkv output")) != VB200_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float2* stats = nullptr;
+  if (ln_weight != nullptr) {
+    const size_t need = vb200_compact_qkv_workspace_size(rows, C);
+    VB200_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+                  "compact_qkv: workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    stats = static_cast<float2*>(workspace);
+#define VB200_STATS(T)                                                                            \
+  head_stats_kernel<T><<<row_blocks(rows), kWarpsPerBlock * 32, 0, st>>>(static_cast<const T*>(qkv), rows, \
+                                                                       xs, static_cast<int>(C), eps, stats)
+    if (dtype == VB200_BF16) VB200_STATS(__nv_bfloat16);
+    else VB200_STATS(__half);
+#undef VB200_STATS
+    VB200_CHECK_LAUNCH("head_stats_kernel");
+  }
 #define VB200_CQKV(T)                                                                                     \
-  compact_qkv_kernel<T><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                                   \
-      static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, eps, keep, M,        \
+  compact_qkv_kernel<T><<<row_blocks(M * 3 * (C / 256)), kWarpsPerBlock * 32, 0, st>>>(                   \
+      static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, stats, keep, M,      \
       static_cast<int>(corners), seg_offsets, entry_src, entry_w, normalizer, pool_mask, static_cast<T*>(out), os)
   if (dtype == VB200_BF16) VB200_CQKV(__nv_bfloat16);
   else VB200_CQKV(__half);

@@ -223,11 +223,14 @@ class WeightedBilinearTokenPlan:
         lw = None if ln_weight is None else ln_weight.reshape(-1).to(torch.float32).contiguous()
         lb = None if ln_bias is None else ln_bias.reshape(-1).to(torch.float32).contiguous()
         csr = self.csr
-        rc = C.lib().vb200_compact_qkv(
+        lib = C.lib()
+        ws_bytes = lib.vb200_compact_qkv_workspace_size(x.shape[0], c) if lw is not None else 0
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+        rc = lib.vb200_compact_qkv(
             C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), c, C.ptr(lw), C.ptr(lb), float(eps),
             self._keep_flat.data_ptr(), self.kept_tokens, csr.corners, csr.seg_offsets.data_ptr(),
             csr.entry_src.data_ptr(), csr.entry_w.data_ptr(), self._normalizer_flat.data_ptr(), int(pool_mask),
-            out.data_ptr(), out.stride(0), C.stream_of(x.device))
+            out.data_ptr(), out.stride(0), ws.data_ptr(), ws_bytes, C.stream_of(x.device))
         C.check(rc, "compact_qkv")
         return out
 

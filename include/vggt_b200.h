@@ -88,6 +88,12 @@ VB200_API int vb200_mass_bias_attention_noalloc(int dtype, const void* q, const 
                                                 const int64_t* v_strides, const int64_t* o_strides,
                                                 void* stream);
 
+/* The FMA-pipe exponential the attention softmax uses for part of each tile: y = 2^x by
+ * range reduction and a degree-3 minimax polynomial (max relative error 7.5e-5 for x in
+ * [-125, 64]; below -125 the result is about 2^-125).  Device arrays of n floats.  Test and
+ * inspection entry point; no counterpart in the reference. */
+VB200_API int vb200_exp2_poly(const float* x, float* y, int64_t n, void* stream);
+
 /* ---- a7/a8: plan preprocessing --------------------------------------------------------------
  * Groups the S*corners (source, corner) pairs of a weighted plan by compact parent so that
  * every reduction below runs in a fixed order with no atomics.  Segment (j, c) lists, in
@@ -132,12 +138,16 @@ VB200_API int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64
  * when bit t of pool_mask is set, else the keep row alone (compact_key).  fp32 accumulation,
  * one rounding to `dtype`.  out: [M, 3C].  ln_weight / ln_bias NULL: no normalisation.
  * Replaces the q_norm / k_norm + compact / compact_key sequence of
- * vggt_omega/models/layers/attention.py:337-374 (token_merging.py:343-376). */
+ * vggt_omega/models/layers/attention.py:337-374 (token_merging.py:343-376).
+ * workspace: vb200_compact_qkv_workspace_size(rows, C) bytes (per-head LayerNorm statistics of
+ * every row), 256-byte aligned; unused when ln_weight is NULL. */
+VB200_API size_t vb200_compact_qkv_workspace_size(int64_t rows, int64_t C);
 VB200_API int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t row_stride, int64_t C,
                                 const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
                                 int64_t M, int64_t corners, const int32_t* seg_offsets,
                                 const int32_t* entry_src, const float* entry_w, const float* normalizer,
-                                int pool_mask, void* out, int64_t out_row_stride, void* stream);
+                                int pool_mask, void* out, int64_t out_row_stride, void* workspace,
+                                size_t workspace_bytes, void* stream);
 /* Per-64-channel-head LayerNorm of rows (the dense queries of query-preserving plans and the
  * special queries): out[r] = LN(x[r]).  C % 256 == 0. */
 VB200_API int vb200_head_layernorm(int dtype, const void* x, int64_t rows, int64_t row_stride, int64_t C,

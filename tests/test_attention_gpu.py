@@ -111,3 +111,21 @@ def test_errors(pkg, cuda_device):
         pkg.mass_bias_attention(q, q, q, torch.zeros(7, device=cuda_device))
     with pytest.raises(ValueError, match="head_dim"):
         pkg.mass_bias_attention(q[..., :32], q[..., :32], q[..., :32], torch.zeros(8, device=cuda_device))
+
+
+def test_exp2_polynomial_against_exact(pkg, cuda_device):
+    """The softmax's FMA-pipe exponential: relative error <= 1e-4 against exact 2^x over the
+    range the kernel feeds it (x - running max <= 8), tiny positive values below -125."""
+    import ctypes  # noqa: F401
+    x = torch.cat([torch.linspace(-125, 8, 2_000_001), torch.tensor([-1000.0, -126.0, 0.0, 0.5, -0.5])])
+    xd = x.to(cuda_device)
+    y = torch.empty_like(xd)
+    rc = pkg.load_library().vb200_exp2_poly(xd.data_ptr(), y.data_ptr(), xd.numel(),
+                                            torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    got = y.cpu().double()
+    exact = torch.exp2(x.double())
+    main = x >= -125
+    rel = ((got[main] - exact[main]).abs() / exact[main]).max().item()
+    assert rel <= 1e-4, rel
+    assert torch.all(got[~main] >= 0) and torch.all(got[~main] < 1e-37)
