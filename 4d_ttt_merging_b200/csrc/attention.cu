@@ -15,6 +15,7 @@
 
 #include <cmath>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -30,8 +31,13 @@ constexpr int kBN = 128;  // keys per tile
 constexpr int kHD = 64;   // head dim
 constexpr int kStages = 4;
 constexpr int kTileBytes = kBM * kHD * 2;  // 16 KB: one Q, K or V tile
-constexpr int kBiasBytes = kBN * 4;
-constexpr int kStageStride = 34816;        // K + V + bias, rounded up to 1024 bytes
+// The per-key bias rides in the QK product: an extra K=16 chunk holds 1 in column 0 of every
+// query row (kOffQx, written once per CTA) and 8 * bias_j in column 0 of key row j (kx tiles
+// prepared in global memory), so S' = q.k + 8 bias_j and the log2-domain logit is
+// S' * log2(e)/8 (8 = sqrt(64); multiplying a 16-bit value by 8 is exact).  The chunk uses the
+// no-swizzle K-major layout: [16 row groups][2 K halves][8 rows][16 bytes].
+constexpr int kKxBytes = 4096;
+constexpr int kStageStride = 36864;        // K, V (16 KB each) + extra K chunk (4 KB)
 constexpr int kThreads = 384;              // warpgroups: 0, 1 softmax; 2 = producer (warp 8) + MMA (warp 9)
 // Register split (setmaxnreg): the block launches with kLaunchRegs per thread; the producer
 // warpgroup drops to kRegsLow and the two softmax warpgroups rise to kRegsHigh.  The shares
@@ -46,10 +52,12 @@ constexpr float kRescaleThreshold = 8.0f;  // lazy rescale: P stays <= 2^8
 // MUFU.  Measured: the softmax is issue-bound, not MUFU-bound, at head_dim 64, and the
 // polynomial costs ~5 instructions per value against 1, so all exponentials use MUFU.
 constexpr int kPolyPairs = 0;
+constexpr int kNamedBarTurn = 1;  // named barriers 1 and 2 (0 is __syncthreads)
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 constexpr int kOffQ = 0;                                  // kQT tiles
-constexpr int kOffStage = kOffQ + kQT * kTileBytes;       // kStages x {K, V, bias}
+constexpr int kOffQx = kOffQ + kQT * kTileBytes;          // constant extra Q chunk
+constexpr int kOffStage = kOffQx + kKxBytes;              // kStages x {K, V, extra K chunk}
 constexpr int kOffBar = kOffStage + kStages * kStageStride;
 constexpr int kBarQFull = 0;
 constexpr int kBarKVFull = 1;
@@ -65,10 +73,10 @@ constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for aligning the dynamic 
 constexpr uint32_t kTmemCols = 512;           // S_t at 128t, P_t at 256 + 64t, O_t at 384 + 64t
 constexpr uint32_t kTmemP = 256;
 constexpr uint32_t kTmemO = 384;
-static_assert(kStageStride >= 2 * kTileBytes + kBiasBytes && kStageStride % 1024 == 0, "stage layout");
+static_assert(kStageStride >= 2 * kTileBytes + kKxBytes && kStageStride % 1024 == 0, "stage layout");
 
 struct AttnParams {
-  const float* bias;  // [n_tiles * kBN] log2-domain bias, -inf past Nk
+  const uint8_t* kx;  // [n_tiles][kKxBytes] extra K chunks (8 * bias, masked past Nk)
   void* out;
   long long o_sb, o_sh, o_sn;  // element strides
   int H, Nq, Nk, n_tiles;
@@ -125,6 +133,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  if (threadIdx.x < kKxBytes / 16) {
+    // extra Q chunk: 1 in column 0 of every row (half 0 of each 8-row group), 0 elsewhere
+    const int half = (threadIdx.x >> 3) & 1;
+    const uint32_t one = kBF16 ? 0x3F80u : 0x3C00u;  // 1.0 in bf16 / fp16
+    *reinterpret_cast<uint4*>(smem + kOffQx + 16 * threadIdx.x) = make_uint4(half == 0 ? one : 0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();  // generic-proxy writes become visible to the tensor core
+  }
   if (warp == 8 && lane == 0) {
     prefetch_tmap(&tmap_q);
     prefetch_tmap(&tmap_k);
@@ -159,10 +174,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const uint32_t st = sbase + kOffStage + s * kStageStride;
-        mbar_arrive_expect_tx(bar(kBarKVFull + s), 2 * kTileBytes + kBiasBytes);
+        mbar_arrive_expect_tx(bar(kBarKVFull + s), 2 * kTileBytes + kKxBytes);
         tma_load_4d(st, &tmap_k, bar(kBarKVFull + s), 0, j * kBN, head, batch);
         tma_load_4d(st + kTileBytes, &tmap_v, bar(kBarKVFull + s), 0, j * kBN, head, batch);
-        bulk_load(st + 2 * kTileBytes, p.bias + static_cast<size_t>(j) * kBN, kBiasBytes, bar(kBarKVFull + s));
+        bulk_load(st + 2 * kTileBytes, p.kx + static_cast<size_t>(j) * kKxBytes, kKxBytes, bar(kBarKVFull + s));
       }
       if (!ok) *abort_flag = 1;
     }
@@ -183,6 +198,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t bdesc = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
           umma_ss(tmem + t * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
         }
+        // + 1 * (8 bias_j): the extra K=16 chunk (no swizzle: LBO 128 B along K, SBO 256 B)
+        umma_ss(tmem + t * 128, smem_desc_noswz(sbase + kOffQx, 128, 256),
+                smem_desc_noswz(k_addr + 2 * kTileBytes, 128, 256), idesc_qk, 1u);
         umma_commit(bar(kBarSFull + t));
       };
       // O_t += P_t V_j (P_t from TMEM, V MN-major from shared memory)
@@ -236,140 +254,145 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t p_addr = tmem + lane_off + kTmemP + t * kHD;
     const uint32_t o_addr = tmem + lane_off + kTmemO + t * kHD;
     const float scale = p.scale_log2;
+    const uint64_t scale2 = pk2(scale, scale);
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
+    // The two warpgroups take turns for the exponential phase (named barriers kNamedBarTurn
+    // and kNamedBarTurn + 1): while one drives MUFU, the other stores P, loads its next S and
+    // reduces the row max.  Every iteration performs its hand-over even after a failed wait,
+    // so neither warpgroup can be left waiting on the other.
+    const int my_turn = kNamedBarTurn + t;
+    const int other_turn = kNamedBarTurn + (1 - t);
+    if (t == 1) named_bar_arrive(kNamedBarTurn, 256);  // warpgroup 0 goes first
 
     for (int j = 0; j < n_tiles; ++j) {
-      const int s = j % kStages;
-      if (*abort_flag) { ok = false; break; }
-      if (!mbar_wait(bar(kBarSFull + t), j & 1, &g_attn_err)) { ok = false; break; }
-      if (!mbar_wait(bar(kBarKVFull + s), (j / kStages) & 1, &g_attn_err)) { ok = false; break; }
-      tc_fence_after();
+      ok = ok && !*abort_flag;
+      if (ok) ok = mbar_wait(bar(kBarSFull + t), j & 1, &g_attn_err);
+      ok = __all_sync(0xffffffffu, ok);  // warp-uniform before warp-collective TMEM access
       uint32_t r[kBN];
-      tmem_ld32x32b_x32_nowait(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      tmem_ld32x32b_x32_nowait(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      tmem_ld32x32b_x32_nowait(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-      tmem_ld32x32b_x32_nowait(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
-      tmem_wait_ld();
-      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[96]));
-      tc_fence_before();
-      mbar_arrive(bar(kBarSFree + t));  // S_t(j) is in registers: QK_t(j+1) may overwrite it
-
-      // log2-domain logits x = s * log2e/sqrt(d) + bias (bias = -inf past the last key)
-      const float4* bias4 = reinterpret_cast<const float4*>(smem + kOffStage + s * kStageStride + 2 * kTileBytes);
-      float mxa = -INFINITY, mxb = -INFINITY;  // two max chains
-      const uint64_t scale2 = pk2(scale, scale);
-#pragma unroll
-      for (int i = 0; i < kBN; i += 4) {
-        const float4 bv = bias4[i / 4];
-        const uint64_t x01 = ffma2(pk2(u2f(r[i + 0]), u2f(r[i + 1])), scale2, pk2(bv.x, bv.y));
-        const uint64_t x23 = ffma2(pk2(u2f(r[i + 2]), u2f(r[i + 3])), scale2, pk2(bv.z, bv.w));
-        float x0, x1, x2, x3;
-        upk2(x01, x0, x1);
-        upk2(x23, x2, x3);
-        r[i + 0] = f2u(x0);
-        r[i + 1] = f2u(x1);
-        r[i + 2] = f2u(x2);
-        r[i + 3] = f2u(x3);
-        mxa = fmax3(mxa, x0, x1);
-        mxb = fmax3(mxb, x2, x3);
-      }
-      const float mx = fmaxf(mxa, mxb);
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = m_new > m_run + kRescaleThreshold;  // always true on the first tile
-      if (j > 0) {
-        // PV_t(j-1) must be complete before P_t is overwritten or O_t is rescaled
-        if (!mbar_wait(bar(kBarODone + t), (j - 1) & 1, &g_attn_err)) { ok = false; break; }
+      float m_use = 0.f;
+      if (ok) {
         tc_fence_after();
-      }
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_tgt = need ? m_new : m_run;
-        const float alpha = ex2_approx(m_run - m_tgt);  // 0 on the first tile, 1 if unchanged
+        tmem_ld32x32b_x32_nowait(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld32x32b_x32_nowait(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        tmem_ld32x32b_x32_nowait(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+        tmem_ld32x32b_x32_nowait(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+        tmem_wait_ld();
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+        tc_fence_before();
+        mbar_arrive(bar(kBarSFree + t));  // S_t(j) is in registers: QK_t(j+1) may overwrite it
+
+        // S' = q.k + 8 bias; the log2-domain logit is S' * scale (scale = log2(e)/8 > 0), so
+        // the row max is taken on S' directly (four 3-input max chains)
+        float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kBN; i += 8) {
+          mxa = fmax3(mxa, u2f(r[i + 0]), u2f(r[i + 1]));
+          mxb = fmax3(mxb, u2f(r[i + 2]), u2f(r[i + 3]));
+          mxc = fmax3(mxc, u2f(r[i + 4]), u2f(r[i + 5]));
+          mxd = fmax3(mxd, u2f(r[i + 6]), u2f(r[i + 7]));
+        }
+        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd)) * scale);
+        const bool need = m_new > m_run + kRescaleThreshold;  // always true on the first tile
         if (j > 0) {
+          // PV_t(j-1) must be complete before P_t is overwritten or O_t is rescaled
+          ok = mbar_wait(bar(kBarODone + t), (j - 1) & 1, &g_attn_err);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) tc_fence_after();
+        }
+        if (ok && __any_sync(0xffffffffu, need)) {
+          const float m_tgt = need ? m_new : m_run;
+          const float alpha = ex2_approx(m_run - m_tgt);  // 0 on the first tile, 1 if unchanged
+          if (j > 0) {
 #pragma unroll
-          for (int h = 0; h < kHD; h += 32) {  // two halves keep the register peak low
-            uint32_t o[32];
-            tmem_ld32x32b_x32_nowait(o_addr + h, o);
-            tmem_wait_ld();
-            reg_fence32(o);
+            for (int h = 0; h < kHD; h += 32) {  // two halves keep the register peak low
+              uint32_t o[32];
+              tmem_ld32x32b_x32_nowait(o_addr + h, o);
+              tmem_wait_ld();
+              reg_fence32(o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
-            tmem_st32x32b_x32(o_addr + h, o);
+              for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
+              tmem_st32x32b_x32(o_addr + h, o);
+            }
           }
+          l_run *= alpha;
+          m_run = m_tgt;
         }
-        l_run *= alpha;
-        m_run = m_tgt;
+        m_use = (m_run == -INFINITY) ? 0.f : m_run;
       }
-      // probabilities against m_run, packed in place: r[i] <- (p[2i], p[2i+1])
-      // Exponentials: kPolyPairs of every 8 pairs on the FMA pipe (exp2_poly2), the rest on
-      // MUFU, so both pipes share the 16K exponentials of a tile.
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      const uint64_t neg_m2 = pk2(-m_use, -m_use);
-      uint64_t ls0 = pk2(0.f, 0.f), ls1 = pk2(0.f, 0.f);
+
+      named_bar_sync(my_turn, 256);  // this warpgroup's turn on MUFU
+      if (ok) {
+        // P = 2^(S' * scale - m), packed in place: r[i] <- (p[2i], p[2i+1]).  kPolyPairs of
+        // every 8 pairs may use the FMA-pipe exponential instead of MUFU.
+        const uint64_t neg_m2 = pk2(-m_use, -m_use);
+        uint64_t ls0 = pk2(0.f, 0.f), ls1 = pk2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < kBN / 2; ++i) {
-        float e0, e1, p0, p1;
-        upk2(fadd2(pk2(u2f(r[2 * i]), u2f(r[2 * i + 1])), neg_m2), e0, e1);
-        if ((i & 7) < kPolyPairs) {
-          exp2_poly2(e0, e1, p0, p1);
-        } else {
-          p0 = ex2_approx(e0);
-          p1 = ex2_approx(e1);
+        for (int i = 0; i < kBN / 2; ++i) {
+          float e0, e1, p0, p1;
+          upk2(ffma2(pk2(u2f(r[2 * i]), u2f(r[2 * i + 1])), scale2, neg_m2), e0, e1);
+          if ((i & 7) < kPolyPairs) {
+            exp2_poly2(e0, e1, p0, p1);
+          } else {
+            p0 = ex2_approx(e0);
+            p1 = ex2_approx(e1);
+          }
+          if (i & 1) ls1 = fadd2(ls1, pk2(p0, p1));
+          else ls0 = fadd2(ls0, pk2(p0, p1));
+          r[i] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
         }
-        if (i & 1) ls1 = fadd2(ls1, pk2(p0, p1));
-        else ls0 = fadd2(ls0, pk2(p0, p1));
-        r[i] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-      }
-      {
         float a0, a1, b0, b1;
         upk2(ls0, a0, a1);
         upk2(ls1, b0, b1);
         l_run += (a0 + a1) + (b0 + b1);
       }
-      tmem_st32x32b_x32(p_addr + 0, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
-      tmem_st32x32b_x32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(kBarPFull + t));
+      named_bar_arrive(other_turn, 256);  // hand MUFU to the other warpgroup
+      if (ok) {
+        tmem_st32x32b_x32(p_addr + 0, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
+        tmem_st32x32b_x32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(kBarPFull + t));
+      }
     }
+    if (t == 0) named_bar_sync(kNamedBarTurn, 256);  // consume warpgroup 1's last hand-over
 
     if (ok) {
-      if (mbar_wait(bar(kBarODone + t), (n_tiles - 1) & 1, &g_attn_err)) {
-        tc_fence_after();
-        uint32_t o[kHD];
-        tmem_ld32x32b_x32_nowait(o_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-        tmem_ld32x32b_x32_nowait(o_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
-        tmem_wait_ld();
-        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[32]));
-        const int grow = (q_block * kQT + t) * kBM + row;
-        if (grow < p.Nq) {
-          const float inv = 1.f / l_run;
-          uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
-                          2 * (batch * p.o_sb + head * p.o_sh + static_cast<long long>(grow) * p.o_sn);
+      ok = mbar_wait(bar(kBarODone + t), (n_tiles - 1) & 1, &g_attn_err);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      uint32_t o[kHD];
+      tmem_ld32x32b_x32_nowait(o_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+      tmem_ld32x32b_x32_nowait(o_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      tmem_wait_ld();
+      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      const int grow = (q_block * kQT + t) * kBM + row;
+      if (grow < p.Nq) {
+        const float inv = 1.f / l_run;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
+                        2 * (batch * p.o_sb + head * p.o_sh + static_cast<long long>(grow) * p.o_sn);
 #pragma unroll
-          for (int c = 0; c < kHD / 8; ++c) {
-            uint4 w;
-            uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+        for (int c = 0; c < kHD / 8; ++c) {
+          uint4 w;
+          uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float a = u2f(o[c * 8 + 2 * i]) * inv, b2 = u2f(o[c * 8 + 2 * i + 1]) * inv;
-              wp[i] = kBF16 ? pack_bf16x2(a, b2) : pack_f16x2(a, b2);
-            }
-            *reinterpret_cast<uint4*>(orow + c * 16) = w;
+          for (int i = 0; i < 4; ++i) {
+            const float a = u2f(o[c * 8 + 2 * i]) * inv, b2 = u2f(o[c * 8 + 2 * i + 1]) * inv;
+            wp[i] = kBF16 ? pack_bf16x2(a, b2) : pack_f16x2(a, b2);
           }
+          *reinterpret_cast<uint4*>(orow + c * 16) = w;
         }
-      } else {
-        ok = false;
       }
     }
     if (!ok) *abort_flag = 1;
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {
@@ -394,6 +417,29 @@ __global__ void prepare_bias_kernel(const TB* log_mass, float* bias, int Nk, int
     }
   }
   bias[j] = v;
+}
+
+// Extra K chunks of the tensor-core path, one 4 KB tile per 128 keys in the no-swizzle K-major
+// layout [16 row groups][2 K halves][8 rows][8 elements]: column 0 of key row j holds
+// 8 * round_to_dtype(log_mass[j]) (0 without a bias), keys past Nk hold a large negative value
+// (their exponential underflows to 0), every other element is 0.
+template <typename TB, typename TQ>
+__global__ void prepare_kx_kernel(const TB* log_mass, TQ* kx, int Nk, long long total) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const long long tile = idx >> 11;
+  const int rem = static_cast<int>(idx & 2047);
+  const int g = rem >> 7, half = (rem >> 6) & 1, r8 = (rem >> 3) & 7, e = rem & 7;
+  float val = 0.f;
+  if (half == 0 && e == 0) {
+    const long long key = tile * kBN + g * 8 + r8;
+    if (key < Nk) {
+      val = log_mass == nullptr ? 0.f : 8.f * to_f32<TQ>(from_f32<TQ>(to_f32<TB>(log_mass[key])));
+    } else {
+      val = sizeof(TQ) == 2 && std::is_same<TQ, __half>::value ? -65504.f : -1.0e30f;
+    }
+  }
+  kx[idx] = from_f32<TQ>(val);
 }
 
 // fp32 path: one warp per (query row, batch*head); lanes stride over keys with their own
@@ -492,8 +538,10 @@ unsigned attention_error_word(int clear) {
 using namespace vb200;
 
 extern "C" size_t vb200_mass_bias_attention_workspace_size(int64_t Nk) {
+  // the larger of the fp32 path's padded bias (512 B per key tile) and the tensor-core
+  // path's extra K chunks (4 KB per key tile)
   const int64_t tiles = (Nk + kBN - 1) / kBN;
-  return align_up(static_cast<size_t>(tiles > 0 ? tiles : 1) * kBN * sizeof(float), 256);
+  return align_up(static_cast<size_t>(tiles > 0 ? tiles : 1) * kKxBytes, 256);
 }
 
 namespace {
@@ -519,6 +567,26 @@ int launch_bias(int dtype, const void* log_mass, int bias_dtype, float* bias, in
   }
 #undef VB200_BIAS_CASE
   VB200_CHECK_LAUNCH("prepare_bias_kernel");
+  return VB200_OK;
+}
+
+int launch_kx(int dtype, const void* log_mass, int bias_dtype, void* kx, int Nk, int n_tiles, cudaStream_t st) {
+  const long long total = static_cast<long long>(n_tiles) * (kKxBytes / 2);
+  const dim3 grid(static_cast<unsigned>((total + 255) / 256)), block(256);
+#define VB200_KX_CASE(TB, TQ) \
+  prepare_kx_kernel<TB, TQ><<<grid, block, 0, st>>>(static_cast<const TB*>(log_mass), static_cast<TQ*>(kx), Nk, total)
+  if (bias_dtype == VB200_F32) {
+    if (dtype == VB200_BF16) VB200_KX_CASE(float, __nv_bfloat16);
+    else VB200_KX_CASE(float, __half);
+  } else if (bias_dtype == VB200_BF16) {
+    if (dtype == VB200_BF16) VB200_KX_CASE(__nv_bfloat16, __nv_bfloat16);
+    else VB200_KX_CASE(__nv_bfloat16, __half);
+  } else {
+    if (dtype == VB200_BF16) VB200_KX_CASE(__half, __nv_bfloat16);
+    else VB200_KX_CASE(__half, __half);
+  }
+#undef VB200_KX_CASE
+  VB200_CHECK_LAUNCH("prepare_kx_kernel");
   return VB200_OK;
 }
 
@@ -566,13 +634,13 @@ extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k
   int rc = check_sm100();
   if (rc != VB200_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* bias = static_cast<float*>(workspace);
   const int n_tiles = static_cast<int>((Nk + kBN - 1) / kBN);
-  rc = launch_bias(dtype, log_key_mass, bias_dtype, bias, static_cast<int>(Nk), n_tiles * kBN, st);
-  if (rc != VB200_OK) return rc;
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(kHD));
 
   if (dtype == VB200_F32) {
+    float* bias = static_cast<float*>(workspace);
+    rc = launch_bias(dtype, log_key_mass, bias_dtype, bias, static_cast<int>(Nk), n_tiles * kBN, st);
+    if (rc != VB200_OK) return rc;
     const dim3 grid(static_cast<unsigned>((Nq + 7) / 8), static_cast<unsigned>(B * H));
     mass_bias_attention_f32_kernel<<<grid, 256, 0, st>>>(
         static_cast<const float*>(q), static_cast<const float*>(k), static_cast<const float*>(v),
@@ -586,13 +654,15 @@ extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k
   VB200_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15u) == 0 && os[0] % 8 == 0 && os[1] % 8 == 0 &&
                     os[2] % 8 == 0,
                 "output rows must be 16-byte aligned");
+  rc = launch_kx(dtype, log_key_mass, bias_dtype, workspace, static_cast<int>(Nk), n_tiles, st);
+  if (rc != VB200_OK) return rc;
   CUtensorMap tq, tk, tv;
   if ((rc = make_qkv_map(&tq, q, dtype, Nq, H, B, qs)) != VB200_OK) return rc;
   if ((rc = make_qkv_map(&tk, k, dtype, Nk, H, B, ks)) != VB200_OK) return rc;
   if ((rc = make_qkv_map(&tv, v, dtype, Nk, H, B, vs)) != VB200_OK) return rc;
 
   AttnParams prm;
-  prm.bias = bias;
+  prm.kx = static_cast<const uint8_t*>(workspace);
   prm.out = out;
   prm.o_sb = os[0];
   prm.o_sh = os[1];
@@ -640,12 +710,13 @@ extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k
 // to obtain scratch from), and latency-critical serving loops that must not call cudaMalloc /
 // cudaFree because those calls synchronise the device.  For them the attention's only scratch
 // buffer — the padded log2-domain bias — lives in a fixed file-scope device array instead of a
-// caller workspace.  Every GPU that loads this library holds the array (1 MiB) until exit.
+// caller workspace.  Every GPU that loads this library holds the array (4 MiB) until exit.
 // ------------------------------------------------------------------------------------------
 namespace {
 
-constexpr int64_t kNoAllocMaxKeys = 262144;  // keys per call; a multiple of the 128-key tile
-static __device__ __align__(256) float g_noalloc_bias[kNoAllocMaxKeys];
+constexpr int64_t kNoAllocMaxKeys = 131072;  // keys per call; a multiple of the 128-key tile
+constexpr size_t kNoAllocBytes = static_cast<size_t>(kNoAllocMaxKeys / kBN) * kKxBytes;  // 4 MiB
+static __device__ __align__(256) uint8_t g_noalloc_bias[kNoAllocBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mutex;
@@ -687,7 +758,7 @@ extern "C" int vb200_mass_bias_attention_noalloc(int dtype, const void* q, const
   // The bias kernel rewrites every scratch entry the attention kernel reads (real keys and the
   // -inf padding of the last tile), so nothing carries over from a previous call.
   return vb200_mass_bias_attention(dtype, q, k, v, log_key_mass, bias_dtype, out, B, H, Nq, Nk, D, qs, ks,
-                                   vs, os, scratch, sizeof(float) * kNoAllocMaxKeys, stream);
+                                   vs, os, scratch, kNoAllocBytes, stream);
 }
 
 // ------------------------------------------------------------------------------------------

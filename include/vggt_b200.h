@@ -60,8 +60,9 @@ VB200_API int vb200_device_error_flags(unsigned* flags, int clear);
  *   runs an fp32 FMA path.  log_key_mass has `bias_dtype` and Nk entries; as in the
  *   reference it is rounded to `dtype` before use.
  * strides: {batch, head, token} for each of q, k, v, out; the channel stride is 1.
- * workspace: device scratch of vb200_mass_bias_attention_workspace_size(Nk) bytes (the
- *   padded log2-domain bias), 256-byte aligned. */
+ * workspace: device scratch of vb200_mass_bias_attention_workspace_size(Nk) bytes (4 KB per
+ *   128-key tile: the bias operand of the QK product, or the padded fp32 bias of the fp32
+ *   path), 256-byte aligned. */
 VB200_API size_t vb200_mass_bias_attention_workspace_size(int64_t Nk);
 VB200_API int vb200_mass_bias_attention(int dtype, const void* q, const void* k, const void* v,
                               const void* log_key_mass, int bias_dtype, void* out, int64_t B,
@@ -74,8 +75,9 @@ VB200_API int vb200_mass_bias_attention(int dtype, const void* q, const void* k,
  * memory: code that only holds raw device pointers handed over by another runtime (no
  * allocator to get a workspace from) and latency-critical loops that must not call
  * cudaMalloc / cudaFree, which synchronise the device.  It allocates nothing: its scratch (the
- * padded bias) is a fixed 1 MiB array inside the library, present on every GPU that loads it
- * until the process exits, so Nk is limited to 262,144 keys (larger Nk returns VB200_EINVAL).
+ * per-key-tile bias operand) is a fixed 4 MiB array inside the library, present on every GPU that
+ * loads it until the process exits, so Nk is limited to 131,072 keys (larger Nk returns
+ * VB200_EINVAL).
  * The first call on a device resolves that array's device address (cudaGetSymbolAddress) with
  * the device current; make that first call before any stream capture.  All calls share the
  * array: calls that may overlap on the GPU (different streams, or different host threads on one

@@ -70,8 +70,8 @@ def test_reference_exceptions_without_gpu(pkg):
 
 def test_host_side_size_checks(pkg):
     lib = pkg.load_library()
-    assert lib.vb200_mass_bias_attention_workspace_size(1) == 512
-    assert lib.vb200_mass_bias_attention_workspace_size(129) == 1024
+    assert lib.vb200_mass_bias_attention_workspace_size(1) == 4096
+    assert lib.vb200_mass_bias_attention_workspace_size(129) == 8192
     rc = lib.vb200_proj_gather(1, None, 0, None, 0, None, None, None, 0, 9, None, 0, 0, 8, 0, None)
     assert rc == pkg._clib.EINVAL and b"corners" in lib.vb200_last_error()
     rc = lib.vb200_sim_topk(None, 0, None, 0, 4, 4, 64, 3, None, None, 1, None, None, None)

@@ -18,7 +18,7 @@ from helpers import assert_close, to_np
 
 pytestmark = pytest.mark.gpu
 
-MAX_KEYS = 262144
+MAX_KEYS = 131072
 
 
 def _strides(t):
