@@ -7,7 +7,7 @@
 // probabilities rounded to the value dtype before the PV product, output divided by the
 // running sum and written in the input dtype.
 //
-// Kernel design: one CTA per 256 query rows (two 128-row tiles) and (batch, head), 10 warps,
+// Kernel design: one CTA per 256 query rows (two 128-row tiles) and (batch, head), 20 warps,
 // one CTA per SM; see mass_bias_attention_tc_kernel.  Shared-memory tiles use the 128-byte
 // swizzle written by TMA; the UMMA descriptors describe the same layout (K-major for Q and K,
 // MN-major for V).  No TMA multicast is used.
@@ -26,7 +26,7 @@ namespace {
 static __device__ unsigned g_attn_err;
 
 constexpr int kBM = 128;  // query rows per tile (one TMEM lane per row)
-constexpr int kQT = 2;    // query tiles per CTA, one softmax warpgroup each
+constexpr int kQT = 2;    // query tiles per CTA, two softmax warpgroups each
 constexpr int kBN = 128;  // keys per tile
 constexpr int kHD = 64;   // head dim
 constexpr int kStages = 4;
@@ -38,21 +38,26 @@ constexpr int kTileBytes = kBM * kHD * 2;  // 16 KB: one Q, K or V tile
 // no-swizzle K-major layout: [16 row groups][2 K halves][8 rows][16 bytes].
 constexpr int kKxBytes = 4096;
 constexpr int kStageStride = 36864;        // K, V (16 KB each) + extra K chunk (4 KB)
-constexpr int kThreads = 384;              // warpgroups: 0, 1 softmax; 2 = producer (warp 8) + MMA (warp 9)
+constexpr int kHalfKeys = kBN / 2;        // key columns per softmax warpgroup
+constexpr int kSoftmaxWarps = 16;         // four softmax warpgroups: 2 query tiles x 2 column halves
+constexpr int kWarpProducer = kSoftmaxWarps;
+constexpr int kWarpMma = kSoftmaxWarps + 1;
+constexpr int kThreads = (kSoftmaxWarps + 4) * 32;  // + one warpgroup for the producer and MMA warps
 // Register split (setmaxnreg): the block launches with kLaunchRegs per thread; the producer
-// warpgroup drops to kRegsLow and the two softmax warpgroups rise to kRegsHigh.  The shares
-// add up exactly to the launch total, which the host checks before every launch.
-constexpr int kLaunchRegs = 168;
-constexpr int kRegsHigh = 232;
-constexpr int kRegsLow = 40;
-static_assert(2 * 128 * kRegsHigh + 128 * kRegsLow == kThreads * kLaunchRegs, "register split");
+// warpgroup drops to kRegsLow and the softmax warpgroups rise to kRegsHigh.  The shares add up
+// exactly to the launch total, which the host checks before every launch.
+constexpr int kLaunchRegs = 96;
+constexpr int kRegsHigh = 104;
+constexpr int kRegsLow = 64;
+static_assert(kSoftmaxWarps * 32 * kRegsHigh + 128 * kRegsLow == kThreads * kLaunchRegs, "register split");
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // lazy rescale: P stays <= 2^8
 // Of every 8 exponent pairs, how many are computed on the FMA pipe (exp2_poly2) instead of
-// MUFU.  Measured: the softmax is issue-bound, not MUFU-bound, at head_dim 64, and the
-// polynomial costs ~5 instructions per value against 1, so all exponentials use MUFU.
-constexpr int kPolyPairs = 0;
-constexpr int kNamedBarTurn = 1;  // named barriers 1 and 2 (0 is __syncthreads)
+// MUFU (16 exponentials per clock per SM).  Measured on the config-2 attention: 2 of 8 is
+// fastest (0: 459 us, 1: 414 us, 2: 407 us, 3: 457 us); beyond that the extra instructions
+// take issue slots from the MMA warp.
+constexpr int kPolyPairs = 2;
+constexpr int kNamedBarPair = 1;  // named barriers 1, 2: the two warpgroups of query tile 0, 1
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 constexpr int kOffQ = 0;                                  // kQT tiles
@@ -67,7 +72,8 @@ constexpr int kBarPFull = kBarSFull + kQT;
 constexpr int kBarODone = kBarPFull + kQT;
 constexpr int kBarSFree = kBarODone + kQT;
 constexpr int kNumBars = kBarSFree + kQT;
-constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+constexpr int kOffRed = kOffBar + kNumBars * 8;  // [tile][half][parity][row] fp32 exchange slots
+constexpr int kOffTmemSlot = kOffRed + kQT * 2 * 2 * kBM * 4;
 constexpr int kSmemUsed = kOffTmemSlot + 16;
 constexpr int kSmemBytes = kSmemUsed + 1024;  // slack for aligning the dynamic base
 constexpr uint32_t kTmemCols = 512;           // S_t at 128t, P_t at 256 + 64t, O_t at 384 + 64t
@@ -83,22 +89,89 @@ struct AttnParams {
   float scale_log2;  // log2(e) / sqrt(64)
 };
 
+// MMA groups, each one asm block executed by the whole MMA warp: elect.sync once, then the
+// elected lane issues every MMA of the group and the commit(s).  The MMA warp shares its SM
+// sub-partition with four busy softmax warps and only gets a small share of the issue slots,
+// so the instruction count per MMA (not the tensor pipe) sets the pace: one descriptor add
+// and one tcgen05.mma per step keeps the stream close to the pipe rate (measured: 1.8x
+// faster than one helper call per MMA under full contention).
+//
+// S_t = Q_t K^T over head_dim 64 (four K=16 steps; both descriptors' start addresses advance by
+// 32 bytes = 2 units per step) + the bias chunk (xa, xb); the first step overwrites.
+__device__ __forceinline__ void issue_qk_group(uint32_t d, uint64_t a, uint64_t b, uint64_t xa, uint64_t xb,
+                                               uint32_t idesc, uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, 0, 0;\n\t"
+      "setp.eq.b32 pt, 0, 0;\n\t"
+      "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\t"
+      "add.s64 a2, %1, 4;\n\tadd.s64 b2, %2, 4;\n\t"
+      "add.s64 a3, %1, 6;\n\tadd.s64 b3, %2, 6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %5, pf;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %5, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %5, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %5, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %4, %5, pt;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "l"(xa), "l"(xb), "r"(idesc), "r"(bar)
+      : "memory");
+}
+// O_t (+)= P_t V over 128 keys: eight K=16 steps; P_t in TMEM (A advances 8 columns = 16
+// packed keys per step), V MN-major (B advances 2048 bytes = 128 units per step).  Commits to
+// `bar`, and also to `bar2` when use_bar2 is nonzero.
+__device__ __forceinline__ void issue_pv_group(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
+                                               uint32_t acc_first, uint32_t bar, uint32_t bar2,
+                                               uint32_t use_bar2) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt, p2;\n\t.reg .b64 b1, b2, b3, b4, b5, b6, b7;\n\t"
+      ".reg .b32 a1, a2, a3, a4, a5, a6, a7;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, %4, 0;\n\t"
+      "setp.eq.b32 pt, 0, 0;\n\t"
+      "setp.ne.and.b32 p2, %7, 0, e;\n\t"
+      "add.s32 a1, %1, 8;\n\tadd.s64 b1, %2, 128;\n\t"
+      "add.s32 a2, %1, 16;\n\tadd.s64 b2, %2, 256;\n\t"
+      "add.s32 a3, %1, 24;\n\tadd.s64 b3, %2, 384;\n\t"
+      "add.s32 a4, %1, 32;\n\tadd.s64 b4, %2, 512;\n\t"
+      "add.s32 a5, %1, 40;\n\tadd.s64 b5, %2, 640;\n\t"
+      "add.s32 a6, %1, 48;\n\tadd.s64 b6, %2, 768;\n\t"
+      "add.s32 a7, %1, 56;\n\tadd.s64 b7, %2, 896;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, pf;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], b4, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], b5, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], b6, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], b7, %3, pt;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t"
+      "@p2 tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc_first), "r"(bar), "r"(bar2), "r"(use_bar2)
+      : "memory");
+}
+
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 __device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
 
-// Mass-bias attention, two query tiles per CTA (FA4-style ping-pong):
-//   warps 0-3 / 4-7  softmax warpgroup of query tile 0 / 1: thread = query row = TMEM lane.
-//   warps 8-11       warp 8: TMA producer: both Q tiles once; K_j, V_j and the bias of key tile j
-//                    into a 4-stage ring.
-//                    warp 9: TMEM allocation; one lane issues all tcgen05.mma.  Per key
-//                    tile j it issues QK_0(j+1), QK_1(j+1) as soon as the softmax has read
-//                    S_t(j) into registers, then PV_0(j), PV_1(j) once P_t(j) is written, so
-//                    the next scores are computed underneath the current softmax.
+// Mass-bias attention, two query tiles per CTA:
+//   warps 0-15   four softmax warpgroups; warpgroup 2t+h owns query tile t (thread = query row =
+//                TMEM lane) and key columns [64h, 64h+64) of every S tile.  The two halves of a
+//                tile exchange their row maxima each key tile, so they share one running max
+//                and one O accumulator.  Four softmax warps per SM sub-partition keep the
+//                exponential unit busy while other warps load S, reduce maxima or store P.
+//   warp 16      TMA producer: both Q tiles once; K_j, V_j and the bias chunk of key tile j
+//                into a 4-stage ring.
+//   warp 17      TMEM allocation and the MMA stream (converged warp, one elected lane issues).
+//                Per key tile j it issues QK_0(j+1), QK_1(j+1) as soon as both halves have
+//                read S_t(j) into registers, then PV_0(j), PV_1(j) once P_t(j) is written, so
+//                the next scores are computed underneath the current softmax.
+//   warps 18-19  idle (they complete the warpgroup that setmaxnreg.dec applies to).
 // TMEM (512 columns): S_t in [128t, 128t+128), P_t as packed 16-bit values in
 // [256+64t, 256+64t+64) (the A operand of the TS-MMA), O_t accumulating in [384+64t, ...).
-// The running max is lazy: O_t is rescaled (in TMEM, by the softmax thread that owns the row)
-// only when a row's max grows by more than 2^8, otherwise P is formed against the stale max,
-// which the final division by the matching running sum cancels exactly.
+// The running max is lazy: O_t is rescaled (in TMEM, each half rescaling its 32 columns) only
+// when a row's max grows by more than 2^8; otherwise P is formed against the stale max, which
+// the final division by the matching running sum cancels exactly.
 template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
     mass_bias_attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -115,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int batch = bh / p.H;
   const int head = bh - batch * p.H;
   const int n_tiles = p.n_tiles;
-  auto bar = [&](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
+  auto bar = [=](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
 
   if (threadIdx.x == 0) {
@@ -126,9 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kQT; ++t) {
       mbar_init(bar(kBarSFull + t), 1);
-      mbar_init(bar(kBarPFull + t), 128);
+      mbar_init(bar(kBarPFull + t), 2 * 128);
       mbar_init(bar(kBarODone + t), 1);
-      mbar_init(bar(kBarSFree + t), 128);
+      mbar_init(bar(kBarSFree + t), 2 * 128);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -140,12 +213,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     *reinterpret_cast<uint4*>(smem + kOffQx + 16 * threadIdx.x) = make_uint4(half == 0 ? one : 0u, 0u, 0u, 0u);
     fence_proxy_async_smem();  // generic-proxy writes become visible to the tensor core
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == kWarpProducer && lane == 0) {
     prefetch_tmap(&tmap_q);
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_v);
   }
-  if (warp == 9) {
+  if (warp == kWarpMma) {
     tmem_alloc(sbase + kOffTmemSlot, kTmemCols);
     tmem_relinquish();
   }
@@ -156,9 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Each role's code is dominated by its own setmaxnreg (no merge point in between), so the
   // register allocator gives every branch the budget its warpgroup actually holds.
-  if (warp >= 8) {
+  if (warp >= kSoftmaxWarps) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
-  if (warp == 8) {
+  if (warp == kWarpProducer) {
     // ------------------------------- producer -------------------------------
     if (lane == 0) {
       bool ok = true;
@@ -181,158 +254,137 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp == 9) {
+  } else if (warp == kWarpMma) {
     // ------------------------------- MMA issuer -------------------------------
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, kBF16 ? 1 : 0, 0, 0);
-      constexpr uint32_t idesc_pv = idesc_f16(kBM, kHD, kBF16 ? 1 : 0, 0, 1);
-      bool ok = mbar_wait(bar(kBarQFull), 0, &g_attn_err);
-      // S_t = Q_t K_j^T
-      auto issue_qk = [&](int t, int j) {
-        const int s = j % kStages;
-        const uint32_t q_addr = sbase + kOffQ + t * kTileBytes;
-        const uint32_t k_addr = sbase + kOffStage + s * kStageStride;
-#pragma unroll
-        for (int kk = 0; kk < kHD / 16; ++kk) {
-          const uint64_t adesc = smem_desc_sw128(q_addr + kk * 32, 16, 1024);
-          const uint64_t bdesc = smem_desc_sw128(k_addr + kk * 32, 16, 1024);
-          umma_ss(tmem + t * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-        // + 1 * (8 bias_j): the extra K=16 chunk (no swizzle: LBO 128 B along K, SBO 256 B)
-        umma_ss(tmem + t * 128, smem_desc_noswz(sbase + kOffQx, 128, 256),
-                smem_desc_noswz(k_addr + 2 * kTileBytes, 128, 256), idesc_qk, 1u);
-        umma_commit(bar(kBarSFull + t));
-      };
-      // O_t += P_t V_j (P_t from TMEM, V MN-major from shared memory)
-      auto issue_pv = [&](int t, int j) -> bool {
-        const int s = j % kStages;
-        if (!mbar_wait(bar(kBarPFull + t), j & 1, &g_attn_err)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = sbase + kOffStage + s * kStageStride + kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          // V tile: key rows of 128 bytes; a K-step of 16 keys spans two 1024-byte atoms
-          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, 16384, 1024);
-          umma_ts(tmem + kTmemO + t * kHD, tmem + kTmemP + t * kHD + kk * 8, bdesc, idesc_pv,
-                  (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(bar(kBarODone + t));
-        if (t == kQT - 1) umma_commit(bar(kBarKVEmpty + s));
-        return true;
-      };
-      if (ok) ok = mbar_wait(bar(kBarKVFull + 0), 0, &g_attn_err);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < kQT; ++t) issue_qk(t, 0);
-      }
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        if (*abort_flag) { ok = false; break; }
-        if (j + 1 < n_tiles) {
-          const int s1 = (j + 1) % kStages;
-          if (!mbar_wait(bar(kBarKVFull + s1), ((j + 1) / kStages) & 1, &g_attn_err)) { ok = false; break; }
-          for (int t = 0; t < kQT && ok; ++t) {
-            // S_t(j) has been read into registers: overwrite it with the next tile's scores
-            if (!mbar_wait(bar(kBarSFree + t), j & 1, &g_attn_err)) { ok = false; break; }
+    // The whole warp runs this loop (every lane waits on the barriers) and one elected lane
+    // issues each tcgen05 operation.  Descriptors are built once for Q tile 0 / stage 0; the
+    // start-address field counts 16-byte units, so a byte offset b is added as b >> 4 (shared
+    // addresses stay below 256 KB, so the 14-bit field never carries).
+    constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, kBF16 ? 1 : 0, 0, 0);
+    constexpr uint32_t idesc_pv = idesc_f16(kBM, kHD, kBF16 ? 1 : 0, 0, 1);
+    const uint64_t q_desc = smem_desc_sw128(sbase + kOffQ, 16, 1024);
+    const uint64_t k_desc = smem_desc_sw128(sbase + kOffStage, 16, 1024);
+    // V is MN-major: key rows of 128 bytes, so a K-step of 16 keys spans two 1024-byte atoms
+    const uint64_t v_desc = smem_desc_sw128(sbase + kOffStage + kTileBytes, 16384, 1024);
+    // the bias chunk (no swizzle: LBO 128 B along K, SBO 256 B between 8-row groups)
+    const uint64_t qx_desc = smem_desc_noswz(sbase + kOffQx, 128, 256);
+    const uint64_t kx_desc = smem_desc_noswz(sbase + kOffStage + 2 * kTileBytes, 128, 256);
+    // S_t = Q_t K_j^T + 1 * (8 bias_j)
+    auto issue_qk = [=](int t, int j) {
+      const uint64_t so = static_cast<uint64_t>((j % kStages) * (kStageStride >> 4));
+      issue_qk_group(tmem + t * 128, q_desc + t * (kTileBytes >> 4), k_desc + so, qx_desc, kx_desc + so, idesc_qk,
+                     bar(kBarSFull + t));
+    };
+    // O_t += P_t V_j (P_t from TMEM); the last tile's group also frees the K/V stage
+    auto issue_pv = [=](int t, int j) {
+      const uint64_t so = static_cast<uint64_t>((j % kStages) * (kStageStride >> 4));
+      issue_pv_group(tmem + kTmemO + t * kHD, tmem + kTmemP + t * kHD, v_desc + so, idesc_pv, j > 0 ? 1u : 0u,
+                     bar(kBarODone + t), bar(kBarKVEmpty + j % kStages), t == kQT - 1 ? 1u : 0u);
+    };
+    auto wait_all = [&](int b, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, &g_attn_err));
+    };
+    bool ok = wait_all(kBarQFull, 0) && wait_all(kBarKVFull + 0, 0);
+    if (ok) {
+      tc_fence_after();
+      for (int t = 0; t < kQT; ++t) issue_qk(t, 0);
+    }
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      if (j + 1 < n_tiles) {
+        ok = wait_all(kBarKVFull + (j + 1) % kStages, ((j + 1) / kStages) & 1);
+        for (int t = 0; t < kQT && ok; ++t) {
+          // S_t(j) has been read into registers: overwrite it with the next tile's scores
+          ok = wait_all(kBarSFree + t, j & 1);
+          if (ok) {
             tc_fence_after();
             issue_qk(t, j + 1);
           }
-          if (!ok) break;
         }
-        for (int t = 0; t < kQT && ok; ++t) ok = issue_pv(t, j);
+        if (!ok) break;
       }
-      if (!ok) *abort_flag = 1;
+      for (int t = 0; t < kQT && ok; ++t) {
+        ok = wait_all(kBarPFull + t, j & 1);
+        if (ok) {
+          tc_fence_after();
+          issue_pv(t, j);
+        }
+      }
     }
+    if (!ok && lane == 0) *abort_flag = 1;
   }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------- softmax warpgroups -------------------------------
-    const int t = warp >> 2;    // query tile of this warpgroup
+    // Warpgroup g = 2t + h owns query tile t and key columns [64h, 64h + 64) of every S tile;
+    // its partner (same t, other h) owns the other 64 columns of the same rows.
+    const int g = warp >> 2;
+    const int t = g >> 1;
+    const int h = g & 1;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + t * 128;
-    const uint32_t p_addr = tmem + lane_off + kTmemP + t * kHD;
-    const uint32_t o_addr = tmem + lane_off + kTmemO + t * kHD;
+    const uint32_t s_addr = tmem + lane_off + t * 128 + h * kHalfKeys;
+    const uint32_t p_addr = tmem + lane_off + kTmemP + t * kHD + h * (kHalfKeys / 2);
+    const uint32_t o_addr = tmem + lane_off + kTmemO + t * kHD + h * (kHD / 2);
+    float* red_mine = reinterpret_cast<float*>(smem + kOffRed) + ((t * 2 + h) * 2) * kBM + row;
+    const float* red_other = reinterpret_cast<const float*>(smem + kOffRed) + ((t * 2 + (1 - h)) * 2) * kBM + row;
+    const int pair_bar = kNamedBarPair + t;
     const float scale = p.scale_log2;
     const uint64_t scale2 = pk2(scale, scale);
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
-    // The two warpgroups take turns for the exponential phase (named barriers kNamedBarTurn
-    // and kNamedBarTurn + 1): while one drives MUFU, the other stores P, loads its next S and
-    // reduces the row max.  Every iteration performs its hand-over even after a failed wait,
-    // so neither warpgroup can be left waiting on the other.
-    const int my_turn = kNamedBarTurn + t;
-    const int other_turn = kNamedBarTurn + (1 - t);
-    if (t == 1) named_bar_arrive(kNamedBarTurn, 256);  // warpgroup 0 goes first
 
     for (int j = 0; j < n_tiles; ++j) {
       ok = ok && !*abort_flag;
       if (ok) ok = mbar_wait(bar(kBarSFull + t), j & 1, &g_attn_err);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform before warp-collective TMEM access
-      uint32_t r[kBN];
-      float m_use = 0.f;
+      uint32_t r[kHalfKeys];
+      float mx = -INFINITY;
       if (ok) {
         tc_fence_after();
         tmem_ld32x32b_x32_nowait(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         tmem_ld32x32b_x32_nowait(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        tmem_ld32x32b_x32_nowait(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-        tmem_ld32x32b_x32_nowait(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
         tmem_wait_ld();
         reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[0]));
         reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[64]));
-        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&r[96]));
         tc_fence_before();
-        mbar_arrive(bar(kBarSFree + t));  // S_t(j) is in registers: QK_t(j+1) may overwrite it
-
+        mbar_arrive(bar(kBarSFree + t));  // this half of S_t(j) is in registers
         // S' = q.k + 8 bias; the log2-domain logit is S' * scale (scale = log2(e)/8 > 0), so
         // the row max is taken on S' directly (four 3-input max chains)
         float mxa = -INFINITY, mxb = -INFINITY, mxc = -INFINITY, mxd = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < kBN; i += 8) {
+        for (int i = 0; i < kHalfKeys; i += 8) {
           mxa = fmax3(mxa, u2f(r[i + 0]), u2f(r[i + 1]));
           mxb = fmax3(mxb, u2f(r[i + 2]), u2f(r[i + 3]));
           mxc = fmax3(mxc, u2f(r[i + 4]), u2f(r[i + 5]));
           mxd = fmax3(mxd, u2f(r[i + 6]), u2f(r[i + 7]));
         }
-        const float m_new = fmaxf(m_run, fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd)) * scale);
-        const bool need = m_new > m_run + kRescaleThreshold;  // always true on the first tile
-        if (j > 0) {
-          // PV_t(j-1) must be complete before P_t is overwritten or O_t is rescaled
-          ok = mbar_wait(bar(kBarODone + t), (j - 1) & 1, &g_attn_err);
-          ok = __all_sync(0xffffffffu, ok);
-          if (ok) tc_fence_after();
-        }
-        if (ok && __any_sync(0xffffffffu, need)) {
-          const float m_tgt = need ? m_new : m_run;
-          const float alpha = ex2_approx(m_run - m_tgt);  // 0 on the first tile, 1 if unchanged
-          if (j > 0) {
-#pragma unroll
-            for (int h = 0; h < kHD; h += 32) {  // two halves keep the register peak low
-              uint32_t o[32];
-              tmem_ld32x32b_x32_nowait(o_addr + h, o);
-              tmem_wait_ld();
-              reg_fence32(o);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = f2u(u2f(o[i]) * alpha);
-              tmem_st32x32b_x32(o_addr + h, o);
-            }
-          }
-          l_run *= alpha;
-          m_run = m_tgt;
-        }
-        m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
       }
-
-      named_bar_sync(my_turn, 256);  // this warpgroup's turn on MUFU
+      // Exchange the half-row maxima with the partner warpgroup.  Both halves then see the
+      // same tile max and make the same rescale decision, so they share one running max and
+      // one O accumulator.  The barrier runs every iteration, also after a failed wait, so
+      // the partner can never be left waiting; slots alternate with j so a slot is rewritten
+      // only after the partner has passed the next barrier.
+      red_mine[(j & 1) * kBM] = mx;
+      named_bar_sync(pair_bar, 256);
+      mx = fmaxf(mx, red_other[(j & 1) * kBM]);
       if (ok) {
-        // P = 2^(S' * scale - m), packed in place: r[i] <- (p[2i], p[2i+1]).  kPolyPairs of
-        // every 8 pairs may use the FMA-pipe exponential instead of MUFU.
+        // Lazy running max: move it (and rescale O_t, l) only when the row max grows by more
+        // than kRescaleThreshold, so P = 2^(S' * scale - m) stays <= 2^kRescaleThreshold.
+        const float m_new = fmaxf(m_run, mx * scale);
+        const bool need = __any_sync(0xffffffffu, m_new > m_run + kRescaleThreshold);  // true on the first tile
+        const float m_tgt = (m_new > m_run + kRescaleThreshold) ? m_new : m_run;
+        const float alpha = ex2_approx(m_run - m_tgt);  // 0 on the first tile, 1 if unchanged
+        const float m_use = (m_tgt == -INFINITY) ? 0.f : m_tgt;
+        // P packed in place: r[i] <- (p[2i], p[2i+1]).  kPolyPairs of every 8 pairs use the
+        // FMA-pipe exponential instead of MUFU.
         const uint64_t neg_m2 = pk2(-m_use, -m_use);
         uint64_t ls0 = pk2(0.f, 0.f), ls1 = pk2(0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < kBN / 2; ++i) {
+        for (int i = 0; i < kHalfKeys / 2; ++i) {
           float e0, e1, p0, p1;
           upk2(ffma2(pk2(u2f(r[2 * i]), u2f(r[2 * i + 1])), scale2, neg_m2), e0, e1);
           if ((i & 7) < kPolyPairs) {
@@ -348,38 +400,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         float a0, a1, b0, b1;
         upk2(ls0, a0, a1);
         upk2(ls1, b0, b1);
-        l_run += (a0 + a1) + (b0 + b1);
-      }
-      named_bar_arrive(other_turn, 256);  // hand MUFU to the other warpgroup
-      if (ok) {
-        tmem_st32x32b_x32(p_addr + 0, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
-        tmem_st32x32b_x32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar(kBarPFull + t));
+        l_run = l_run * alpha + ((a0 + a1) + (b0 + b1));
+        m_run = m_tgt;
+        if (j > 0) {
+          // PV_t(j-1) must be complete before P_t is overwritten or O_t is rescaled
+          ok = mbar_wait(bar(kBarODone + t), (j - 1) & 1, &g_attn_err);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) tc_fence_after();
+          if (ok && need) {
+#pragma unroll
+            for (int c = 0; c < kHD / 2; c += 16) {  // this warpgroup's 32 columns of O_t
+              uint32_t o[16];
+              tmem_ld32x32b_x16(o_addr + c, o);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = f2u(u2f(o[i]) * alpha);
+              tmem_st32x32b_x16(o_addr + c, o);
+            }
+          }
+        }
+        if (ok) {
+          tmem_st32x32b_x32(p_addr, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(kBarPFull + t));
+        }
       }
     }
-    if (t == 0) named_bar_sync(kNamedBarTurn, 256);  // consume warpgroup 1's last hand-over
 
+    // Both halves' running sums share one scale: O_t / (l_half0 + l_half1).
+    red_mine[(n_tiles & 1) * kBM] = l_run;
+    named_bar_sync(pair_bar, 256);
+    const float l_tot = l_run + red_other[(n_tiles & 1) * kBM];
     if (ok) {
       ok = mbar_wait(bar(kBarODone + t), (n_tiles - 1) & 1, &g_attn_err);
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
       tc_fence_after();
-      uint32_t o[kHD];
-      tmem_ld32x32b_x32_nowait(o_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-      tmem_ld32x32b_x32_nowait(o_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      uint32_t o[kHD / 2];
+      tmem_ld32x32b_x32_nowait(o_addr, o);
       tmem_wait_ld();
-      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-      reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      reg_fence32(o);
       const int grow = (q_block * kQT + t) * kBM + row;
       if (grow < p.Nq) {
-        const float inv = 1.f / l_run;
+        const float inv = 1.f / l_tot;
         uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
-                        2 * (batch * p.o_sb + head * p.o_sh + static_cast<long long>(grow) * p.o_sn);
+                        2 * (batch * p.o_sb + head * p.o_sh + static_cast<long long>(grow) * p.o_sn + h * (kHD / 2));
 #pragma unroll
-        for (int c = 0; c < kHD / 8; ++c) {
+        for (int c = 0; c < kHD / 16; ++c) {
           uint4 w;
           uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
@@ -395,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
