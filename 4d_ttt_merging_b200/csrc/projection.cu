@@ -454,6 +454,211 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
   store_vec<T>(out + j * os + t * C + col, acc);
 }
 
+// Staged compaction for C <= 1024: the same result as compact_qkv_kernel, with the source rows
+// fetched by the bulk-copy engine instead of per-thread loads.
+//   warps 0 .. 3C/256-1   consumers: thread i owns channels [8i, 8i + 8) of the q|k|v row
+//   last warp             producer: for every item (the keep row, then the CSR entries of the
+//                         merged row) one cp.async.bulk of the whole 3C-channel source row and
+//                         one of its 2H LayerNorm statistics into a ring of shared-memory slots.
+// CTAs take merged rows j = blockIdx.x, blockIdx.x + gridDim.x, ..., so at any time the GPU works
+// on neighbouring merged rows, whose sources overlap and stay in L2.  Per item a consumer thread
+// reads 16 bytes and one float2 of statistics from shared memory and does 4 packed FMAs; the
+// copy engine keeps up to kStageSlots rows in flight per CTA without holding registers.
+constexpr int kStageSlots = 16;
+constexpr int kIssueLanes = 4;  // producer lanes that issue copies together
+constexpr int kStageHeaderBytes = 512;
+
+// Two 16-bit values of one 32-bit word as an fp32 pair (low half first).  bf16 -> fp32 is a
+// shift of the bit pattern.
+template <typename T>
+__device__ __forceinline__ uint64_t unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ uint64_t unpack2<__nv_bfloat16>(uint32_t w) {
+  return pk2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ uint64_t unpack2<__half>(uint32_t w) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return pk2(f.x, f.y);
+}
+struct StageSlotMeta {
+  int src;
+  float w;
+};
+static_assert(2 * kStageSlots * 8 + kStageSlots * sizeof(StageSlotMeta) <= kStageHeaderBytes, "stage header");
+
+template <typename T>
+__global__ void __launch_bounds__(416, 2)
+    compact_qkv_staged_kernel(const T* __restrict__ qkv, long long rows, long long xs, int C,
+                              const float* __restrict__ ln_w, const float* __restrict__ ln_b,
+                              const float2* __restrict__ stats, const int64_t* __restrict__ keep, long long M,
+                              int corners, const int32_t* __restrict__ seg_offsets,
+                              const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
+                              const float* __restrict__ normalizer, int pool_mask, T* __restrict__ out,
+                              long long os) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int n_cons = 3 * C / 8;  // consumer threads, a whole number of warps (C % 256 == 0)
+  const int heads2 = 2 * C / 64;
+  const uint32_t row_bytes = static_cast<uint32_t>(3 * C * sizeof(T));
+  const uint32_t stat_bytes = ln_w != nullptr ? static_cast<uint32_t>(heads2 * sizeof(float2)) : 0u;
+  const uint32_t slot_bytes = row_bytes + stat_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kStageSlots;
+  StageSlotMeta* meta = reinterpret_cast<StageSlotMeta*>(empty + kStageSlots);
+  uint8_t* data = smem + kStageHeaderBytes;  // after the barriers (256 B) and slot metadata (128 B)
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cons_warps = n_cons / 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStageSlots; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), cons_warps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const bool pooled_any = pool_mask != 0;
+
+  if (warp == cons_warps) {
+    // ------------------------------- producer -------------------------------
+    // The whole warp walks the item stream; lane u holds entry u of the current merged row
+    // (loaded together, one row ahead of use), and lane 0 issues each item's copies as soon as
+    // its slot is free, taking (source, weight) from the owning lane by shuffle.
+    long long item = 0;
+    bool ok = true;
+    auto load_row = [&](long long jr, int& e0, int& e1, long long& kr, int& src, float& w) {
+      e0 = pooled_any ? seg_offsets[jr * corners] : 0;
+      e1 = pooled_any ? seg_offsets[(jr + 1) * corners] : 0;
+      kr = keep[jr];
+      src = 0;
+      w = 0.f;
+      if (e0 + lane < e1) {
+        src = entry_src[e0 + lane];
+        w = entry_w[e0 + lane];
+      }
+    };
+    int e0 = 0, e1 = 0, src = 0;
+    long long kr = 0;
+    float w = 0.f;
+    if (blockIdx.x < M) load_row(blockIdx.x, e0, e1, kr, src, w);
+    for (long long j = blockIdx.x; j < M && ok; j += gridDim.x) {
+      int ne0 = 0, ne1 = 0, nsrc = 0;
+      long long nkr = 0;
+      float nw = 0.f;
+      if (j + gridDim.x < M) load_row(j + gridDim.x, ne0, ne1, nkr, nsrc, nw);  // next row, ahead of use
+      const int n_items = e1 - e0 + 1;  // the keep row, then the entries
+      for (int u0 = 0; u0 < n_items && ok; u0 += kIssueLanes) {
+        // lanes 0..kIssueLanes-1 take items u0 + lane: a batch waits only for the oldest
+        // kIssueLanes slots, so the ring stays at least kStageSlots - kIssueLanes deep
+        const int u = u0 + lane;
+        long long s = __shfl_sync(0xffffffffu, src, (u - 1) & 31);
+        float wi = __shfl_sync(0xffffffffu, w, (u - 1) & 31);
+        const bool mine = lane < kIssueLanes && u < n_items;
+        bool wok = true;
+        if (mine) {
+          if (u == 0) {
+            s = kr;
+            wi = 1.f;
+          } else if (u > 32) {  // rows with more than 32 entries: read the rest directly
+            s = entry_src[e0 + u - 1];
+            wi = entry_w[e0 + u - 1];
+          }
+          if (s < 0 || s >= rows) {
+            atomicOr(&g_proj_err, kErrBadArgument);
+            s = 0;
+            wi = 0.f;
+          }
+          const long long it = item + u;
+          if (it >= kStageSlots)
+            wok = mbar_wait(smem_u32(&empty[it % kStageSlots]), static_cast<uint32_t>((it / kStageSlots) - 1) & 1u,
+                            &g_proj_err);
+        }
+        ok = __all_sync(0xffffffffu, wok);
+        if (ok && mine) {
+          const int slot = static_cast<int>((item + u) % kStageSlots);
+          meta[slot].src = static_cast<int>(s);
+          meta[slot].w = wi;
+          const uint32_t dst = smem_u32(data + static_cast<size_t>(slot) * slot_bytes);
+          const uint32_t bar = smem_u32(&full[slot]);
+          mbar_arrive_expect_tx(bar, slot_bytes);
+          bulk_load(dst, qkv + s * xs, row_bytes, bar);
+          if (stat_bytes) bulk_load(dst + row_bytes, stats + s * heads2, stat_bytes, bar);
+        }
+      }
+      item += n_items;
+      e0 = ne0;
+      e1 = ne1;
+      kr = nkr;
+      src = nsrc;
+      w = nw;
+    }
+    return;  // no block-wide barrier follows
+  }
+
+  // ------------------------------- consumers -------------------------------
+  // Thread i owns channels [8i, 8i + 8) of the q|k|v row (one tensor, one LayerNorm head).
+  // Each item is released as soon as the warp has read it; each 16-bit pair becomes an fp32 pair
+  // for one packed FMA.
+  const int i = threadIdx.x;
+  const int t = i / (C / 8);             // tensor: 0 q, 1 k, 2 v
+  const int col = (i - t * (C / 8)) * 8;  // channel within the tensor
+  const bool ln = ln_w != nullptr && t < 2;
+  const bool pooled_t = (pool_mask >> t) & 1;
+  const int stat_idx = t * (C / 64) + col / 64;
+  long long item = 0;
+  bool ok = true;
+  for (long long j = blockIdx.x; j < M && ok; j += gridDim.x) {
+    const int e0 = pooled_any ? seg_offsets[j * corners] : 0;
+    const int e1 = pooled_any ? seg_offsets[(j + 1) * corners] : 0;
+    const int n_items = e1 - e0 + 1;
+    uint64_t acc2[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc2[q] = 0ull;  // (+0.0f, +0.0f)
+    float csum = 0.f, wsum = 0.f;
+    for (int u = 0; u < n_items; ++u) {
+      const long long it = item + u;
+      const int slot = static_cast<int>(it % kStageSlots);
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(smem_u32(&full[slot]), static_cast<uint32_t>(it / kStageSlots) & 1u, &g_proj_err));
+      if (!ok) break;
+      if (u == 0 || pooled_t) {  // item 0 is the keep row
+        const uint8_t* base = data + static_cast<size_t>(slot) * slot_bytes;
+        float a = meta[slot].w;
+        wsum += a;
+        if (ln) {
+          const float2 st = reinterpret_cast<const float2*>(base + row_bytes)[stat_idx];
+          a *= st.y;  // w r
+          csum = fmaf(a, st.x, csum);
+        }
+        const uint4 r0 = *reinterpret_cast<const uint4*>(base + static_cast<size_t>(i) * 16);
+        const uint64_t a2 = pk2(a, a);
+        acc2[0] = ffma2(a2, unpack2<T>(r0.x), acc2[0]);
+        acc2[1] = ffma2(a2, unpack2<T>(r0.y), acc2[1]);
+        acc2[2] = ffma2(a2, unpack2<T>(r0.z), acc2[2]);
+        acc2[3] = ffma2(a2, unpack2<T>(r0.w), acc2[3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
+    }
+    item += n_items;
+    if (!ok) break;
+    float acc[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) upk2(acc2[q], acc[2 * q], acc[2 * q + 1]);
+    if (ln) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        acc[q] = fmaf(__ldg(ln_w + t * 64 + col % 64 + q), acc[q] - csum, __ldg(ln_b + t * 64 + col % 64 + q) * wsum);
+    }
+    if (pooled_t) {
+      const float norm = normalizer[j];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[q] = __fdiv_rn(acc[q], norm);
+    }
+    store_vec<T>(out + j * os + t * C + col, acc);
+  }
+}
+
 // Per-head LayerNorm of the q block of qkv rows (query-preserving plans keep every query).
 template <typename T>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
@@ -854,6 +1059,31 @@ extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64
     else VB200_STATS(__half);
 #undef VB200_STATS
     VB200_CHECK_LAUNCH("head_stats_kernel");
+  }
+  if (C <= 1024) {
+    // staged path: one producer warp + 3C/256 consumer warps per CTA, two CTAs per SM
+    const int threads = static_cast<int>(3 * C / 8) + 32;
+    const size_t smem = kStageHeaderBytes +
+                        static_cast<size_t>(kStageSlots) * (3 * C * 2 + (ln_weight ? 2 * C / 64 * sizeof(float2) : 0));
+    int dev = 0, sms = 0;
+    VB200_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    VB200_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+    const unsigned grid = static_cast<unsigned>(M < 2ll * sms ? M : 2ll * sms);
+#define VB200_CQKV_STAGED(T)                                                                                     \
+  VB200_CHECK_CUDA(cudaFuncSetAttribute(compact_qkv_staged_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                        static_cast<int>(smem)),                                                 \
+                   "cudaFuncSetAttribute");                                                                      \
+  compact_qkv_staged_kernel<T><<<grid, threads, smem, st>>>(                                                     \
+      static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, stats, keep, M,             \
+      static_cast<int>(corners), seg_offsets, entry_src, entry_w, normalizer, pool_mask, static_cast<T*>(out), os)
+    if (dtype == VB200_BF16) {
+      VB200_CQKV_STAGED(__nv_bfloat16);
+    } else {
+      VB200_CQKV_STAGED(__half);
+    }
+#undef VB200_CQKV_STAGED
+    VB200_CHECK_LAUNCH("compact_qkv_staged_kernel");
+    return VB200_OK;
   }
 #define VB200_CQKV(T)                                                                                     \
   compact_qkv_kernel<T><<<row_blocks(M * 3 * (C / 256)), kWarpsPerBlock * 32, 0, st>>>(                   \
