@@ -98,79 +98,95 @@ AssignWorkspace assign_layout(int64_t S, int64_t total) {
 }
 
 // One warp per source: the 4x4 Gram of its supports and the 4 support-source products,
-// accumulated in fp32 over the channels (lane-strided, then a fixed butterfly), and with
-// steps > 0 the projected-gradient solve by lane 0.
+// accumulated in fp32 over the channels (lane-strided, then a fixed butterfly).  With steps > 0
+// the block's kFitWarps systems go through shared memory to warp 0, whose lanes run the
+// projected-gradient solves side by side (one source per lane) instead of one lane per warp.
+constexpr int kFitWarps = 16;
 template <typename T>
-__global__ void support_fit_kernel(const T* __restrict__ feat, long long rows, long long fs,
+__global__ void __launch_bounds__(kFitWarps * 32)
+    support_fit_kernel(const T* __restrict__ feat, long long rows, long long fs,
                                    const int64_t* __restrict__ src_rows,
                                    const int64_t* __restrict__ parent_rows, long long S, int D,
                                    float* __restrict__ gram, float* __restrict__ rhs,
                                    float* __restrict__ alpha, int steps) {
   constexpr int V = 16 / sizeof(T);
-  const long long s = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  __shared__ float sys[kFitWarps][20];  // G (16) and rhs (4) of each warp's source
+  const int warp = threadIdx.x >> 5;
+  const long long s = static_cast<long long>(blockIdx.x) * kFitWarps + warp;
   const int lane = threadIdx.x & 31;
-  if (s >= S) return;
-  long long r[5];
-  r[0] = src_rows ? src_rows[s] : s;
+  if (s < S) {
+    long long r[5];
+    r[0] = src_rows ? src_rows[s] : s;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) r[c + 1] = parent_rows[s * 4 + c];
-  bool bad = false;
-#pragma unroll
-  for (int c = 0; c < 5; ++c) {
-    if (r[c] < 0 || r[c] >= rows) { bad = true; r[c] = 0; }
-  }
-  if (bad && lane == 0) atomicOr(&g_plan_err, kErrBadArgument);
-  // products: g[i][j] for i <= j (10) + rhs[i] (4)
-  float acc[14];
-#pragma unroll
-  for (int i = 0; i < 14; ++i) acc[i] = 0.f;
-  for (int v0 = lane * V; v0 < D; v0 += 32 * V) {
-    float x[5][V];
+    for (int c = 0; c < 4; ++c) r[c + 1] = parent_rows[s * 4 + c];
+    bool bad = false;
 #pragma unroll
     for (int c = 0; c < 5; ++c) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(feat + r[c] * fs + v0));
-      const T* e = reinterpret_cast<const T*>(&raw);
+      if (r[c] < 0 || r[c] >= rows) { bad = true; r[c] = 0; }
+    }
+    if (bad && lane == 0) atomicOr(&g_plan_err, kErrBadArgument);
+    // products: g[i][j] for i <= j (10) + rhs[i] (4)
+    float acc[14];
 #pragma unroll
-      for (int q = 0; q < V; ++q) x[c][q] = to_f32<T>(e[q]);
+    for (int i = 0; i < 14; ++i) acc[i] = 0.f;
+    for (int v0 = lane * V; v0 < D; v0 += 32 * V) {
+      float x[5][V];
+#pragma unroll
+      for (int c = 0; c < 5; ++c) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(feat + r[c] * fs + v0));
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int q = 0; q < V; ++q) x[c][q] = to_f32<T>(e[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < V; ++q) {
+        int idx = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = i; j < 4; ++j) {
+            acc[idx] = fmaf(x[i + 1][q], x[j + 1][q], acc[idx]);
+            ++idx;
+          }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[10 + i] = fmaf(x[i + 1][q], x[0][q], acc[10 + i]);
+      }
     }
 #pragma unroll
-    for (int q = 0; q < V; ++q) {
+    for (int i = 0; i < 14; ++i)
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
+    if (lane == 0) {
       int idx = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = i; j < 4; ++j) {
-          acc[idx] = fmaf(x[i + 1][q], x[j + 1][q], acc[idx]);
+          sys[warp][i * 4 + j] = acc[idx];
+          sys[warp][j * 4 + i] = acc[idx];
           ++idx;
         }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[10 + i] = fmaf(x[i + 1][q], x[0][q], acc[10 + i]);
+      for (int i = 0; i < 4; ++i) sys[warp][16 + i] = acc[10 + i];
+      if (gram) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) gram[s * 16 + i] = sys[warp][i];
+      }
+      if (rhs) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) rhs[s * 4 + i] = acc[10 + i];
+      }
     }
-  }
-#pragma unroll
-  for (int i = 0; i < 14; ++i)
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
-  if (lane != 0) return;
-  float G[16], R4[4];
-  {
-    int idx = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = i; j < 4; ++j) { G[i * 4 + j] = acc[idx]; G[j * 4 + i] = acc[idx]; ++idx; }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) R4[i] = acc[10 + i];
-  }
-  if (gram) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) gram[s * 16 + i] = G[i];
-  }
-  if (rhs) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) rhs[s * 4 + i] = R4[i];
-  }
+  }  // s < S
   if (alpha == nullptr) return;
+  __syncthreads();
+  const long long sl = static_cast<long long>(blockIdx.x) * kFitWarps + lane;  // warp 0, lane = source
+  if (warp != 0 || lane >= kFitWarps || sl >= S) return;
+  float G[16], R4[4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) G[i] = sys[lane][i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) R4[i] = sys[lane][16 + i];
   // projected gradient on the simplex (same iteration as the standalone solver)
   const float n0 = fabsf(G[0]) + fabsf(G[1]) + fabsf(G[2]) + fabsf(G[3]);
   const float n1 = fabsf(G[4]) + fabsf(G[5]) + fabsf(G[6]) + fabsf(G[7]);
@@ -199,10 +215,10 @@ __global__ void support_fit_kernel(const T* __restrict__ feat, long long rows, l
     a2 = fmaxf(p2 - theta, 0.f);
     a3 = fmaxf(p3 - theta, 0.f);
   }
-  alpha[s * 4 + 0] = a0;
-  alpha[s * 4 + 1] = a1;
-  alpha[s * 4 + 2] = a2;
-  alpha[s * 4 + 3] = a3;
+  alpha[sl * 4 + 0] = a0;
+  alpha[sl * 4 + 1] = a1;
+  alpha[sl * 4 + 2] = a2;
+  alpha[sl * 4 + 3] = a3;
 }
 
 inline unsigned blocks(long long n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
@@ -290,7 +306,7 @@ extern "C" int vb200_support_fit(int dtype, const void* feat, int64_t rows, int6
                 "support_fit: rows must be 16-byte aligned and D a multiple of %d", 16 / es);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define VB200_FIT(T)                                                                                \
-  support_fit_kernel<T><<<blocks(S, 8), 256, 0, st>>>(static_cast<const T*>(feat), rows, row_stride, \
+  support_fit_kernel<T><<<blocks(S, kFitWarps), kFitWarps * 32, 0, st>>>(static_cast<const T*>(feat), rows, row_stride, \
                                                        src_rows, parent_rows, S, static_cast<int>(D),  \
                                                        gram, rhs, alpha, steps)
   if (dtype == VB200_F32) VB200_FIT(float);
