@@ -9,12 +9,15 @@
 // rounds the accumulator to bf16 before ranking, :51-54), without writing the score matrix.
 //
 // Kernel (one CTA per 128 query rows of one group, 6 warps):
-//   warp 0      TMA producer: for every basis tile of 256 rows and every 64-channel k-block,
-//               the query k-block [128 x 64] and the basis k-block [256 x 64] (128-byte
-//               swizzle), 4-stage ring.
-//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32 accumulators) and issues
-//               tcgen05.mma M=128 N=256 K=16, committing each finished tile to the epilogue.
-//   warps 2..5  epilogue: thread t owns query row t, reads its 256 scores per tile from TMEM,
+//   warp 0      TMA producer: for every basis tile of tile_n rows and every 64-channel
+//               k-block, the query k-block [128 x 64] and the basis k-block [tile_n x 64]
+//               (128-byte swizzle), 4-stage ring.  tile_n (<= 256, a multiple of 16) is chosen
+//               per launch so the tiles cover the largest basis group with little padding
+//               (1029 rows: 5 x 208 instead of 5 x 256).
+//   warp 1      allocates 512 TMEM columns (two 128 x tile_n fp32 accumulators, 256 apart) and
+//               issues tcgen05.mma M=128 N=tile_n K=16 as a converged warp (one asm block per
+//               k-block), committing each finished tile to the epilogue.
+//   warps 2..5  epilogue: thread t owns query row t, reads its tile_n scores per tile from TMEM,
 //               rounds each to bf16 and keeps a running top-k in registers; the accumulator
 //               buffer is handed back as soon as it has been read, so tile t+1's MMAs overlap
 //               tile t's ranking.
@@ -33,7 +36,7 @@ namespace {
 static __device__ unsigned g_merge_err;
 
 constexpr int kBM = 128;
-constexpr int kBN = 256;
+constexpr int kBN = 256;  // largest basis tile (rows); the launch picks tile_n <= kBN
 constexpr int kBK = 64;  // channels per k-block (128 bytes of bf16: one swizzle row)
 constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KB
@@ -63,7 +66,29 @@ struct TopkParams {
   int64_t* indices;     // [R, k]
   int k;
   int k_blocks;         // D / 64
+  int tile_n;           // basis rows per tile (multiple of 16, <= kBN)
 };
+
+// One k-block (K = 64) of the score tile: four K=16 steps, both descriptors advancing 32 bytes
+// (2 units) per step, issued by one elected lane of the converged warp, then a commit.
+__device__ __forceinline__ void issue_kblock(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                             uint32_t acc_first, uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e, pf, pt;\n\t.reg .b64 a1, a2, a3, b1, b2, b3;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 pf, %4, 0;\n\t"
+      "setp.eq.b32 pt, 0, 0;\n\t"
+      "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\t"
+      "add.s64 a2, %1, 4;\n\tadd.s64 b2, %2, 4;\n\t"
+      "add.s64 a3, %1, 6;\n\tadd.s64 b3, %2, 6;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pf;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, pt;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc_first), "r"(bar)
+      : "memory");
+}
 
 __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
@@ -92,7 +117,33 @@ __device__ __forceinline__ void topk_insert(float (&tv)[4], int (&ti)[4], float 
   }
 }
 
-template <int K>
+// Branch-free top-4: an order-preserving 32-bit key per (score, column).  High half: the score's
+// bf16 bit pattern mapped so that unsigned order is numeric order (sign bit set for positive
+// values, all bits flipped for negative ones; -0 is folded to +0 first so equal scores compare
+// equal).  Low half: 65535 - column (group-local).  A larger key is a higher score or, on equal
+// scores, the lower column, which is the order of the strict-> running top-k; inserting is
+// then a 4-level max/min cascade with no divergent branches.  Key 0 marks an empty slot.
+// (A NaN score ranks above +inf here.)
+__device__ __forceinline__ uint32_t score_key(float s, int col) {
+  const float z = s + 0.0f;  // -0 -> +0
+  const uint32_t b = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(z))) << 16;
+  const uint32_t o = b ^ (static_cast<uint32_t>(static_cast<int32_t>(b) >> 31) | 0x80000000u);
+  return (o & 0xFFFF0000u) | static_cast<uint32_t>(0xFFFF - col);
+}
+__device__ __forceinline__ float key_score(uint32_t k) {
+  const uint32_t o = k & 0xFFFF0000u;
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7FFFFFFFu) : (~o & 0xFFFF0000u));
+}
+__device__ __forceinline__ void key_insert(uint32_t (&kk)[4], uint32_t key) {
+  uint32_t m;
+  m = max(kk[0], key); key = min(kk[0], key); kk[0] = m;
+  m = max(kk[1], key); key = min(kk[1], key); kk[1] = m;
+  m = max(kk[2], key); key = min(kk[2], key); kk[2] = m;
+  kk[3] = max(kk[3], key);
+}
+
+// kKeys: top-4 through score_key (every basis group has at most 65536 rows).
+template <int K, bool kKeys>
 __global__ void __launch_bounds__(kThreads, 1)
     sim_topk_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ GroupTable groups, TopkParams p) {
@@ -107,8 +158,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long b0 = groups.b_begin[g], b1 = groups.b_begin[g + 1];
   const long long row0 = q0 + static_cast<long long>(blockIdx.x) * kBM;
   if (row0 >= q1) return;  // uniform across the CTA, before any barrier or TMEM use
-  const int n_tiles = static_cast<int>((b1 - b0 + kBN - 1) / kBN);
+  const int tile_n = p.tile_n;
+  const int n_tiles = static_cast<int>((b1 - b0 + tile_n - 1) / tile_n);
   const int kb = p.k_blocks;
+  const uint32_t b_bytes = static_cast<uint32_t>(tile_n) * kBK * 2;
   auto bar = [&](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
 
@@ -149,43 +202,38 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t st = sbase + kOffStage + s * kStageBytes;
-          mbar_arrive_expect_tx(bar(kBarFull + s), kStageBytes);
+          mbar_arrive_expect_tx(bar(kBarFull + s), kABytes + b_bytes);
           tma_load_2d(st, &tmap_q, bar(kBarFull + s), k * kBK, static_cast<int32_t>(row0));
           tma_load_2d(st + kABytes, &tmap_b, bar(kBarFull + s), k * kBK,
-                      static_cast<int32_t>(b0 + static_cast<long long>(t) * kBN));
+                      static_cast<int32_t>(b0 + static_cast<long long>(t) * tile_n));
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_tiles > 0) {
-      constexpr uint32_t idesc = idesc_f16(kBM, kBN, 1, 0, 0);
+    if (n_tiles > 0) {
+      const uint32_t idesc = idesc_f16(kBM, tile_n, 1, 0, 0);
+      const uint64_t a_desc = smem_desc_sw128(sbase + kOffStage, 16, 1024);
+      const uint64_t b_desc = smem_desc_sw128(sbase + kOffStage + kABytes, 16, 1024);
       int it = 0;
       bool ok = true;
       for (int t = 0; t < n_tiles && ok; ++t) {
         const int ab = t & 1;
-        if (t >= 2 && !mbar_wait(bar(kBarAccEmpty + ab), ((t - 2) >> 1) & 1, &g_merge_err)) {
-          ok = false;
-          break;
-        }
+        if (t >= 2) ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarAccEmpty + ab), ((t - 2) >> 1) & 1, &g_merge_err));
+        if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem + ab * kBN;
         for (int k = 0; k < kb; ++k, ++it) {
           const int s = it % kStages;
-          if (!mbar_wait(bar(kBarFull + s), (it / kStages) & 1, &g_merge_err)) { ok = false; break; }
+          ok = __all_sync(0xffffffffu, mbar_wait(bar(kBarFull + s), (it / kStages) & 1, &g_merge_err));
+          if (!ok) break;
           tc_fence_after();
-          const uint32_t st = sbase + kOffStage + s * kStageBytes;
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t adesc = smem_desc_sw128(st + kk * 32, 16, 1024);
-            const uint64_t bdesc = smem_desc_sw128(st + kABytes + kk * 32, 16, 1024);
-            umma_ss(d_tmem, adesc, bdesc, idesc, (k > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(bar(kBarEmpty + s));
+          const uint64_t so = static_cast<uint64_t>(s * (kStageBytes >> 4));
+          issue_kblock(d_tmem, a_desc + so, b_desc + so, idesc, k > 0 ? 1u : 0u, bar(kBarEmpty + s));
         }
         if (!ok) break;
-        umma_commit(bar(kBarAccFull + ab));
+        umma_commit_warp(bar(kBarAccFull + ab));
       }
-      if (!ok) *abort_flag = 1;
+      if (!ok && lane == 0) *abort_flag = 1;
     }
   } else {
     const int quad = warp & 3;
@@ -193,22 +241,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     float tv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     int ti[4] = {-1, -1, -1, -1};
+    uint32_t kk[4] = {0u, 0u, 0u, 0u};
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
       const int ab = t & 1;
       if (!mbar_wait(bar(kBarAccFull + ab), (t >> 1) & 1, &g_merge_err)) { ok = false; break; }
       tc_fence_after();
-      const long long col0 = b0 + static_cast<long long>(t) * kBN;
+      const long long col0 = b0 + static_cast<long long>(t) * tile_n;
       const long long remaining = b1 - col0;
-      const int valid = remaining < kBN ? static_cast<int>(remaining) : kBN;
+      const int valid = remaining < tile_n ? static_cast<int>(remaining) : tile_n;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32x32b_x32(tmem + lane_off + ab * kBN + c * 32, r);
-        if (c * 32 < valid) {
+      for (int c = 0; c < tile_n / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld32x32b_x16(tmem + lane_off + ab * kBN + c * 16, r);
+        if constexpr (kKeys) {
+          const int gcol = t * tile_n + c * 16;  // group-local column of r[0]
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int local = c * 32 + i;
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t key = score_key(__uint_as_float(r[i]), gcol + i);
+            key_insert(kk, c * 16 + i < valid ? key : 0u);
+          }
+        } else if (c * 16 < valid) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int local = c * 16 + i;
             if (local < valid)
               topk_insert<K>(tv, ti, bf16_round(__uint_as_float(r[i])), static_cast<int>(col0 + local));
           }
@@ -218,6 +274,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(bar(kBarAccEmpty + ab));
     }
     if (!ok) *abort_flag = 1;
+    if constexpr (kKeys) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        tv[i] = kk[i] ? key_score(kk[i]) : -INFINITY;
+        ti[i] = kk[i] ? static_cast<int>(b0 + (0xFFFF - static_cast<int>(kk[i] & 0xFFFFu))) : -1;
+      }
+    }
     const long long grow = row0 + row;
     if (grow < q1) {
 #pragma unroll
@@ -290,12 +353,18 @@ extern "C" int vb200_sim_topk(const void* query, int64_t q_row_stride, const voi
   int rc = check_sm100();
   if (rc != VB200_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // basis tile: the fewest tiles of <= kBN rows that cover the largest group, each as narrow as
+  // possible (multiple of 16)
+  long long max_nb = 0;
+  for (int64_t g = 0; g < groups; ++g) max_nb = std::max(max_nb, bb[g + 1] - bb[g]);
+  const long long n_tiles_max = std::max(1ll, (max_nb + kBN - 1) / kBN);
+  const int tile_n = static_cast<int>(std::max(16ll, (((max_nb + n_tiles_max - 1) / n_tiles_max) + 15) / 16 * 16));
   CUtensorMap tq, tb;
   if ((rc = make_rows_map(&tq, query, R, D, q_row_stride, kBM)) != VB200_OK) return rc;
-  if (Nb > 0 && (rc = make_rows_map(&tb, basis, Nb, D, b_row_stride, kBN)) != VB200_OK) return rc;
+  if (Nb > 0 && (rc = make_rows_map(&tb, basis, Nb, D, b_row_stride, tile_n)) != VB200_OK) return rc;
   if (Nb == 0) tb = tq;  // never read: every group then has zero basis tiles
-  TopkParams prm{values, indices, k, static_cast<int>(D / kBK)};
-  auto kernel = k == 1 ? sim_topk_kernel<1> : sim_topk_kernel<4>;
+  TopkParams prm{values, indices, k, static_cast<int>(D / kBK), tile_n};
+  auto kernel = k == 1 ? sim_topk_kernel<1, false> : (max_nb <= 65536 ? sim_topk_kernel<4, true> : sim_topk_kernel<4, false>);
   VB200_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
                    "cudaFuncSetAttribute");
   for (int64_t g0 = 0; g0 < groups; g0 += kMaxGroups) {

@@ -95,3 +95,28 @@ def test_streaming_top4_transposed_basis(pkg, oracle, cuda_device):
     _check_topk(oracle, q, b, to_np(v), i.cpu().numpy(), 4)
     with pytest.raises(ValueError, match="at least four"):
         pkg.streaming_top4(_bf16(q, cuda_device), bt[:, :3])
+
+
+@pytest.mark.parametrize("half", [100, 300])  # 300: the copies fall in a different basis tile
+def test_exact_ties_prefer_lower_index(pkg, oracle, cuda_device, half):
+    """Basis rows duplicated (row c and row c + half are identical), so every score appears
+    twice and ties are exact in any accumulation order: the top-4 must list equal scores with
+    the lower index first (the strict-> running top-k and the stable sort of the reference).
+    Some queries are exact negatives of a basis row, so negative and zero scores occur too."""
+    rng = np.random.default_rng(11)
+    D = 64
+    b1 = oracle.round_bf16(rng.standard_normal((half, D)).astype(np.float32) / 8)
+    b = np.concatenate([b1, b1])
+    q = oracle.round_bf16(rng.standard_normal((260, D)).astype(np.float32) / 8)
+    q[:20] = -b1[:20]
+    q[20:30] = 0.0
+    v, i = pkg.similarity_topk(_bf16(q, cuda_device), _bf16(b, cuda_device), 4)
+    v, i = to_np(v), i.cpu().numpy()
+    for r in range(len(q)):
+        pairs = list(zip(-v[r], i[r]))
+        assert pairs == sorted(pairs), f"row {r}: not ordered by (score desc, index asc): {pairs}"
+        for c in i[r]:
+            if c >= half:  # the later copy may only appear after its earlier twin
+                assert c - half in i[r] and list(i[r]).index(c - half) < list(i[r]).index(c), (r, i[r])
+    assert np.all(i[20:30] == np.arange(4))  # all scores 0: the four lowest indices
+    _check_topk(oracle, q, b, v, i, 4)
