@@ -14,6 +14,8 @@
 // warp in a fixed order (keep row, then corner 0..3 partial sums, each in source order).
 #include <cub/cub.cuh>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_common.h"
 
@@ -127,6 +129,38 @@ __global__ void proj_gather_kernel(const T* __restrict__ y, long long ys, const 
     }
   }
   T* drow = out + dst * os;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    // bf16: the rounded products w_c * y come from packed bf16 multiplies (the exact product of
+    // two bf16 values fits in fp32, so one correctly rounded bf16 multiply equals rounding the
+    // fp32 product), then each pair is widened and summed in fp32 in corner order.
+    __nv_bfloat162 w2[kMaxCorners];
+#pragma unroll
+    for (int c = 0; c < kMaxCorners; ++c) w2[c] = __float2bfloat162_rn(wc[c]);
+    for (int i = lane; i < nvec; i += 32) {
+      uint4 raw[kMaxCorners];
+#pragma unroll
+      for (int c = 0; c < kMaxCorners; ++c)
+        if (c < corners) raw[c] = __ldg(reinterpret_cast<const uint4*>(prow[c] + i * V));
+      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+      for (int c = 0; c < kMaxCorners; ++c) {
+        if (c < corners) {
+          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&raw[c]);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const __nv_bfloat162 prod = __hmul2(w2[c], *reinterpret_cast<const __nv_bfloat162*>(&xw[h]));
+            const uint32_t pw = *reinterpret_cast<const uint32_t*>(&prod);
+            acc2[h] = fadd2(acc2[h], pk2(__uint_as_float(pw << 16), __uint_as_float(pw & 0xffff0000u)));
+          }
+        }
+      }
+      float acc[V];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) upk2(acc2[h], acc[2 * h], acc[2 * h + 1]);
+      store_vec<T>(drow + i * V, acc);
+    }
+    return;
+  }
   for (int i = lane; i < nvec; i += 32) {
     float vals[kMaxCorners][V];
 #pragma unroll
@@ -750,6 +784,9 @@ __global__ void csr_mass_kernel(const int32_t* __restrict__ seg_offsets, const f
 // ------------------------------------------------------------------------------------------
 // row normalisation to bf16
 // ------------------------------------------------------------------------------------------
+// One warp per row.  Rows of up to kNormVecs 16-byte vectors per lane (2048 bf16 channels) are
+// read once into registers, reduced, and scaled from registers; wider rows take a second read.
+constexpr int kNormVecs = 8;
 template <typename T>
 __global__ void row_normalize_kernel(const T* __restrict__ x, long long x_rows, long long xs,
                                      const int64_t* __restrict__ rows, long long R, int C, float eps,
@@ -764,8 +801,56 @@ __global__ void row_normalize_kernel(const T* __restrict__ x, long long x_rows, 
     return;
   }
   const T* xr = x + src * xs;
+  __nv_bfloat16* orow = out + r * os;
+  const int nvec = C / V;
+  // V input values -> V bf16 outputs (16 bytes for 16-bit input; two 16-byte halves for fp32)
+  auto emit = [&](int i, const float (&v)[V], float denom) {
+    uint32_t w[V / 2];
+#pragma unroll
+    for (int e = 0; e < V; e += 2) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(__fdiv_rn(v[e], denom), __fdiv_rn(v[e + 1], denom));
+      w[e / 2] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    if constexpr (V == 8) {
+      *reinterpret_cast<uint4*>(orow + i * V) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      *reinterpret_cast<uint2*>(orow + i * V) = make_uint2(w[0], w[1]);
+    }
+  };
+  if (nvec <= 32 * kNormVecs) {
+    uint4 raw[kNormVecs];
+#pragma unroll
+    for (int k = 0; k < kNormVecs; ++k)
+      if (lane + 32 * k < nvec) raw[k] = __ldg(reinterpret_cast<const uint4*>(xr) + lane + 32 * k);
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormVecs; ++k) {
+      if (lane + 32 * k < nvec) {
+        const T* e = reinterpret_cast<const T*>(&raw[k]);
+#pragma unroll
+        for (int q = 0; q < V; ++q) {
+          const float f = to_f32<T>(e[q]);
+          ss = fmaf(f, f, ss);
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float denom = fmaxf(sqrtf(ss), eps);
+#pragma unroll
+    for (int k = 0; k < kNormVecs; ++k) {
+      if (lane + 32 * k < nvec) {
+        float v[V];
+        const T* e = reinterpret_cast<const T*>(&raw[k]);
+#pragma unroll
+        for (int q = 0; q < V; ++q) v[q] = to_f32<T>(e[q]);
+        emit(lane + 32 * k, v, denom);
+      }
+    }
+    return;
+  }
   float ss = 0.f;
-  for (int i = lane; i < C / V; i += 32) {
+  for (int i = lane; i < nvec; i += 32) {
     float v[V];
     load_vec<T>(xr + i * V, v);
 #pragma unroll
@@ -774,15 +859,10 @@ __global__ void row_normalize_kernel(const T* __restrict__ x, long long x_rows, 
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float denom = fmaxf(sqrtf(ss), eps);
-  __nv_bfloat16* orow = out + r * os;
-  for (int i = lane; i < C / V; i += 32) {
+  for (int i = lane; i < nvec; i += 32) {
     float v[V];
     load_vec<T>(xr + i * V, v);
-#pragma unroll
-    for (int e = 0; e < V; e += 2) {
-      const __nv_bfloat162 b = __floats2bfloat162_rn(__fdiv_rn(v[e], denom), __fdiv_rn(v[e + 1], denom));
-      *reinterpret_cast<__nv_bfloat162*>(orow + i * V + e) = b;
-    }
+    emit(i, v, denom);
   }
 }
 
