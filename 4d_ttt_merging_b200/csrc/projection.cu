@@ -159,8 +159,7 @@ __global__ void proj_gather_kernel(const T* __restrict__ y, long long ys, const 
       for (int h = 0; h < 4; ++h) upk2(acc2[h], acc[2 * h], acc[2 * h + 1]);
       store_vec<T>(drow + i * V, acc);
     }
-    return;
-  }
+  } else {
   for (int i = lane; i < nvec; i += 32) {
     float vals[kMaxCorners][V];
 #pragma unroll
@@ -177,6 +176,7 @@ __global__ void proj_gather_kernel(const T* __restrict__ y, long long ys, const 
       }
     }
     store_vec<T>(drow + i * V, acc);
+  }
   }
 }
 
