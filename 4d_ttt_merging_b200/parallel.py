@@ -6,7 +6,9 @@ supports inside their own frame group).  Per global layer a rank
 
   1. builds its plan (merge step) and projects / compacts its own tokens (no exchange),
   2. all-gathers the merged K and V ([K_local, C] bf16 each) and the log-mass vector
-     ([K_local] fp32) with NCCL — the only collective of the layer,
+     ([K_local] fp32) — the only exchange of the layer: peer loads over NVLink from
+     symmetric memory between two device barriers (PeerExchange), or NCCL
+     all_gather_into_tensor where peer-mapped memory is unavailable,
   3. runs mass-bias attention of its own compact queries over all merged keys,
   4. projects and restores its own tokens.
 
@@ -15,12 +17,13 @@ the same key sequence as a single GPU would: results do not depend on the rank c
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["FrameShard", "frame_shard", "gather_merged", "ShardedGlobalBlock"]
+__all__ = ["FrameShard", "frame_shard", "gather_merged", "PeerExchange", "ShardedGlobalBlock"]
 
 
 @dataclass(frozen=True)
@@ -70,6 +73,57 @@ def gather_merged(tensors: list[torch.Tensor], group=None) -> list[torch.Tensor]
     return out
 
 
+class PeerExchange:
+    """The merged-K/V and log-mass all-gather of the sharded block over peer-mapped memory.
+
+    One symmetric allocation per GPU (PyTorch symmetric memory: the same-sized buffer on every
+    GPU, mapped into every rank's address space) holds this rank's compacted q|k|v rows, its
+    log-mass vector and the full rank-ordered K|V buffer.  `exchange` runs a device-side
+    barrier (every rank has compacted, and has finished with its previous full buffer), then
+    `vb200_peer_push` stores this rank's K|V rows into every rank's full buffer (posted NVLink
+    writes) and `vb200_peer_gather` reads every rank's log-mass, then a second barrier (all
+    writes landed).  Ranks must have the same number of merged rows.  The barriers give up
+    after BARRIER_TIMEOUT_MS (a rank that never arrives ends the wait instead of spinning
+    forever)."""
+
+    BARRIER_TIMEOUT_MS = 60_000
+
+    def __init__(self, group, rows: int, C: int, dtype: torch.dtype, device: torch.device):
+        import torch.distributed._symmetric_memory as symm_mem
+        from . import _clib
+        self.rows, self.C = rows, C
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.es = es = torch.empty(0, dtype=dtype).element_size()
+        up = lambda n: -(-n // 256) * 256
+        packed_bytes, lm_bytes = up(rows * 3 * C * es), up(rows * 4)
+        kv_bytes = self.world * rows * 2 * C * es
+        self.buf = symm_mem.empty(packed_bytes + lm_bytes + kv_bytes, dtype=torch.uint8, device=device)
+        self.handle = symm_mem.rendezvous(self.buf, group)
+        self.packed = self.buf[:rows * 3 * C * es].view(dtype).view(rows, 3 * C)
+        self.log_mass = self.buf[packed_bytes:packed_bytes + rows * 4].view(torch.float32)
+        kv_off = packed_bytes + lm_bytes
+        self.kv = self.buf[kv_off:kv_off + kv_bytes].view(dtype).view(self.world * rows, 2 * C)
+        ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        u64 = ctypes.c_uint64 * self.world
+        self._kv_dst = u64(*[p + kv_off for p in ptrs])
+        self._lm_src = u64(*[p + packed_bytes for p in ptrs])
+        self.log_mass_all = torch.empty(self.world * rows, dtype=torch.float32, device=device)
+        self._lib, self._clib = _clib.lib(), _clib
+
+    def exchange(self):
+        """-> (kv [world*rows, 2C], log_mass [world*rows]) in rank order, on the current stream."""
+        C, es, rows = self.C, self.es, self.rows
+        stream = self._clib.stream_of(self.kv.device)
+        self.handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        self._clib.check(self._lib.vb200_peer_push(self.packed.data_ptr() + C * es, rows, 3 * C * es, 2 * C * es,
+                                                   self._kv_dst, self.world, self.rank * rows, 2 * C * es, stream),
+                         "peer_push")
+        self._clib.check(self._lib.vb200_peer_gather(self._lm_src, self.world, 1, rows * 4, rows * 4,
+                                                     self.log_mass_all.data_ptr(), rows * 4, stream), "peer_gather")
+        self.handle.barrier(channel=1, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        return self.kv, self.log_mass_all
+
+
 class ShardedGlobalBlock:
     """One global-attention layer with a per-rank uniform convex plan (see module docstring).
 
@@ -88,6 +142,8 @@ class ShardedGlobalBlock:
         self.world = world
         self.timers = None  # optional dict name -> list of (start, end) CUDA events
         self._ln = None     # fp32 q/k LayerNorm parameters, [2, 64] each
+        self._xchg = None   # PeerExchange (world > 1, CUDA), built on the first step
+        self._xchg_failed = False
 
     def _ev(self, name):
         if self.timers is None:
@@ -101,6 +157,24 @@ class ShardedGlobalBlock:
     def _end(e):
         if e is not None:
             e[1].record()
+
+    def _exchange(self, rows: int, C: int, dtype: torch.dtype, device: torch.device):
+        """The PeerExchange for this shape (built collectively on first use: every rank reaches
+        this point with the same rows), or None where peer-mapped memory is unavailable (then
+        the NCCL all-gather is used)."""
+        if self._xchg_failed or device.type != "cuda":
+            return None
+        x = self._xchg
+        if x is None or x.rows != rows or x.C != C or x.packed.dtype != dtype:
+            try:
+                self._xchg = x = PeerExchange(self.group if self.group is not None else dist.group.WORLD,
+                                              rows, C, dtype, device)
+            except (RuntimeError, ImportError) as err:  # e.g. no CUDA virtual-memory IPC on this system
+                import warnings
+                warnings.warn(f"peer-memory exchange unavailable ({err}); using NCCL all-gather")
+                self._xchg_failed, self._xchg = True, None
+                return None
+        return x
 
     def plan(self, tokens: torch.Tensor):
         from .planners import build_uniform_convex_plan
@@ -126,14 +200,21 @@ class ShardedGlobalBlock:
             from .attention_block import _ln_params
             self._ln = _ln_params(attn.q_norm, attn.k_norm)
         lw, lb, eps = self._ln if self._ln is not None else (None, None, 1e-5)
-        packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111)  # [K_local, 3C]: q | k | v
+        xchg = self._exchange(plan.kept_tokens, C, qkv.dtype, qkv.device) if self.world > 1 else None
+        # [K_local, 3C]: q | k | v, written straight into the peer-readable buffer when sharded
+        packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111,
+                                  out=None if xchg is None else xchg.packed)
         self._end(e)
         log_mass = plan.key_log_mass.reshape(-1)
         K_local = packed.shape[0]
         kv = packed[:, C:]
         if self.world > 1:
             e = self._ev("all_gather")
-            kv, log_mass = gather_merged([kv, log_mass], self.group)
+            if xchg is not None:
+                xchg.log_mass.copy_(log_mass)
+                kv, log_mass = xchg.exchange()
+            else:
+                kv, log_mass = gather_merged([kv, log_mass], self.group)
             self._end(e)
         e = self._ev("attention")
         view = lambda t: t.view(1, t.shape[0], H, C // H).transpose(1, 2)

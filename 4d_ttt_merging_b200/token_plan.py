@@ -207,17 +207,24 @@ class WeightedBilinearTokenPlan:
 
     def compact_qkv(self, qkv: torch.Tensor, ln_weight: torch.Tensor | None = None,
                     ln_bias: torch.Tensor | None = None, eps: float = 1e-5,
-                    pool_mask: int = 0b111) -> torch.Tensor:
+                    pool_mask: int = 0b111, out: torch.Tensor | None = None) -> torch.Tensor:
         """Fused q/k LayerNorm + Q||K||V compaction of a [N, 3C] (or [1, N, 3C]) qkv buffer in
         one kernel (``vb200_compact_qkv``); returns [M, 3C].  ``ln_weight`` / ``ln_bias`` are
         [2, 64] fp32 (q then k) or None.  Bit t of ``pool_mask`` pools tensor t (q, k, v);
-        a clear bit keeps the physical row only (compact_key semantics)."""
+        a clear bit keeps the physical row only (compact_key semantics).  ``out``: an optional
+        [M, 3C] destination (rows 16-byte aligned, unit channel stride), e.g. a buffer that other
+        GPUs read."""
         x = qkv[0] if qkv.ndim == 3 else qkv
         C.require_cuda(x, "compact_qkv")
         if x.stride(-1) != 1 or x.data_ptr() % 16 or (x.stride(0) * x.element_size()) % 16:
             x = x.contiguous()
         c = x.shape[1] // 3
-        out = torch.empty((self.kept_tokens, 3 * c), device=x.device, dtype=x.dtype)
+        if out is None:
+            out = torch.empty((self.kept_tokens, 3 * c), device=x.device, dtype=x.dtype)
+        elif (out.shape != (self.kept_tokens, 3 * c) or out.dtype != x.dtype or out.device != x.device
+              or out.stride(-1) != 1):
+            raise ValueError(f"compact_qkv: out must be [{self.kept_tokens}, {3 * c}] {x.dtype} on {x.device} "
+                             f"with unit channel stride")
         if not self.pool_source_content or self.source_original.shape[1] == 0:
             pool_mask = 0
         lw = None if ln_weight is None else ln_weight.reshape(-1).to(torch.float32).contiguous()

@@ -175,6 +175,24 @@ VB200_API int vb200_proj_gather(int dtype, const void* y, int64_t y_row_stride, 
 VB200_API int vb200_row_gather(int dtype, const void* x, int64_t x_rows, int64_t x_row_stride, const int64_t* index,
                      int64_t R, void* out, int64_t out_row_stride, int64_t C, void* stream);
 
+/* ---- e: rank-ordered gather from other GPUs (sharded global block) ----------------------------
+ * dst row (r * rows + i) = row i of rank r's block at src_ptrs[r] (row stride src_stride_bytes),
+ * for r < world (<= 16) and i < rows; row_bytes per row.  src_ptrs is a HOST array of device
+ * addresses that are valid in this process (peer memory mapped by the caller, e.g. PyTorch
+ * symmetric memory; the local block may be one of them).  Sizes and strides must be multiples of
+ * 4 bytes (16-byte aligned blocks use 16-byte peer loads).  The caller orders the launch after
+ * the peers have written their blocks and before they overwrite them.  Replaces the merged-K/V
+ * and log-mass all-gather of the sharded path (NCCL all_gather_into_tensor). */
+VB200_API int vb200_peer_gather(const uint64_t* src_ptrs, int world, int64_t rows, int64_t src_stride_bytes,
+                                int64_t row_bytes, void* dst, int64_t dst_stride_bytes, void* stream);
+/* Push form of the same exchange: this rank's rows (local src) are stored into every rank's
+ * destination dst_ptrs[r] at rows [dst_row0, dst_row0 + rows) (dst_ptrs: HOST array of
+ * peer-mapped device addresses, 16-byte aligned; all sizes and strides multiples of 16 bytes),
+ * followed by a system-scope fence. */
+VB200_API int vb200_peer_push(const void* src, int64_t rows, int64_t src_stride_bytes, int64_t row_bytes,
+                              const uint64_t* dst_ptrs, int world, int64_t dst_row0, int64_t dst_stride_bytes,
+                              void* stream);
+
 /* ---- a9/a11: merge step ----------------------------------------------------------------------
  * Row L2 normalisation to bf16 (F.normalize(x.float(), dim=-1, eps).to(bfloat16)),
  * as in build_fastvggt_plan (token_merging.py:1102-1103).  `rows` may be NULL (identity)

@@ -76,3 +76,14 @@ def test_host_side_size_checks(pkg):
     assert rc == pkg._clib.EINVAL and b"corners" in lib.vb200_last_error()
     rc = lib.vb200_sim_topk(None, 0, None, 0, 4, 4, 64, 3, None, None, 1, None, None, None)
     assert rc != 0
+
+
+def test_peer_exchange_argument_checks(pkg):
+    lib = pkg.load_library()
+    one = (ctypes.c_uint64 * 1)(16)
+    rc = lib.vb200_peer_gather(one, 17, 1, 16, 16, None, 16, None)
+    assert rc == pkg._clib.EINVAL and b"world" in lib.vb200_last_error()
+    rc = lib.vb200_peer_gather(one, 1, 1, 16, 6, 16, 16, None)
+    assert rc == pkg._clib.EINVAL and b"multiples of 4" in lib.vb200_last_error()
+    rc = lib.vb200_peer_push(8, 1, 16, 16, one, 1, 0, 16, None)  # source not 16-byte aligned
+    assert rc == pkg._clib.EINVAL and b"16-byte" in lib.vb200_last_error()

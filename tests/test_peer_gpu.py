@@ -1,0 +1,49 @@
+"""The rank-ordered exchange kernels of the sharded block (vb200_peer_gather / vb200_peer_push)
+on one GPU: several local buffers stand in for the ranks' peer-mapped blocks, so the copies,
+row offsets, strides and both vector paths are checked against torch.cat."""
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _u64(ptrs):
+    return (ctypes.c_uint64 * len(ptrs))(*ptrs)
+
+
+@pytest.mark.parametrize("cols,pad,dtype", [(96, 8, torch.bfloat16), (7, 5, torch.float32)])  # 16- / 4-byte paths
+def test_peer_gather_rank_order(pkg, cuda_device, cols, pad, dtype):
+    lib, C = pkg.load_library(), pkg._clib
+    world, rows = 3, 37
+    g = torch.Generator(device="cpu").manual_seed(0)
+    # each "rank" holds a [rows, pad + cols] block; the exchanged part is its last `cols` columns
+    blocks = [torch.randn(rows, pad + cols, generator=g).to(cuda_device, dtype) for _ in range(world)]
+    es = blocks[0].element_size()
+    src = _u64([b.data_ptr() + pad * es for b in blocks])
+    out = torch.empty(world * rows, cols, device=cuda_device, dtype=dtype)
+    rc = lib.vb200_peer_gather(src, world, rows, (pad + cols) * es, cols * es, out.data_ptr(), cols * es,
+                               torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.vb200_last_error()
+    torch.cuda.synchronize()
+    assert torch.equal(out, torch.cat([b[:, pad:] for b in blocks]))
+
+
+def test_peer_push_to_every_rank(pkg, cuda_device):
+    lib = pkg.load_library()
+    world, rows, cols = 4, 29, 64
+    g = torch.Generator(device="cpu").manual_seed(1)
+    full = [torch.zeros(world * rows, cols, device=cuda_device, dtype=torch.bfloat16) for _ in range(world)]
+    mine = [torch.randn(rows, 3 * cols, generator=g).to(cuda_device, torch.bfloat16) for _ in range(world)]
+    dst = _u64([f.data_ptr() for f in full])
+    for r in range(world):  # rank r pushes columns [cols, 2 cols) of its rows into every buffer
+        rc = lib.vb200_peer_push(mine[r].data_ptr() + cols * 2, rows, 3 * cols * 2, cols * 2, dst, world, r * rows,
+                                 cols * 2, torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, lib.vb200_last_error()
+    torch.cuda.synchronize()
+    expect = torch.cat([m[:, cols:2 * cols] for m in mine])
+    for f in full:
+        assert torch.equal(f, expect)
