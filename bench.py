@@ -266,6 +266,10 @@ def run_ours(args) -> None:
         raise RuntimeError("device error flags set during the timed steps")
 
     hbm_peak, tf_peak, peak_kind = _peaks()
+    # DRAM bytes (read + written) of one config-2 attention launch on one GPU, from an ncu
+    # capture of this bench (dram__bytes_read.sum + dram__bytes_write.sum): 50.9 MB + 1.9 MB,
+    # essentially the compulsory Q, K, V read (50.6 MB); the output stays in L2 during the kernel.
+    ATTN_DRAM_BYTES = 52.8e6
     frames_per_s = FRAMES * args.steps / (total_ms / 1e3)
     # attention: compact queries of this rank over all merged keys
     K_total = FRAMES * TOKENS_PER_FRAME // MERGE_FACTOR
@@ -296,7 +300,7 @@ def run_ours(args) -> None:
         "components": {"attention_tflops": attn_tflops, "attention_ms": attn_ms,
                        "compact_qkv_gbs": compact_gbs, "restore_gbs": restore_gbs, "phase_ms": phases},
         "roofline": {"bound": "tensor", "achieved": attn_tflops, "peak": tf_peak, "unit": "TFLOP/s",
-                     "frac": attn_tflops / tf_peak, "traffic": None,
+                     "frac": attn_tflops / tf_peak, "traffic": ATTN_DRAM_BYTES if world == 1 else None,
                      "kernel": "mass_bias_attention_tc_kernel",
                      "peak_source": f"{peak_kind} bf16 dense (burst)"},
         "clocks": clocks.summary(),
