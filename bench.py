@@ -52,18 +52,48 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and clock-event (throttle) reasons of one GPU, sampled every 5 ms through NVML
+    (read-only queries) while the timed region runs; nvidia-smi at its 200 ms minimum when NVML
+    is unavailable."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    PERIOD_S = 0.005
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        self.gpu = gpu_index  # CUDA device index (NVML is addressed by PCI bus id, so remapping is harmless)
         self.proc = None
         self.lines: list[str] = []
+        self.rows: list[tuple[float, float, list[str]]] = []
+        self._stop = threading.Event()
+        self._nvml = None
 
     def __enter__(self):
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            prop = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            bits = [pynvml.nvmlClocksEventReasonHwSlowdown, pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    pynvml.nvmlClocksEventReasonSwThermalSlowdown, pynvml.nvmlClocksEventReasonSwPowerCap]
+            max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self._stop.is_set():
+                    mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.rows.append((mhz, max_mhz, ["Active" if r & b else "Not Active" for b in bits]))
+                    self._stop.wait(self.PERIOD_S)
+            self._nvml = pynvml
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # no NVML binding or library: fall back to nvidia-smi
+            self._nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
@@ -79,6 +109,13 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self._nvml is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -87,7 +124,7 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        rows = []
+        rows = list(self.rows)
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
@@ -98,10 +135,9 @@ class ClockSampler:
                 continue
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clocks not sampled"]}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        reasons = sorted({self.NAMES[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvml" if self.rows else "nvidia-smi"}
 
 
 def _cpu_pipeline_inputs(seed: int = 0):
@@ -321,7 +357,7 @@ def run_ours(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
