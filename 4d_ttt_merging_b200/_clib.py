@@ -52,8 +52,9 @@ _SIGNATURES = {
     "vb200_proj_scatter": (
         _c_int,
         [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
-         _c_i64, _c_i64, _c_vp],
+         _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp],
     ),
+    "vb200_proj_scatter_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "vb200_compact_qkv_workspace_size": (_c_size, [_c_i64, _c_i64]),
     "vb200_compact_qkv": (
         _c_int,

@@ -191,6 +191,81 @@ __global__ void zero_rows_kernel(T* out, long long os, long long N, int C) {
 }
 
 // ------------------------------------------------------------------------------------------
+// scatter, long rows: a merged row with more than kScatterChunk CSR entries (skewed plans: a
+// Zipf-popular parent can own a sizeable fraction of all entries) is split into chunks of
+// kScatterChunk consecutive entries.  One warp per chunk writes the chunk's fp32 sum of w * x
+// (sequential within the chunk); proj_scatter_kernel then adds the keep row and the chunk sums
+// in chunk order.  The result is deterministic and the work is balanced across warps.
+// ------------------------------------------------------------------------------------------
+constexpr int kScatterChunk = 512;
+
+__global__ void scatter_count_kernel(const int32_t* __restrict__ seg_offsets, long long M, int corners,
+                                     int32_t* __restrict__ nchunk) {
+  const long long j = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (j > M) return;
+  if (j == M) {
+    nchunk[j] = 0;
+    return;
+  }
+  const int len = seg_offsets[(j + 1) * corners] - seg_offsets[j * corners];
+  nchunk[j] = len > kScatterChunk ? (len + kScatterChunk - 1) / kScatterChunk : 0;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    scatter_chunk_kernel(const T* __restrict__ x, long long x_rows, long long xs,
+                         const int32_t* __restrict__ seg_offsets, long long M, int corners,
+                         const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
+                         const int32_t* __restrict__ chunk_base, float* __restrict__ partials, int C) {
+  constexpr int V = Vec<T>::N;
+  const long long c = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (c >= chunk_base[M]) return;
+  long long lo = 0, hi = M;  // the row j with chunk_base[j] <= c < chunk_base[j + 1]
+  while (hi - lo > 1) {
+    const long long mid = (lo + hi) / 2;
+    if (chunk_base[mid] <= c) lo = mid;
+    else hi = mid;
+  }
+  const long long j = lo;
+  const int r0 = seg_offsets[j * corners], r1 = seg_offsets[(j + 1) * corners];
+  const int e0 = r0 + static_cast<int>(c - chunk_base[j]) * kScatterChunk;
+  const int e1 = e0 + kScatterChunk < r1 ? e0 + kScatterChunk : r1;
+  float* pr = partials + c * C;
+  for (int col = lane * V; col < C; col += 32 * V) {
+    float part[V];
+#pragma unroll
+    for (int q = 0; q < V; ++q) part[q] = 0.f;
+    int e = e0;
+    for (; e + 1 < e1; e += 2) {  // two rows in flight per lane
+      int s0 = __ldg(entry_src + e), s1 = __ldg(entry_src + e + 1);
+      float w0 = __ldg(entry_w + e), w1 = __ldg(entry_w + e + 1);
+      if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
+      if (s1 < 0 || s1 >= x_rows) { s1 = 0; w1 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
+      float v0[V], v1[V];
+      load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0);
+      load_vec<T>(x + static_cast<long long>(s1) * xs + col, v1);
+#pragma unroll
+      for (int q = 0; q < V; ++q) {
+        part[q] = __fadd_rn(part[q], __fmul_rn(w0, v0[q]));
+        part[q] = __fadd_rn(part[q], __fmul_rn(w1, v1[q]));
+      }
+    }
+    if (e < e1) {
+      int s0 = __ldg(entry_src + e);
+      float w0 = __ldg(entry_w + e);
+      if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
+      float v0[V];
+      load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0);
+#pragma unroll
+      for (int q = 0; q < V; ++q) part[q] = __fadd_rn(part[q], __fmul_rn(w0, v0[q]));
+    }
+#pragma unroll
+    for (int q = 0; q < V; ++q) pr[col + q] = part[q];
+  }
+}
+
+// ------------------------------------------------------------------------------------------
 // scatter (compact): out[j] = (keep_j + sum_c part_c) / normalizer_j
 //   kCB 16-byte vectors per lane are reduced per pass (kCB * 32 * V channels).
 // ------------------------------------------------------------------------------------------
@@ -200,7 +275,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
                         long long M, int corners, const int32_t* __restrict__ seg_offsets,
                         const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
                         const float* __restrict__ normalizer, T* __restrict__ out, long long os,
-                        int C) {
+                        int C, const int32_t* __restrict__ chunk_base, const float* __restrict__ partials) {
   constexpr int V = Vec<T>::N;
   constexpr int kChunk = kCB * 32 * V;  // channels per pass
   const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
@@ -218,6 +293,28 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   }
   T* drow = out + j * os;
   const int32_t* seg = seg_offsets + j * corners;
+  if (chunk_base != nullptr && chunk_base[j + 1] > chunk_base[j]) {
+    // long row: keep row + the fp32 partial sums of its entry chunks, in chunk order
+    const int k0 = chunk_base[j], k1 = chunk_base[j + 1];
+    for (int col = lane * V; col < C; col += 32 * V) {
+      float acc[V];
+      if (krow != nullptr) {
+        load_vec<T>(krow + col, acc);
+      } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = 0.f;
+      }
+      for (int k = k0; k < k1; ++k) {
+        const float* pr = partials + static_cast<long long>(k) * C + col;
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = __fadd_rn(acc[e], pr[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < V; ++e) acc[e] = __fdiv_rn(acc[e], norm);
+      store_vec<T>(drow + col, acc);
+    }
+    return;
+  }
 
   for (int base = 0; base < C; base += kChunk) {
     float acc[kCB][V];
@@ -990,23 +1087,80 @@ extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int
   return VB200_OK;
 }
 
+struct ScatterWorkspace {
+  size_t nchunk, chunk_base, scan_tmp, partials, total, scan_bytes;
+  long long bound;  // upper bound on the number of chunks
+};
+
+ScatterWorkspace scatter_layout(int64_t M, int64_t n_entries, int64_t C) {
+  ScatterWorkspace w{};
+  size_t scan_bytes = 0;
+  cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int32_t*>(nullptr), static_cast<int32_t*>(nullptr),
+                                static_cast<int>(M + 1));
+  // a long row (> L entries) has ceil(len / L) <= 2 len / L chunks, so all chunks <= 2 n / L
+  w.bound = 2 * ((n_entries + kScatterChunk - 1) / kScatterChunk) + 1;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  };
+  w.nchunk = take(static_cast<size_t>(M + 1) * 4);
+  w.chunk_base = take(static_cast<size_t>(M + 1) * 4);
+  w.scan_tmp = take(scan_bytes);
+  w.partials = take(static_cast<size_t>(w.bound) * static_cast<size_t>(C) * 4);
+  w.total = off;
+  w.scan_bytes = scan_bytes;
+  return w;
+}
+
+extern "C" size_t vb200_proj_scatter_workspace_size(int64_t M, int64_t n_entries, int64_t C) {
+  if (M < 0 || n_entries < 0 || C < 0) return 0;
+  return scatter_layout(M, n_entries, C).total;
+}
+
 extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64_t xs, const int64_t* keep,
                                   int64_t M, int64_t corners, const int32_t* seg_offsets,
                                   const int32_t* entry_src, const float* entry_w,
                                   const float* normalizer, void* out, int64_t os, int64_t C,
-                                  void* stream) {
+                                  int64_t n_entries, void* workspace, size_t workspace_bytes, void* stream) {
   VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "proj_scatter: bad dtype %d", dtype);
-  VB200_REQUIRE(M >= 0 && C >= 0 && corners >= 1, "proj_scatter: bad sizes");
+  VB200_REQUIRE(M >= 0 && C >= 0 && corners >= 1 && n_entries >= 0, "proj_scatter: bad sizes");
   if (M == 0 || C == 0) return VB200_OK;
   VB200_REQUIRE(x && out && seg_offsets && normalizer && x_rows > 0, "proj_scatter: null pointer or empty input");
+  const ScatterWorkspace lay = scatter_layout(M, n_entries, C);
+  VB200_REQUIRE(workspace != nullptr && workspace_bytes >= lay.total,
+                "proj_scatter: workspace of %zu bytes required (got %zu)", lay.total, workspace_bytes);
   int rc;
   if ((rc = check_rows(dtype, x, xs, C, "proj_scatter input")) != VB200_OK) return rc;
   if ((rc = check_rows(dtype, out, os, C, "proj_scatter output")) != VB200_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* nchunk = reinterpret_cast<int32_t*>(ws + lay.nchunk);
+  int32_t* chunk_base = reinterpret_cast<int32_t*>(ws + lay.chunk_base);
+  float* partials = reinterpret_cast<float*>(ws + lay.partials);
+  scatter_count_kernel<<<static_cast<unsigned>((M + 1 + 255) / 256), 256, 0, st>>>(seg_offsets, M,
+                                                                                  static_cast<int>(corners), nchunk);
+  VB200_CHECK_LAUNCH("scatter_count_kernel");
+  size_t scan_bytes = lay.scan_bytes;
+  VB200_CHECK_CUDA(cub::DeviceScan::ExclusiveSum(ws + lay.scan_tmp, scan_bytes, nchunk, chunk_base,
+                                                 static_cast<int>(M + 1), st),
+                   "cub::DeviceScan::ExclusiveSum");
+  if (n_entries > kScatterChunk) {
+#define VB200_CHUNKS(T)                                                                              \
+  scatter_chunk_kernel<T><<<row_blocks(lay.bound), kWarpsPerBlock * 32, 0, st>>>(                     \
+      static_cast<const T*>(x), x_rows, xs, seg_offsets, M, static_cast<int>(corners), entry_src, entry_w, \
+      chunk_base, partials, static_cast<int>(C))
+    if (dtype == VB200_F32) VB200_CHUNKS(float);
+    else if (dtype == VB200_BF16) VB200_CHUNKS(__nv_bfloat16);
+    else VB200_CHUNKS(__half);
+#undef VB200_CHUNKS
+    VB200_CHECK_LAUNCH("scatter_chunk_kernel");
+  }
 #define VB200_SCATTER(T, CB)                                                                  \
   proj_scatter_kernel<T, CB><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                  \
       static_cast<const T*>(x), x_rows, xs, keep, M, static_cast<int>(corners), seg_offsets, entry_src, \
-      entry_w, normalizer, static_cast<T*>(out), os, static_cast<int>(C))
+      entry_w, normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials)
   if (dtype == VB200_F32) {
     if (C <= 128) VB200_SCATTER(float, 1);
     else VB200_SCATTER(float, 4);

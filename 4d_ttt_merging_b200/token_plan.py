@@ -38,10 +38,15 @@ def _as_rows(value: torch.Tensor) -> torch.Tensor:
 def _scatter(x2d: torch.Tensor, keep: torch.Tensor | None, csr: PlanCSR, normalizer: torch.Tensor,
              rows_out: int) -> torch.Tensor:
     out = torch.empty((rows_out, x2d.shape[1]), device=x2d.device, dtype=x2d.dtype)
-    rc = C.lib().vb200_proj_scatter(
+    lib = C.lib()
+    n_entries = csr.entry_src.numel()
+    ws_bytes = lib.vb200_proj_scatter_workspace_size(rows_out, n_entries, x2d.shape[1])
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2d.device)
+    rc = lib.vb200_proj_scatter(
         C.dtype_code(x2d.dtype), x2d.data_ptr(), x2d.shape[0], x2d.stride(0), C.ptr(keep), rows_out, csr.corners,
         csr.seg_offsets.data_ptr(), csr.entry_src.data_ptr(), csr.entry_w.data_ptr(),
-        normalizer.data_ptr(), out.data_ptr(), out.stride(0), x2d.shape[1], C.stream_of(x2d.device),
+        normalizer.data_ptr(), out.data_ptr(), out.stride(0), x2d.shape[1], n_entries, ws.data_ptr(), ws_bytes,
+        C.stream_of(x2d.device),
     )
     C.check(rc, "proj_scatter")
     return out

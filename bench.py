@@ -185,6 +185,73 @@ def cpu_baseline(repeats: int = 2) -> dict:
                       f"{t:.2f} s per sample"}
 
 
+def projection_stress(pkg, dev, hbm_peak: float) -> dict:
+    """Config 5 (top-4 projection bandwidth stress) on one GPU: N = 1,048,576 tokens,
+    M = 65,536 evenly spaced merged tokens, D = 1024 bf16.  Each source draws four distinct
+    parents Zipf(1.1) over the merged tokens (ranks mapped to ids by a seeded permutation), with
+    Dirichlet(1,1,1,1) weights; sampled on the GPU.  Times the scatter (tokens -> merged,
+    `plan.compact`) and the gather (merged -> tokens, `plan.restore`) with CUDA events; GB/s
+    counts compulsory HBM bytes (every token row and merged row once, plus the plan arrays)."""
+    import torch
+    N, M, D, corners = 1 << 20, 1 << 16, 1024, 4
+    g = torch.Generator(device=dev).manual_seed(5)
+    keep = torch.arange(M, device=dev, dtype=torch.long) * (N // M)
+    mask = torch.ones(N, dtype=torch.bool, device=dev)
+    mask[keep] = False
+    src = torch.nonzero(mask).flatten()
+    S = src.numel()
+    zipf = torch.arange(1, M + 1, device=dev, dtype=torch.float64).pow(-1.1)
+    perm = torch.randperm(M, device=dev, generator=g)
+    draws = perm[torch.multinomial(zipf.float(), S * 12, replacement=True, generator=g).view(S, 12)]
+    earlier = torch.tril(torch.ones(12, 12, dtype=torch.bool, device=dev), diagonal=-1)  # [j, k]: k < j
+    dup = ((draws[:, :, None] == draws[:, None, :]) & earlier).any(-1)
+    first = (~dup).cumsum(1)
+    pick = (~dup) & (first <= corners)
+    short = pick.sum(1) < corners  # rows with fewer than four distinct draws (rare)
+    parent = torch.empty(S, corners, dtype=torch.long, device=dev)
+    ok_rows = ~short
+    parent[ok_rows] = draws[ok_rows][pick[ok_rows]].view(-1, corners)
+    if short.any():
+        base = torch.randint(0, M - corners, (int(short.sum()),), device=dev, generator=g)
+        parent[short] = base[:, None] + torch.arange(corners, device=dev)[None]
+    e = -torch.rand(S, corners, device=dev, generator=g).clamp_min(1e-12).log()
+    w = (e / e.sum(1, keepdim=True)).float()
+    norm = pkg.deterministic_weighted_normalizer(parent[None], w[None], M)
+    plan = pkg.WeightedBilinearTokenPlan(
+        keep=keep[None], source_original=src[None], source_parent_compact=parent[None], source_pool_weights=w[None],
+        source_restore_weights=w[None], original_tokens=N, normalizer=norm, key_log_mass=norm[..., 0].log())
+    x = torch.randn(1, N, D, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.randn(1, M, D, device=dev, generator=g).to(torch.bfloat16)
+
+    def timed(fn, reps=5):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        return statistics.median(ms)
+
+    scatter_ms = timed(lambda: plan.compact(x))
+    gather_ms = timed(lambda: plan.restore(y))
+    meta = S * corners * (4 + 4) + M * 4 * 2
+    scatter_bytes = N * D * 2 + M * D * 2 + meta
+    gather_bytes = M * D * 2 + N * D * 2 + S * corners * (8 + 8 + 4) + M * 8
+    sgbs = scatter_bytes / (scatter_ms / 1e3) / 1e9
+    ggbs = gather_bytes / (gather_ms / 1e3) / 1e9
+    del x, y, plan
+    return {"workload": "config 5: N=1,048,576 tokens, M=65,536 merged, D=1024 bf16, Zipf(1.1) parents, "
+                        "Dirichlet(1,1,1,1) weights, 1 GPU",
+            "scatter_ms": scatter_ms, "scatter_gbs": sgbs, "scatter_frac": sgbs / hbm_peak,
+            "gather_ms": gather_ms, "gather_gbs": ggbs, "gather_frac": ggbs / hbm_peak,
+            "peak_gbs": hbm_peak}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -345,6 +412,8 @@ def run_ours(args) -> None:
                 "d2h_bytes_per_step": FRAMES * TOKENS_PER_FRAME * DIM * 2},
         "gpu_launches": int(launches),
     }
+    if world == 1:
+        line["components"]["projection_config5"] = projection_stress(pkg, dev, hbm_peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:

@@ -120,7 +120,8 @@ VB200_API int vb200_plan_csr_build(const int64_t* parent, const float* weights, 
 /* ---- a4: top-4 scatter-accumulate (tokens -> merged) ----------------------------------------
  * out[j] = (x[keep[j]] + sum_c sum_{e in seg(j,c)} w_e * x[entry_src[e]]) / normalizer[j]
  * accumulated in fp32 (each product rounded to fp32, corner partial sums added in corner
- * order), written in `dtype`.  keep may be NULL (hard-merge mean pooling: the accumulator
+ * order; the entries of a merged row with more than 512 of them are summed in 512-entry chunks,
+ * chunk sums added in chunk order), written in `dtype`.  keep may be NULL (hard-merge mean pooling: the accumulator
  * starts at zero).  Row strides in elements; C % 8 == 0 for 16-bit types, C % 4 for fp32;
  * rows 16-byte aligned.  Rows of x outside [0, x_rows) referenced by keep or entry_src set
  * device error bit 1 and are skipped (keep: the accumulator starts at zero).
@@ -130,7 +131,13 @@ VB200_API int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64
                        const int64_t* keep, int64_t M, int64_t corners,
                        const int32_t* seg_offsets, const int32_t* entry_src,
                        const float* entry_w, const float* normalizer, void* out,
-                       int64_t out_row_stride, int64_t C, void* stream);
+                       int64_t out_row_stride, int64_t C, int64_t n_entries, void* workspace,
+                       size_t workspace_bytes, void* stream);
+/* Scratch of vb200_proj_scatter for M merged rows, n_entries CSR entries (the length of
+ * entry_src) and C channels.  Merged rows with more than 512 entries (skewed plans) are split
+ * into 512-entry chunks whose fp32 sums are added to the keep row in chunk order; the scratch
+ * holds those sums (at most 2 * n_entries / 512 + 1 chunks of C floats). */
+VB200_API size_t vb200_proj_scatter_workspace_size(int64_t M, int64_t n_entries, int64_t C);
 
 /* ---- a4 + q/k norm fused: Q||K||V compaction of the qkv projection ---------------------------
  * qkv: [rows, 3C] rows of [q | k | v] (C = heads * 64, C % 256 == 0), bf16 or fp16.  q and k

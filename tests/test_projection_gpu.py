@@ -85,6 +85,28 @@ def test_zipf_skewed_segments(pkg, oracle, cuda_device):
     assert_close(got, ref, "bf16", tol=8e-3)
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_scatter_long_rows_chunked(pkg, oracle, cuda_device, dtype):
+    """Every merged row owns thousands of entries (16 rows for 20,000 tokens), so the scatter
+    splits rows into 512-entry chunks whose fp32 sums are added in chunk order.  Matches the
+    oracle's sequential sum within the parity tolerance and is bit-repeatable."""
+    N, M, C = 20000, 16, 96
+    rng = np.random.default_rng(2)
+    keep, src, parent, w = oracle.random_plan(rng, N, M)
+    plan = _plan(pkg, keep, src, parent, w, N, dev=cuda_device)
+    norm = oracle.normalizer(parent, w, M)
+    x = rng.standard_normal((N, C)).astype(np.float32)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    if dtype == "bf16":
+        x = oracle.round_bf16(x)
+    xt = torch.from_numpy(x).to(cuda_device, tdt)[None]
+    ref = oracle.compact(x, keep, src, parent, w, norm, dtype=dtype)
+    got = plan.compact(xt)
+    assert_close(to_np(got[0]), ref, dtype)
+    assert torch.equal(got, plan.compact(xt))
+    assert pkg.device_error_flags() == 0
+
+
 def test_empty_sources_and_partial_cover(pkg, cuda_device):
     dev = cuda_device
     N, K, C = 50, 50, 64
