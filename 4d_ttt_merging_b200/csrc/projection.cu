@@ -192,23 +192,86 @@ __global__ void zero_rows_kernel(T* out, long long os, long long N, int C) {
 
 // ------------------------------------------------------------------------------------------
 // scatter, long rows: a merged row with more than kScatterChunk CSR entries (skewed plans: a
-// Zipf-popular parent can own a sizeable fraction of all entries) is split into chunks of
-// kScatterChunk consecutive entries.  One warp per chunk writes the chunk's fp32 sum of w * x
-// (sequential within the chunk); proj_scatter_kernel then adds the keep row and the chunk sums
-// in chunk order.  The result is deterministic and the work is balanced across warps.
+// Zipf-popular parent can own a tenth of all entries) is reduced as a fixed two-level tree.
+// Level 0: one warp per chunk of kScatterChunk consecutive entries writes the chunk's fp32 sum
+// of w * x (sequential within the chunk).  Level 1: a row with more than kScatterGroup chunks
+// gets one warp per group of kScatterGroup consecutive chunk sums.  proj_scatter_kernel then adds
+// the keep row and the row's level-1 sums (or, for shorter rows, its level-0 sums) in order.
+// The result is deterministic and no warp walks more than ~kScatterChunk rows or ~kScatterGroup
+// partial sums (up to rows of kScatterChunk * kScatterGroup^2 entries).
 // ------------------------------------------------------------------------------------------
-constexpr int kScatterChunk = 512;
+constexpr int kScatterChunk = 256;   // entries per level-0 chunk
+constexpr int kScatterGroup = 64;    // level-0 partials per level-1 sum
+constexpr int kScatterInFlight = 4;
 
 __global__ void scatter_count_kernel(const int32_t* __restrict__ seg_offsets, long long M, int corners,
-                                     int32_t* __restrict__ nchunk) {
+                                     int32_t* __restrict__ nchunk, int32_t* __restrict__ ngroup) {
   const long long j = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (j > M) return;
   if (j == M) {
     nchunk[j] = 0;
+    ngroup[j] = 0;
     return;
   }
   const int len = seg_offsets[(j + 1) * corners] - seg_offsets[j * corners];
-  nchunk[j] = len > kScatterChunk ? (len + kScatterChunk - 1) / kScatterChunk : 0;
+  const int n0 = len > kScatterChunk ? (len + kScatterChunk - 1) / kScatterChunk : 0;
+  nchunk[j] = n0;
+  ngroup[j] = n0 > kScatterGroup ? (n0 + kScatterGroup - 1) / kScatterGroup : 0;
+}
+
+// Sum of partial rows [k0, k1) of `src` (C floats each) over the channels of this lane, kept in
+// flight kSumInFlight rows at a time, added in row order.
+constexpr int kSumInFlight = 8;
+__device__ __forceinline__ void sum_partials(const float* __restrict__ src, int k0, int k1, int C, int col,
+                                             float (&acc)[8], int V) {
+  for (int kb = k0; kb < k1; kb += kSumInFlight) {
+    float4 a[kSumInFlight], b[kSumInFlight];
+#pragma unroll
+    for (int u = 0; u < kSumInFlight; ++u) {
+      if (kb + u < k1) {
+        const float* pr = src + static_cast<long long>(kb + u) * C + col;
+        a[u] = *reinterpret_cast<const float4*>(pr);
+        if (V == 8) b[u] = *reinterpret_cast<const float4*>(pr + 4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kSumInFlight; ++u) {
+      if (kb + u < k1) {
+        acc[0] = __fadd_rn(acc[0], a[u].x); acc[1] = __fadd_rn(acc[1], a[u].y);
+        acc[2] = __fadd_rn(acc[2], a[u].z); acc[3] = __fadd_rn(acc[3], a[u].w);
+        if (V == 8) {
+          acc[4] = __fadd_rn(acc[4], b[u].x); acc[5] = __fadd_rn(acc[5], b[u].y);
+          acc[6] = __fadd_rn(acc[6], b[u].z); acc[7] = __fadd_rn(acc[7], b[u].w);
+        }
+      }
+    }
+  }
+}
+
+// Level 1: warp g sums group g's kScatterGroup (or fewer) consecutive level-0 partial rows.
+template <int V>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    scatter_group_kernel(long long M, const int32_t* __restrict__ chunk_base, const int32_t* __restrict__ group_base,
+                         const float* __restrict__ partials, float* __restrict__ partials1, int C) {
+  const long long g = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (g >= group_base[M]) return;
+  long long lo = 0, hi = M;  // row j with group_base[j] <= g < group_base[j + 1]
+  while (hi - lo > 1) {
+    const long long mid = (lo + hi) / 2;
+    if (group_base[mid] <= g) lo = mid;
+    else hi = mid;
+  }
+  const long long j = lo;
+  const int k0 = chunk_base[j] + static_cast<int>(g - group_base[j]) * kScatterGroup;
+  const int k1 = k0 + kScatterGroup < chunk_base[j + 1] ? k0 + kScatterGroup : chunk_base[j + 1];
+  for (int col = lane * V; col < C; col += 32 * V) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    sum_partials(partials, k0, k1, C, col, acc, V);
+    float* dst = partials1 + g * C + col;
+#pragma unroll
+    for (int q = 0; q < V; ++q) dst[q] = acc[q];
+  }
 }
 
 template <typename T>
@@ -236,29 +299,29 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     float part[V];
 #pragma unroll
     for (int q = 0; q < V; ++q) part[q] = 0.f;
-    int e = e0;
-    for (; e + 1 < e1; e += 2) {  // two rows in flight per lane
-      int s0 = __ldg(entry_src + e), s1 = __ldg(entry_src + e + 1);
-      float w0 = __ldg(entry_w + e), w1 = __ldg(entry_w + e + 1);
-      if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-      if (s1 < 0 || s1 >= x_rows) { s1 = 0; w1 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-      float v0[V], v1[V];
-      load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0);
-      load_vec<T>(x + static_cast<long long>(s1) * xs + col, v1);
+    // kScatterInFlight source rows in flight per lane: all loads first, then the FMAs in entry
+    // order (the sum stays sequential within the chunk)
+    for (int eb = e0; eb < e1; eb += kScatterInFlight) {
+      float v[kScatterInFlight][V];
+      float w[kScatterInFlight];
 #pragma unroll
-      for (int q = 0; q < V; ++q) {
-        part[q] = __fadd_rn(part[q], __fmul_rn(w0, v0[q]));
-        part[q] = __fadd_rn(part[q], __fmul_rn(w1, v1[q]));
+      for (int u = 0; u < kScatterInFlight; ++u) {
+        int su = 0;
+        w[u] = 0.f;
+        if (eb + u < e1) {
+          su = __ldg(entry_src + eb + u);
+          w[u] = __ldg(entry_w + eb + u);
+          if (su < 0 || su >= x_rows) { su = 0; w[u] = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
+        }
+        load_vec<T>(x + static_cast<long long>(su) * xs + col, v[u]);
       }
-    }
-    if (e < e1) {
-      int s0 = __ldg(entry_src + e);
-      float w0 = __ldg(entry_w + e);
-      if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-      float v0[V];
-      load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0);
 #pragma unroll
-      for (int q = 0; q < V; ++q) part[q] = __fadd_rn(part[q], __fmul_rn(w0, v0[q]));
+      for (int u = 0; u < kScatterInFlight; ++u) {
+        if (eb + u < e1) {
+#pragma unroll
+          for (int q = 0; q < V; ++q) part[q] = __fadd_rn(part[q], __fmul_rn(w[u], v[u][q]));
+        }
+      }
     }
 #pragma unroll
     for (int q = 0; q < V; ++q) pr[col + q] = part[q];
@@ -275,7 +338,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
                         long long M, int corners, const int32_t* __restrict__ seg_offsets,
                         const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
                         const float* __restrict__ normalizer, T* __restrict__ out, long long os,
-                        int C, const int32_t* __restrict__ chunk_base, const float* __restrict__ partials) {
+                        int C, const int32_t* __restrict__ chunk_base, const float* __restrict__ partials,
+                        const int32_t* __restrict__ group_base, const float* __restrict__ partials1) {
   constexpr int V = Vec<T>::N;
   constexpr int kChunk = kCB * 32 * V;  // channels per pass
   const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
@@ -294,24 +358,27 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   T* drow = out + j * os;
   const int32_t* seg = seg_offsets + j * corners;
   if (chunk_base != nullptr && chunk_base[j + 1] > chunk_base[j]) {
-    // long row: keep row + the fp32 partial sums of its entry chunks, in chunk order
-    const int k0 = chunk_base[j], k1 = chunk_base[j + 1];
+    // long row: keep row + its level-1 sums (or its level-0 chunk sums), in order
+    const bool grouped = group_base[j + 1] > group_base[j];
+    const float* src = grouped ? partials1 : partials;
+    const int k0 = grouped ? group_base[j] : chunk_base[j];
+    const int k1 = grouped ? group_base[j + 1] : chunk_base[j + 1];
     for (int col = lane * V; col < C; col += 32 * V) {
-      float acc[V];
+      float kv[V];
       if (krow != nullptr) {
-        load_vec<T>(krow + col, acc);
+        load_vec<T>(krow + col, kv);
       } else {
 #pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = 0.f;
+        for (int e = 0; e < V; ++e) kv[e] = 0.f;
       }
-      for (int k = k0; k < k1; ++k) {
-        const float* pr = partials + static_cast<long long>(k) * C + col;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = __fadd_rn(acc[e], pr[e]);
-      }
+      for (int e = 0; e < V; ++e) acc[e] = kv[e];
+      sum_partials(src, k0, k1, C, col, acc, V);
+      float out_v[V];
 #pragma unroll
-      for (int e = 0; e < V; ++e) acc[e] = __fdiv_rn(acc[e], norm);
-      store_vec<T>(drow + col, acc);
+      for (int e = 0; e < V; ++e) out_v[e] = __fdiv_rn(acc[e], norm);
+      store_vec<T>(drow + col, out_v);
     }
     return;
   }
@@ -1088,8 +1155,8 @@ extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int
 }
 
 struct ScatterWorkspace {
-  size_t nchunk, chunk_base, scan_tmp, partials, total, scan_bytes;
-  long long bound;  // upper bound on the number of chunks
+  size_t nchunk, chunk_base, ngroup, group_base, scan_tmp, partials, partials1, total, scan_bytes;
+  long long bound, bound1;  // upper bounds on the numbers of level-0 chunks and level-1 groups
 };
 
 ScatterWorkspace scatter_layout(int64_t M, int64_t n_entries, int64_t C) {
@@ -1099,6 +1166,7 @@ ScatterWorkspace scatter_layout(int64_t M, int64_t n_entries, int64_t C) {
                                 static_cast<int>(M + 1));
   // a long row (> L entries) has ceil(len / L) <= 2 len / L chunks, so all chunks <= 2 n / L
   w.bound = 2 * ((n_entries + kScatterChunk - 1) / kScatterChunk) + 1;
+  w.bound1 = 2 * ((w.bound + kScatterGroup - 1) / kScatterGroup) + 1;  // same argument, one level up
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -1107,8 +1175,11 @@ ScatterWorkspace scatter_layout(int64_t M, int64_t n_entries, int64_t C) {
   };
   w.nchunk = take(static_cast<size_t>(M + 1) * 4);
   w.chunk_base = take(static_cast<size_t>(M + 1) * 4);
+  w.ngroup = take(static_cast<size_t>(M + 1) * 4);
+  w.group_base = take(static_cast<size_t>(M + 1) * 4);
   w.scan_tmp = take(scan_bytes);
   w.partials = take(static_cast<size_t>(w.bound) * static_cast<size_t>(C) * 4);
+  w.partials1 = take(static_cast<size_t>(w.bound1) * static_cast<size_t>(C) * 4);
   w.total = off;
   w.scan_bytes = scan_bytes;
   return w;
@@ -1139,11 +1210,18 @@ extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int6
   int32_t* nchunk = reinterpret_cast<int32_t*>(ws + lay.nchunk);
   int32_t* chunk_base = reinterpret_cast<int32_t*>(ws + lay.chunk_base);
   float* partials = reinterpret_cast<float*>(ws + lay.partials);
-  scatter_count_kernel<<<static_cast<unsigned>((M + 1 + 255) / 256), 256, 0, st>>>(seg_offsets, M,
-                                                                                  static_cast<int>(corners), nchunk);
+  int32_t* ngroup = reinterpret_cast<int32_t*>(ws + lay.ngroup);
+  int32_t* group_base = reinterpret_cast<int32_t*>(ws + lay.group_base);
+  float* partials1 = reinterpret_cast<float*>(ws + lay.partials1);
+  scatter_count_kernel<<<static_cast<unsigned>((M + 1 + 255) / 256), 256, 0, st>>>(
+      seg_offsets, M, static_cast<int>(corners), nchunk, ngroup);
   VB200_CHECK_LAUNCH("scatter_count_kernel");
   size_t scan_bytes = lay.scan_bytes;
   VB200_CHECK_CUDA(cub::DeviceScan::ExclusiveSum(ws + lay.scan_tmp, scan_bytes, nchunk, chunk_base,
+                                                 static_cast<int>(M + 1), st),
+                   "cub::DeviceScan::ExclusiveSum");
+  scan_bytes = lay.scan_bytes;
+  VB200_CHECK_CUDA(cub::DeviceScan::ExclusiveSum(ws + lay.scan_tmp, scan_bytes, ngroup, group_base,
                                                  static_cast<int>(M + 1), st),
                    "cub::DeviceScan::ExclusiveSum");
   if (n_entries > kScatterChunk) {
@@ -1156,11 +1234,21 @@ extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int6
     else VB200_CHUNKS(__half);
 #undef VB200_CHUNKS
     VB200_CHECK_LAUNCH("scatter_chunk_kernel");
+    const int V = dtype == VB200_F32 ? 4 : 8;
+    if (V == 8) {
+      scatter_group_kernel<8><<<row_blocks(lay.bound1), kWarpsPerBlock * 32, 0, st>>>(
+          M, chunk_base, group_base, partials, partials1, static_cast<int>(C));
+    } else {
+      scatter_group_kernel<4><<<row_blocks(lay.bound1), kWarpsPerBlock * 32, 0, st>>>(
+          M, chunk_base, group_base, partials, partials1, static_cast<int>(C));
+    }
+    VB200_CHECK_LAUNCH("scatter_group_kernel");
   }
 #define VB200_SCATTER(T, CB)                                                                  \
   proj_scatter_kernel<T, CB><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                  \
       static_cast<const T*>(x), x_rows, xs, keep, M, static_cast<int>(corners), seg_offsets, entry_src, \
-      entry_w, normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials)
+      entry_w, normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials, group_base, \
+      partials1)
   if (dtype == VB200_F32) {
     if (C <= 128) VB200_SCATTER(float, 1);
     else VB200_SCATTER(float, 4);

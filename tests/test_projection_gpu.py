@@ -88,7 +88,7 @@ def test_zipf_skewed_segments(pkg, oracle, cuda_device):
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_scatter_long_rows_chunked(pkg, oracle, cuda_device, dtype):
     """Every merged row owns thousands of entries (16 rows for 20,000 tokens), so the scatter
-    splits rows into 512-entry chunks whose fp32 sums are added in chunk order.  Matches the
+    splits rows into 128-entry chunks whose fp32 sums are added in chunk order.  Matches the
     oracle's sequential sum within the parity tolerance and is bit-repeatable."""
     N, M, C = 20000, 16, 96
     rng = np.random.default_rng(2)
