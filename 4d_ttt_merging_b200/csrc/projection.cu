@@ -221,7 +221,7 @@ __global__ void scatter_count_kernel(const int32_t* __restrict__ seg_offsets, lo
 
 // Sum of partial rows [k0, k1) of `src` (C floats each) over the channels of this lane, kept in
 // flight kSumInFlight rows at a time, added in row order.
-constexpr int kSumInFlight = 8;
+template <int kSumInFlight>
 __device__ __forceinline__ void sum_partials(const float* __restrict__ src, int k0, int k1, int C, int col,
                                              float (&acc)[8], int V) {
   for (int kb = k0; kb < k1; kb += kSumInFlight) {
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   const int k1 = k0 + kScatterGroup < chunk_base[j + 1] ? k0 + kScatterGroup : chunk_base[j + 1];
   for (int col = lane * V; col < C; col += 32 * V) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    sum_partials(partials, k0, k1, C, col, acc, V);
+    sum_partials<8>(partials, k0, k1, C, col, acc, V);
     float* dst = partials1 + g * C + col;
 #pragma unroll
     for (int q = 0; q < V; ++q) dst[q] = acc[q];
@@ -330,10 +330,9 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 
 // ------------------------------------------------------------------------------------------
 // scatter (compact): out[j] = (keep_j + sum_c part_c) / normalizer_j
-//   kCB 16-byte vectors per lane are reduced per pass (kCB * 32 * V channels).
 // ------------------------------------------------------------------------------------------
-template <typename T, int kCB>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4)
     proj_scatter_kernel(const T* __restrict__ x, long long x_rows, long long xs, const int64_t* __restrict__ keep,
                         long long M, int corners, const int32_t* __restrict__ seg_offsets,
                         const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
@@ -341,7 +340,6 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
                         int C, const int32_t* __restrict__ chunk_base, const float* __restrict__ partials,
                         const int32_t* __restrict__ group_base, const float* __restrict__ partials1) {
   constexpr int V = Vec<T>::N;
-  constexpr int kChunk = kCB * 32 * V;  // channels per pass
   const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (j >= M) return;
@@ -374,7 +372,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int e = 0; e < V; ++e) acc[e] = kv[e];
-      sum_partials(src, k0, k1, C, col, acc, V);
+      sum_partials<2>(src, k0, k1, C, col, acc, V);
       float out_v[V];
 #pragma unroll
       for (int e = 0; e < V; ++e) out_v[e] = __fdiv_rn(acc[e], norm);
@@ -383,84 +381,52 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     return;
   }
 
-  for (int base = 0; base < C; base += kChunk) {
-    float acc[kCB][V];
+  // short row: one 16-byte vector of channels per lane per pass, kScatterInFlight source rows
+  // in flight; per corner an fp32 partial sum in entry order, added to the keep row in corner
+  // order, then divided by the normaliser
+  for (int col = lane * V; col < C; col += 32 * V) {
+    float acc[V];
+    if (krow != nullptr) {
+      load_vec<T>(krow + col, acc);
+    } else {
 #pragma unroll
-    for (int cb = 0; cb < kCB; ++cb) {
-      const int col = base + (cb * 32 + lane) * V;
-      if (krow != nullptr && col < C) {
-        load_vec<T>(krow + col, acc[cb]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < V; ++e) acc[cb][e] = 0.f;
-      }
+      for (int q = 0; q < V; ++q) acc[q] = 0.f;
     }
     for (int c = 0; c < corners; ++c) {
       const int e0 = seg[c], e1 = seg[c + 1];
       if (e0 == e1) continue;
-      float part[kCB][V];
+      float part[V];
 #pragma unroll
-      for (int cb = 0; cb < kCB; ++cb)
+      for (int q = 0; q < V; ++q) part[q] = 0.f;
+      for (int eb = e0; eb < e1; eb += kScatterInFlight) {
+        float v[kScatterInFlight][V];
+        float w[kScatterInFlight];
 #pragma unroll
-        for (int e = 0; e < V; ++e) part[cb][e] = 0.f;
-      int e = e0;
-      // two entries per step keeps 2*kCB vector loads in flight per lane
-      for (; e + 1 < e1; e += 2) {
-        int s0 = __ldg(entry_src + e), s1 = __ldg(entry_src + e + 1);
-        float w0 = __ldg(entry_w + e), w1 = __ldg(entry_w + e + 1);
-        if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-        if (s1 < 0 || s1 >= x_rows) { s1 = 0; w1 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-        float v0[kCB][V], v1[kCB][V];
-#pragma unroll
-        for (int cb = 0; cb < kCB; ++cb) {
-          const int col = base + (cb * 32 + lane) * V;
-          if (col < C) {
-            load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0[cb]);
-            load_vec<T>(x + static_cast<long long>(s1) * xs + col, v1[cb]);
+        for (int u = 0; u < kScatterInFlight; ++u) {
+          int su = 0;
+          w[u] = 0.f;
+          if (eb + u < e1) {
+            su = __ldg(entry_src + eb + u);
+            w[u] = __ldg(entry_w + eb + u);
+            if (su < 0 || su >= x_rows) { su = 0; w[u] = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
           }
+          load_vec<T>(x + static_cast<long long>(su) * xs + col, v[u]);
         }
 #pragma unroll
-        for (int cb = 0; cb < kCB; ++cb) {
-          const int col = base + (cb * 32 + lane) * V;
-          if (col < C) {
+        for (int u = 0; u < kScatterInFlight; ++u) {
+          if (eb + u < e1) {
 #pragma unroll
-            for (int q = 0; q < V; ++q) {
-              part[cb][q] = __fadd_rn(part[cb][q], __fmul_rn(w0, v0[cb][q]));
-              part[cb][q] = __fadd_rn(part[cb][q], __fmul_rn(w1, v1[cb][q]));
-            }
-          }
-        }
-      }
-      if (e < e1) {
-        int s0 = __ldg(entry_src + e);
-        float w0 = __ldg(entry_w + e);
-        if (s0 < 0 || s0 >= x_rows) { s0 = 0; w0 = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-#pragma unroll
-        for (int cb = 0; cb < kCB; ++cb) {
-          const int col = base + (cb * 32 + lane) * V;
-          if (col < C) {
-            float v0[V];
-            load_vec<T>(x + static_cast<long long>(s0) * xs + col, v0);
-#pragma unroll
-            for (int q = 0; q < V; ++q) part[cb][q] = __fadd_rn(part[cb][q], __fmul_rn(w0, v0[q]));
+            for (int q = 0; q < V; ++q) part[q] = __fadd_rn(part[q], __fmul_rn(w[u], v[u][q]));
           }
         }
       }
 #pragma unroll
-      for (int cb = 0; cb < kCB; ++cb)
-#pragma unroll
-        for (int q = 0; q < V; ++q) acc[cb][q] = __fadd_rn(acc[cb][q], part[cb][q]);
+      for (int q = 0; q < V; ++q) acc[q] = __fadd_rn(acc[q], part[q]);
     }
+    float o[V];
 #pragma unroll
-    for (int cb = 0; cb < kCB; ++cb) {
-      const int col = base + (cb * 32 + lane) * V;
-      if (col < C) {
-        float o[V];
-#pragma unroll
-        for (int q = 0; q < V; ++q) o[q] = __fdiv_rn(acc[cb][q], norm);
-        store_vec<T>(drow + col, o);
-      }
-    }
+    for (int q = 0; q < V; ++q) o[q] = __fdiv_rn(acc[q], norm);
+    store_vec<T>(drow + col, o);
   }
 }
 
@@ -1244,21 +1210,14 @@ extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int6
     }
     VB200_CHECK_LAUNCH("scatter_group_kernel");
   }
-#define VB200_SCATTER(T, CB)                                                                  \
-  proj_scatter_kernel<T, CB><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                  \
+#define VB200_SCATTER(T)                                                                      \
+  proj_scatter_kernel<T><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                      \
       static_cast<const T*>(x), x_rows, xs, keep, M, static_cast<int>(corners), seg_offsets, entry_src, \
       entry_w, normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials, group_base, \
       partials1)
-  if (dtype == VB200_F32) {
-    if (C <= 128) VB200_SCATTER(float, 1);
-    else VB200_SCATTER(float, 4);
-  } else if (dtype == VB200_BF16) {
-    if (C <= 256) VB200_SCATTER(__nv_bfloat16, 1);
-    else VB200_SCATTER(__nv_bfloat16, 4);
-  } else {
-    if (C <= 256) VB200_SCATTER(__half, 1);
-    else VB200_SCATTER(__half, 4);
-  }
+  if (dtype == VB200_F32) VB200_SCATTER(float);
+  else if (dtype == VB200_BF16) VB200_SCATTER(__nv_bfloat16);
+  else VB200_SCATTER(__half);
 #undef VB200_SCATTER
   VB200_CHECK_LAUNCH("proj_scatter_kernel");
   return VB200_OK;
