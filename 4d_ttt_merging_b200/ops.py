@@ -265,8 +265,10 @@ def deterministic_weighted_normalizer(parent_compact: torch.Tensor, weights: tor
     return csr.mass.view(1, kept_tokens, 1)
 
 
-def row_normalize_bf16(x: torch.Tensor, rows: torch.Tensor | None = None, eps: float = 1e-12) -> torch.Tensor:
-    """F.normalize(x[rows].float(), dim=-1, eps=eps).to(bfloat16) for a 2-D x."""
+def row_normalize_bf16(x: torch.Tensor, rows: torch.Tensor | None = None, eps: float = 1e-12,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """F.normalize(x[rows].float(), dim=-1, eps=eps).to(bfloat16) for a 2-D x; written into
+    ``out`` ([len(rows), C] bf16, unit channel stride, 16-byte aligned rows) when given."""
     C.require_cuda(x, "row_normalize_bf16")
     if x.ndim != 2:
         raise ValueError("row_normalize_bf16 expects a 2-D tensor")
@@ -275,7 +277,10 @@ def row_normalize_bf16(x: torch.Tensor, rows: torch.Tensor | None = None, eps: f
     R = x.shape[0] if rows is None else rows.numel()
     if rows is not None:
         rows = rows.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
-    out = torch.empty((R, x.shape[1]), device=x.device, dtype=torch.bfloat16)
+    if out is None:
+        out = torch.empty((R, x.shape[1]), device=x.device, dtype=torch.bfloat16)
+    elif out.shape != (R, x.shape[1]) or out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise ValueError(f"row_normalize_bf16: out must be [{R}, {x.shape[1]}] bf16 with unit channel stride")
     rc = C.lib().vb200_row_normalize_bf16(
         C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), C.ptr(rows), R, x.shape[1], float(eps),
         out.data_ptr(), out.stride(0), C.stream_of(x.device))

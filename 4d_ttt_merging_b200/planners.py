@@ -22,7 +22,7 @@ import math
 import torch
 
 from . import _clib as C
-from .ops import build_plan_csr, row_gather, row_normalize_bf16, similarity_topk
+from .ops import build_plan_csr, row_normalize_bf16, similarity_topk
 from .token_plan import TokenPlan, WeightedBilinearTokenPlan
 
 __all__ = ["build_fastvggt_plan", "build_uniform_convex_plan", "fastvggt_tables", "uniform_keep_layout"]
@@ -163,17 +163,18 @@ def build_uniform_convex_plan(tokens: torch.Tensor, *, frames: int, tokens_per_f
     lay = uniform_keep_layout(frames, tokens_per_frame, patch_token_start, merge_factor, group_frames)
     dl = _device_layout(lay, dev)
     x = tokens[0]
-    feat = row_normalize_bf16(x)  # one pass over all tokens; sources and keeps are rows of it
-    src_feat = row_gather(feat, dl["source"])
-    basis_feat = row_gather(feat, dl["keep"])
+    S, K = dl["source"].numel(), dl["keep"].numel()
+    # normalised features in one buffer, written in gathered order: rows [0, S) the sources,
+    # rows [S, S + K) the keeps (every token is read once; no separate gathers)
+    feat = row_normalize_bf16(x, dl["source_keep"])
+    src_feat, basis_feat = feat[:S], feat[S:]
     _, parent = similarity_topk(src_feat, basis_feat, 4, query_begin=lay["q_begin"], basis_begin=lay["b_begin"])
-    alpha = torch.empty((dl["source"].numel(), 4), device=dev, dtype=torch.float32)
-    parent_rows = dl["keep"][parent]  # token rows of the supports
+    alpha = torch.empty((S, 4), device=dev, dtype=torch.float32)
+    parent_rows = parent + S  # rows of the supports in feat
     rc = C.lib().vb200_support_fit(C.BF16, feat.data_ptr(), feat.shape[0], feat.stride(0),
-                                   dl["source"].data_ptr(), parent_rows.data_ptr(), dl["source"].numel(),
+                                   None, parent_rows.data_ptr(), S,
                                    feat.shape[1], None, None, alpha.data_ptr(), int(steps), C.stream_of(dev))
     C.check(rc, "support_fit")
-    K = dl["keep"].numel()
     csr = build_plan_csr(parent, alpha, K, src_rows=dl["source"])
     normalizer = csr.mass.view(1, K, 1)
     return WeightedBilinearTokenPlan(
@@ -195,5 +196,6 @@ def _device_layout(lay: dict, dev: torch.device) -> dict:
     hit = _DEVICE_LAYOUTS.get(key)
     if hit is None:
         hit = {k: lay[k].to(dev) for k in ("keep", "source", "special", "special_compact")}
+        hit["source_keep"] = torch.cat([hit["source"], hit["keep"]])  # feature-row order of the planner
         _DEVICE_LAYOUTS[key] = hit
     return hit
