@@ -347,19 +347,43 @@ def run_ours(args) -> None:
     total_ms = sum(step_ms)
 
     # ---- timed end-to-end steps through the public API (host buffers, copies inside) ----
-    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    # Pipelined as a serving loop would run it: step i+1's tokens are copied from pinned host
+    # memory on one stream and step i-1's output is copied back on another while step i
+    # computes (device input double-buffered).  Every step's host->device and device->host
+    # copy is inside the timed region; the L2 flush still precedes every step.
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    dbuf = [torch.empty_like(tokens) for _ in range(2)]
+    in_ready = [torch.cuda.Event() for _ in range(args.steps)]
+    done = [torch.cuda.Event() for _ in range(args.steps)]
+    e2e_0, e2e_1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    e2e_0.record(comp)
+    s_in.wait_event(e2e_0)
+    with torch.cuda.stream(s_in):
+        dbuf[0][0].copy_(host_in, non_blocking=True)
+        in_ready[0].record(s_in)
     for i in range(args.steps):
+        if i + 1 < args.steps:
+            with torch.cuda.stream(s_in):
+                if i >= 1:
+                    s_in.wait_event(done[i - 1])  # step i-1 has finished reading this buffer
+                dbuf[(i + 1) % 2][0].copy_(host_in, non_blocking=True)
+                in_ready[i + 1].record(s_in)
         flush.zero_()
-        ev2[i][0].record()
-        t_in = host_in.to(dev, non_blocking=True)[None]
-        out = block.step(t_in)
-        host_out.copy_(out[0], non_blocking=True)
-        ev2[i][1].record()
+        comp.wait_event(in_ready[i])
+        out = block.step(dbuf[i % 2])
+        done[i].record(comp)
+        s_out.wait_event(done[i])
+        with torch.cuda.stream(s_out):
+            host_out.copy_(out[0], non_blocking=True)
+        out.record_stream(s_out)
+    comp.wait_stream(s_out)
+    e2e_1.record(comp)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
+    e2e_ms = e2e_0.elapsed_time(e2e_1)
 
     if world > 1:
         t = torch.tensor([total_ms, e2e_ms], device=dev, dtype=torch.float64)
@@ -409,7 +433,10 @@ def run_ours(args) -> None:
         "clocks": clocks.summary(),
         "e2e": {"value": FRAMES * args.steps / (e2e_ms / 1e3), "unit": "frames/s",
                 "h2d_bytes_per_step": FRAMES * TOKENS_PER_FRAME * DIM * 2,
-                "d2h_bytes_per_step": FRAMES * TOKENS_PER_FRAME * DIM * 2},
+                "d2h_bytes_per_step": FRAMES * TOKENS_PER_FRAME * DIM * 2,
+                "pipelined": "h2d of step i+1 and d2h of step i-1 overlap step i (copy streams, "
+                             "double-buffered device input); the first h2d and last d2h are inside the "
+                             "timed region"},
         "gpu_launches": int(launches),
     }
     if world == 1:
