@@ -101,7 +101,26 @@ AssignWorkspace assign_layout(int64_t S, int64_t total) {
 // accumulated in fp32 over the channels (lane-strided, then a fixed butterfly).  With steps > 0
 // the block's kFitWarps systems go through shared memory to warp 0, whose lanes run the
 // projected-gradient solves side by side (one source per lane) instead of one lane per warp.
-constexpr int kFitWarps = 16;
+constexpr int kFitWarps = 8;
+__constant__ int kFitPairI[10] = {0, 0, 0, 0, 1, 1, 1, 2, 2, 3};  // Gram entry (i, j), i <= j, row-major
+__constant__ int kFitPairJ[10] = {0, 1, 2, 3, 1, 2, 3, 2, 3, 3};
+
+// A 32-bit word of two 16-bit values as an fp32 pair (low half first).
+template <typename T>
+__device__ __forceinline__ uint64_t widen2(uint32_t w);
+template <>
+__device__ __forceinline__ uint64_t widen2<__nv_bfloat16>(uint32_t w) {
+  return pk2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ uint64_t widen2<__half>(uint32_t w) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+  return pk2(f.x, f.y);
+}
+template <>
+__device__ __forceinline__ uint64_t widen2<float>(uint32_t w) {
+  return pk2(__uint_as_float(w), 0.f);  // unused: fp32 features take the scalar path
+}
 template <typename T>
 __global__ void __launch_bounds__(kFitWarps * 32)
     support_fit_kernel(const T* __restrict__ feat, long long rows, long long fs,
@@ -125,56 +144,103 @@ __global__ void __launch_bounds__(kFitWarps * 32)
       if (r[c] < 0 || r[c] >= rows) { bad = true; r[c] = 0; }
     }
     if (bad && lane == 0) atomicOr(&g_plan_err, kErrBadArgument);
-    // products: g[i][j] for i <= j (10) + rhs[i] (4)
-    float acc[14];
+    // products: g[i][j] for i <= j (10) + rhs[i] (4), accumulated per lane in fp32
+    float acc[16];
 #pragma unroll
-    for (int i = 0; i < 14; ++i) acc[i] = 0.f;
-    for (int v0 = lane * V; v0 < D; v0 += 32 * V) {
-      float x[5][V];
+    for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+    if constexpr (sizeof(T) == 2) {
+      // 16-bit features: each 32-bit word is widened to an fp32 pair and the 14 products are
+      // packed FMAs on (even, odd) channel pairs; the two halves are added at the end
+      uint64_t acc2[14];
 #pragma unroll
-      for (int c = 0; c < 5; ++c) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(feat + r[c] * fs + v0));
-        const T* e = reinterpret_cast<const T*>(&raw);
+      for (int i = 0; i < 14; ++i) acc2[i] = 0ull;
+      for (int v0 = lane * V; v0 < D; v0 += 32 * V) {
+        uint4 raw[5];
 #pragma unroll
-        for (int q = 0; q < V; ++q) x[c][q] = to_f32<T>(e[q]);
+        for (int c = 0; c < 5; ++c) raw[c] = __ldg(reinterpret_cast<const uint4*>(feat + r[c] * fs + v0));
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          uint64_t x[5];
+#pragma unroll
+          for (int c = 0; c < 5; ++c) x[c] = widen2<T>(reinterpret_cast<const uint32_t*>(&raw[c])[h]);
+          int idx = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = i; j < 4; ++j) {
+              acc2[idx] = ffma2(x[i + 1], x[j + 1], acc2[idx]);
+              ++idx;
+            }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc2[10 + i] = ffma2(x[i + 1], x[0], acc2[10 + i]);
+        }
       }
 #pragma unroll
-      for (int q = 0; q < V; ++q) {
-        int idx = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = i; j < 4; ++j) {
-            acc[idx] = fmaf(x[i + 1][q], x[j + 1][q], acc[idx]);
-            ++idx;
-          }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[10 + i] = fmaf(x[i + 1][q], x[0][q], acc[10 + i]);
+      for (int i = 0; i < 14; ++i) {
+        float lo, hi;
+        upk2(acc2[i], lo, hi);
+        acc[i] = lo + hi;
       }
-    }
+    } else {
+      for (int v0 = lane * V; v0 < D; v0 += 32 * V) {
+        float x[5][V];
 #pragma unroll
-    for (int i = 0; i < 14; ++i)
+        for (int c = 0; c < 5; ++c) {
+          const uint4 raw = __ldg(reinterpret_cast<const uint4*>(feat + r[c] * fs + v0));
+          const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], off);
-    if (lane == 0) {
-      int idx = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = i; j < 4; ++j) {
-          sys[warp][i * 4 + j] = acc[idx];
-          sys[warp][j * 4 + i] = acc[idx];
-          ++idx;
+          for (int q = 0; q < V; ++q) x[c][q] = to_f32<T>(e[q]);
         }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sys[warp][16 + i] = acc[10 + i];
+        for (int q = 0; q < V; ++q) {
+          int idx = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = i; j < 4; ++j) {
+              acc[idx] = fmaf(x[i + 1][q], x[j + 1][q], acc[idx]);
+              ++idx;
+            }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[10 + i] = fmaf(x[i + 1][q], x[0][q], acc[10 + i]);
+        }
+      }
+    }
+    // Transposing warp reduction of the 16 (14 used) values: each xor step halves the values a
+    // lane holds while summing over the partner lane, so lane L ends with the full sum of
+    // value (L >> 1) in 16 shuffles instead of 14 x 5.
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = acc[i];
+#pragma unroll
+    for (int n = 8; n >= 1; n >>= 1) {
+      const bool upper = (lane & (2 * n)) != 0;
+#pragma unroll
+      for (int i = 0; i < n; ++i) {
+        const float send = upper ? v[i] : v[i + n];
+        const float keep = upper ? v[i + n] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2 * n);
+      }
+    }
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+    const int vidx = lane >> 1;  // the value this lane now holds
+    if ((lane & 1) == 0 && vidx < 14) {
+      if (vidx < 10) {
+        sys[warp][kFitPairI[vidx] * 4 + kFitPairJ[vidx]] = v[0];
+        sys[warp][kFitPairJ[vidx] * 4 + kFitPairI[vidx]] = v[0];
+      } else {
+        sys[warp][16 + vidx - 10] = v[0];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
       if (gram) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) gram[s * 16 + i] = sys[warp][i];
       }
       if (rhs) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) rhs[s * 4 + i] = acc[10 + i];
+        for (int i = 0; i < 4; ++i) rhs[s * 4 + i] = sys[warp][16 + i];
       }
     }
   }  // s < S
