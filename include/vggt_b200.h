@@ -120,8 +120,9 @@ VB200_API int vb200_plan_csr_build(const int64_t* parent, const float* weights, 
 /* ---- a4: top-4 scatter-accumulate (tokens -> merged) ----------------------------------------
  * out[j] = (x[keep[j]] + sum_c sum_{e in seg(j,c)} w_e * x[entry_src[e]]) / normalizer[j]
  * accumulated in fp32 (each product rounded to fp32, corner partial sums added in corner
- * order; the entries of a merged row with more than 128 of them are summed in 128-entry chunks,
- * chunk sums added in chunk order), written in `dtype`.  keep may be NULL (hard-merge mean pooling: the accumulator
+ * order; the entries of a merged row with more than 256 of them are summed as a fixed two-level
+ * tree: 256-entry chunk sums, then sums of 64 consecutive chunk sums, added in order), written
+ * in `dtype`.  keep may be NULL (hard-merge mean pooling: the accumulator
  * starts at zero).  Row strides in elements; C % 8 == 0 for 16-bit types, C % 4 for fp32;
  * rows 16-byte aligned.  Rows of x outside [0, x_rows) referenced by keep or entry_src set
  * device error bit 1 and are skipped (keep: the accumulator starts at zero).
@@ -134,9 +135,10 @@ VB200_API int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64
                        int64_t out_row_stride, int64_t C, int64_t n_entries, void* workspace,
                        size_t workspace_bytes, void* stream);
 /* Scratch of vb200_proj_scatter for M merged rows, n_entries CSR entries (the length of
- * entry_src) and C channels.  Merged rows with more than 128 entries (skewed plans) are split
- * into 128-entry chunks whose fp32 sums are added to the keep row in chunk order; the scratch
- * holds those sums (at most 2 * n_entries / 128 + 1 chunks of C floats). */
+ * entry_src) and C channels.  Merged rows with more than 256 entries (skewed plans) are split
+ * into 256-entry chunks and groups of 64 chunks; the scratch holds the fp32 chunk and group
+ * sums (at most 2 * ceil(n_entries / 256) + 1 chunks and 2 * ceil(chunks / 64) + 1 groups of
+ * C floats) plus the scan arrays that place them. */
 VB200_API size_t vb200_proj_scatter_workspace_size(int64_t M, int64_t n_entries, int64_t C);
 
 /* ---- a4 + q/k norm fused: Q||K||V compaction of the qkv projection ---------------------------
