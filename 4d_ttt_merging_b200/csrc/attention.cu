@@ -58,6 +58,9 @@ constexpr float kRescaleThreshold = 8.0f;  // lazy rescale: P stays <= 2^8
 // take issue slots from the MMA warp.
 constexpr int kPolyPairs = 2;
 constexpr int kNamedBarPair = 1;  // named barriers 1, 2: the two warpgroups of query tile 0, 1
+constexpr int kNamedBarSoftmax = 3;  // all softmax warps (the split epilogue)
+// Key-range split of the last partial wave: at most this many pieces per (query block, head).
+constexpr int kMaxSplit = 4;
 
 // Shared-memory layout (offsets from a 1024-byte aligned base).
 constexpr int kOffQ = 0;                                  // kQT tiles
@@ -81,11 +84,21 @@ constexpr uint32_t kTmemP = 256;
 constexpr uint32_t kTmemO = 384;
 static_assert(kStageStride >= 2 * kTileBytes + kKxBytes && kStageStride % 1024 == 0, "stage layout");
 
+// Work items are (query block, batch*head) pairs, numbered query block fastest.  CTA c < n_full
+// runs item c over all key tiles.  When the items do not fill whole waves of the GPU, the
+// remaining items (n_full, n_full + 1, ...) are each split into `split` key ranges run by
+// `split` CTAs; every piece writes its unnormalised O, running max and sum to o_part / ml_part,
+// and the piece that finishes last (counted in counters[item - n_full]) merges all pieces in
+// piece order and writes the output.
 struct AttnParams {
   const uint8_t* kx;  // [n_tiles][kKxBytes] extra K chunks (8 * bias, masked past Nk)
   void* out;
   long long o_sb, o_sh, o_sn;  // element strides
   int H, Nq, Nk, n_tiles;
+  int qblocks, n_full, split;
+  float* o_part;          // [tail items][split][kQT][kBM][kHD]
+  float2* ml_part;        // [tail items][split][kQT][kBM]: (running max, running sum)
+  unsigned* counters;     // [tail items], zeroed by prepare_kx_kernel before every launch
   float scale_log2;  // log2(e) / sqrt(64)
 };
 
@@ -183,11 +196,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_block = blockIdx.x;  // kQT * kBM query rows
-  const int bh = blockIdx.y;
+  // this CTA's work item and key-tile range [kt0, kt0 + n_tiles)
+  const int cta = static_cast<int>(blockIdx.x);
+  const bool piece_cta = cta >= p.n_full;
+  int item = cta, piece = 0, kt0 = 0, kt1 = p.n_tiles;
+  if (piece_cta) {
+    const int k = (cta - p.n_full) / p.split;
+    piece = cta - p.n_full - k * p.split;
+    item = p.n_full + k;
+    kt0 = static_cast<int>(static_cast<long long>(piece) * p.n_tiles / p.split);
+    kt1 = static_cast<int>(static_cast<long long>(piece + 1) * p.n_tiles / p.split);
+  }
+  const int q_block = item % p.qblocks;  // kQT * kBM query rows
+  const int bh = item / p.qblocks;
   const int batch = bh / p.H;
   const int head = bh - batch * p.H;
-  const int n_tiles = p.n_tiles;
+  const int n_tiles = kt1 - kt0;
   auto bar = [=](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffTmemSlot + 8);
 
@@ -248,9 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t st = sbase + kOffStage + s * kStageStride;
         mbar_arrive_expect_tx(bar(kBarKVFull + s), 2 * kTileBytes + kKxBytes);
-        tma_load_4d(st, &tmap_k, bar(kBarKVFull + s), 0, j * kBN, head, batch);
-        tma_load_4d(st + kTileBytes, &tmap_v, bar(kBarKVFull + s), 0, j * kBN, head, batch);
-        bulk_load(st + 2 * kTileBytes, p.kx + static_cast<size_t>(j) * kKxBytes, kKxBytes, bar(kBarKVFull + s));
+        tma_load_4d(st, &tmap_k, bar(kBarKVFull + s), 0, (kt0 + j) * kBN, head, batch);
+        tma_load_4d(st + kTileBytes, &tmap_v, bar(kBarKVFull + s), 0, (kt0 + j) * kBN, head, batch);
+        bulk_load(st + 2 * kTileBytes, p.kx + static_cast<size_t>(kt0 + j) * kKxBytes, kKxBytes,
+                  bar(kBarKVFull + s));
       }
       if (!ok) *abort_flag = 1;
     }
@@ -291,24 +316,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int j = 0; j < n_tiles && ok; ++j) {
       if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-      if (j + 1 < n_tiles) {
-        ok = wait_all(kBarKVFull + (j + 1) % kStages, ((j + 1) / kStages) & 1);
-        for (int t = 0; t < kQT && ok; ++t) {
-          // S_t(j) has been read into registers: overwrite it with the next tile's scores
-          ok = wait_all(kBarSFree + t, j & 1);
-          if (ok) {
-            tc_fence_after();
-            issue_qk(t, j + 1);
-          }
-        }
-        if (!ok) break;
-      }
+      if (j + 1 < n_tiles) ok = wait_all(kBarKVFull + (j + 1) % kStages, ((j + 1) / kStages) & 1);
+      // Per query tile: the next scores as soon as S_t(j) is in registers, then O_t += P_t V_j.
+      // Tile by tile (QK_0, PV_0, QK_1, PV_1) measured 2-7% faster than both QKs first.
       for (int t = 0; t < kQT && ok; ++t) {
-        ok = wait_all(kBarPFull + t, j & 1);
-        if (ok) {
+        if (j + 1 < n_tiles) {
+          ok = wait_all(kBarSFree + t, j & 1);
+          if (!ok) break;
           tc_fence_after();
-          issue_pv(t, j);
+          issue_qk(t, j + 1);
         }
+        ok = wait_all(kBarPFull + t, j & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(t, j);
       }
     }
     if (!ok && lane == 0) *abort_flag = 1;
@@ -435,17 +456,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(bar(kBarODone + t), (n_tiles - 1) & 1, &g_attn_err);
       ok = __all_sync(0xffffffffu, ok);
     }
+    uint32_t o[kHD / 2];
     if (ok) {
       tc_fence_after();
-      uint32_t o[kHD / 2];
       tmem_ld32x32b_x32_nowait(o_addr, o);
       tmem_wait_ld();
       reg_fence32(o);
-      const int grow = (q_block * kQT + t) * kBM + row;
-      if (grow < p.Nq) {
+    }
+    const int grow = (q_block * kQT + t) * kBM + row;
+    const long long orow_off = batch * p.o_sb + head * p.o_sh + static_cast<long long>(grow) * p.o_sn + h * (kHD / 2);
+    if (!piece_cta) {
+      if (ok && grow < p.Nq) {
         const float inv = 1.f / l_tot;
-        uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
-                        2 * (batch * p.o_sb + head * p.o_sh + static_cast<long long>(grow) * p.o_sn + h * (kHD / 2));
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) + 2 * orow_off;
 #pragma unroll
         for (int c = 0; c < kHD / 16; ++c) {
           uint4 w;
@@ -456,6 +479,87 @@ __global__ void __launch_bounds__(kThreads, 1)
             wp[i] = kBF16 ? pack_bf16x2(a, b2) : pack_f16x2(a, b2);
           }
           *reinterpret_cast<uint4*>(orow + c * 16) = w;
+        }
+      }
+    } else {
+      // One key range of a split item: publish (O, m, l) of this piece, then the piece that
+      // arrives last merges all pieces in piece order (deterministic for any arrival order).
+      const long long slot0 = static_cast<long long>(item - p.n_full) * p.split;
+      const long long rowi = (slot0 + piece) * kQT * kBM + t * kBM + row;  // this piece's row record
+      if (ok) {
+        float4* dst = reinterpret_cast<float4*>(p.o_part + rowi * kHD + h * (kHD / 2));
+#pragma unroll
+        for (int i = 0; i < kHD / 8; ++i)
+          dst[i] = make_float4(u2f(o[4 * i]), u2f(o[4 * i + 1]), u2f(o[4 * i + 2]), u2f(o[4 * i + 3]));
+        if (h == 0) p.ml_part[rowi] = make_float2(m_run, l_tot);
+      }
+      __threadfence();
+      named_bar_sync(kNamedBarSoftmax, kSoftmaxWarps * 32);
+      volatile int* last_flag = abort_flag + 1;
+      if (threadIdx.x == 0) *last_flag = atomicAdd(p.counters + (item - p.n_full), 1u) == static_cast<unsigned>(p.split - 1);
+      named_bar_sync(kNamedBarSoftmax, kSoftmaxWarps * 32);
+      if (*last_flag && ok && grow < p.Nq) {
+        __threadfence();
+        const long long stride = static_cast<long long>(kQT) * kBM;  // row records between pieces
+        const long long row0 = slot0 * stride + t * kBM + row;       // piece 0's record of this row
+        // Loads are unrolled over the pieces so that each group goes out together (one L2
+        // round trip per group instead of one per piece).
+        float w[kMaxSplit];
+        float m_star = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < kMaxSplit; ++q) {
+          w[q] = 0.f;
+          if (q < p.split) {
+            const float2 ml = __ldcg(&p.ml_part[row0 + q * stride]);
+            w[q] = ml.x;  // running max for now
+            m_star = fmaxf(m_star, ml.x);
+          }
+        }
+        float l_sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < kMaxSplit; ++q) {
+          if (q < p.split) {
+            w[q] = exp2f(w[q] - m_star);
+            l_sum = fmaf(w[q], __ldcg(&p.ml_part[row0 + q * stride]).y, l_sum);
+          }
+        }
+        const float inv = 1.f / l_sum;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) + 2 * orow_off;
+#pragma unroll 1
+        for (int c = 0; c < kHD / 2; c += 8) {  // 8 output columns at a time
+          float4 x[kMaxSplit][2];
+#pragma unroll
+          for (int q = 0; q < kMaxSplit; ++q) {
+            if (q < p.split) {
+              const float4* src = reinterpret_cast<const float4*>(p.o_part + (row0 + q * stride) * kHD + h * (kHD / 2) + c);
+              x[q][0] = __ldcg(src);
+              x[q][1] = __ldcg(src + 1);
+            }
+          }
+          float acc[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+          for (int q = 0; q < kMaxSplit; ++q) {
+            if (q < p.split) {
+              acc[0] = fmaf(w[q], x[q][0].x, acc[0]);
+              acc[1] = fmaf(w[q], x[q][0].y, acc[1]);
+              acc[2] = fmaf(w[q], x[q][0].z, acc[2]);
+              acc[3] = fmaf(w[q], x[q][0].w, acc[3]);
+              acc[4] = fmaf(w[q], x[q][1].x, acc[4]);
+              acc[5] = fmaf(w[q], x[q][1].y, acc[5]);
+              acc[6] = fmaf(w[q], x[q][1].z, acc[6]);
+              acc[7] = fmaf(w[q], x[q][1].w, acc[7]);
+            }
+          }
+          uint4 wv;
+          uint32_t* wp = reinterpret_cast<uint32_t*>(&wv);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float a = acc[2 * i] * inv, b2 = acc[2 * i + 1] * inv;
+            wp[i] = kBF16 ? pack_bf16x2(a, b2) : pack_f16x2(a, b2);
+          }
+          *reinterpret_cast<uint4*>(orow + 2 * c) = wv;
         }
       }
     }
@@ -490,10 +594,13 @@ __global__ void prepare_bias_kernel(const TB* log_mass, float* bias, int Nk, int
 // Extra K chunks of the tensor-core path, one 4 KB tile per 128 keys in the no-swizzle K-major
 // layout [16 row groups][2 K halves][8 rows][8 elements]: column 0 of key row j holds
 // 8 * round_to_dtype(log_mass[j]) (0 without a bias), keys past Nk hold a large negative value
-// (their exponential underflows to 0), every other element is 0.
+// (their exponential underflows to 0), every other element is 0.  Also zeroes the arrival
+// counters of the split items (n_counters <= total).
 template <typename TB, typename TQ>
-__global__ void prepare_kx_kernel(const TB* log_mass, TQ* kx, int Nk, long long total) {
+__global__ void prepare_kx_kernel(const TB* log_mass, TQ* kx, int Nk, long long total, unsigned* counters,
+                                  int n_counters) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx < n_counters) counters[idx] = 0u;
   if (idx >= total) return;
   const long long tile = idx >> 11;
   const int rem = static_cast<int>(idx & 2047);
@@ -614,6 +721,69 @@ extern "C" size_t vb200_mass_bias_attention_workspace_size(int64_t Nk) {
 
 namespace {
 
+// How the tensor-core launch divides its work items over the GPU (see AttnParams).
+struct SplitPlan {
+  long long items = 0, n_full = 0, n_tail = 0;
+  int split = 1;
+  size_t o_bytes = 0, ml_bytes = 0, cnt_bytes = 0;  // partial-result regions of the workspace
+};
+
+int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+  if (dev < 64 && cached[dev] > 0) return cached[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+// The kernel runs one CTA per SM, so `items` CTAs take ceil(items / SMs) waves and the last
+// wave leaves SMs idle.  Splitting each of the last wave's items into s key ranges turns that
+// wave into ceil(tail * s / SMs) rounds of 1/s of an item (plus a per-CTA ramp of about three
+// key tiles); s is the cheapest choice up to kMaxSplit.
+SplitPlan plan_split(long long B, long long H, long long Nq, int n_tiles, int n_sm) {
+  SplitPlan sp;
+  const long long qblocks = (Nq + kQT * kBM - 1) / (kQT * kBM);
+  sp.items = qblocks * B * H;
+  sp.n_full = sp.items;
+  if (n_sm <= 0 || n_tiles < 2 || sp.items <= 0) return sp;
+  const long long tail = sp.items % n_sm;
+  if (tail == 0) return sp;
+  const double ramp = 3.0 / n_tiles;
+  double best = 1.0 + ramp;
+  int best_s = 1;
+  for (int s = 2; s <= kMaxSplit && s <= n_tiles; ++s) {
+    const long long rounds = (tail * s + n_sm - 1) / n_sm;
+    const double cost = static_cast<double>(rounds) * (1.0 / s + ramp);
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  if (best_s == 1) return sp;
+  sp.split = best_s;
+  sp.n_tail = tail;
+  sp.n_full = sp.items - tail;
+  const size_t rows = static_cast<size_t>(tail) * best_s * kQT * kBM;
+  sp.o_bytes = align_up(rows * kHD * sizeof(float), 256);
+  sp.ml_bytes = align_up(rows * sizeof(float2), 256);
+  sp.cnt_bytes = align_up(static_cast<size_t>(tail) * sizeof(unsigned), 256);
+  return sp;
+}
+
+}  // namespace
+
+extern "C" size_t vb200_mass_bias_attention_split_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t Nk) {
+  const size_t base = vb200_mass_bias_attention_workspace_size(Nk);
+  if (B < 1 || H < 1 || Nq < 1 || Nk < 1) return base;
+  const SplitPlan sp = plan_split(B, H, Nq, static_cast<int>((Nk + kBN - 1) / kBN), sm_count());
+  return base + sp.o_bytes + sp.ml_bytes + sp.cnt_bytes;
+}
+
+namespace {
+
 int launch_bias(int dtype, const void* log_mass, int bias_dtype, float* bias, int Nk, int padded,
                 cudaStream_t st) {
   const dim3 grid((padded + 255) / 256), block(256);
@@ -638,11 +808,13 @@ int launch_bias(int dtype, const void* log_mass, int bias_dtype, float* bias, in
   return VB200_OK;
 }
 
-int launch_kx(int dtype, const void* log_mass, int bias_dtype, void* kx, int Nk, int n_tiles, cudaStream_t st) {
+int launch_kx(int dtype, const void* log_mass, int bias_dtype, void* kx, int Nk, int n_tiles, unsigned* counters,
+              int n_counters, cudaStream_t st) {
   const long long total = static_cast<long long>(n_tiles) * (kKxBytes / 2);
   const dim3 grid(static_cast<unsigned>((total + 255) / 256)), block(256);
-#define VB200_KX_CASE(TB, TQ) \
-  prepare_kx_kernel<TB, TQ><<<grid, block, 0, st>>>(static_cast<const TB*>(log_mass), static_cast<TQ*>(kx), Nk, total)
+#define VB200_KX_CASE(TB, TQ)                                                                                     \
+  prepare_kx_kernel<TB, TQ><<<grid, block, 0, st>>>(static_cast<const TB*>(log_mass), static_cast<TQ*>(kx), Nk, total, \
+                                                    counters, n_counters)
   if (bias_dtype == VB200_F32) {
     if (dtype == VB200_BF16) VB200_KX_CASE(float, __nv_bfloat16);
     else VB200_KX_CASE(float, __half);
@@ -722,7 +894,17 @@ extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k
   VB200_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15u) == 0 && os[0] % 8 == 0 && os[1] % 8 == 0 &&
                     os[2] % 8 == 0,
                 "output rows must be 16-byte aligned");
-  rc = launch_kx(dtype, log_key_mass, bias_dtype, workspace, static_cast<int>(Nk), n_tiles, st);
+  // Split the last partial wave when the workspace holds the partial results (see AttnParams).
+  SplitPlan sp = plan_split(B, H, Nq, n_tiles, sm_count());
+  if (sp.split > 1 && workspace_bytes < need + sp.o_bytes + sp.ml_bytes + sp.cnt_bytes) {
+    sp.split = 1;
+    sp.n_full = sp.items;
+    sp.n_tail = 0;
+  }
+  uint8_t* part = static_cast<uint8_t*>(workspace) + need;
+  unsigned* counters = sp.split > 1 ? reinterpret_cast<unsigned*>(part + sp.o_bytes + sp.ml_bytes) : nullptr;
+  rc = launch_kx(dtype, log_key_mass, bias_dtype, workspace, static_cast<int>(Nk), n_tiles, counters,
+                 static_cast<int>(sp.n_tail), st);
   if (rc != VB200_OK) return rc;
   CUtensorMap tq, tk, tv;
   if ((rc = make_qkv_map(&tq, q, dtype, Nq, H, B, qs)) != VB200_OK) return rc;
@@ -739,8 +921,15 @@ extern "C" int vb200_mass_bias_attention(int dtype, const void* q, const void* k
   prm.Nq = static_cast<int>(Nq);
   prm.Nk = static_cast<int>(Nk);
   prm.n_tiles = n_tiles;
+  prm.qblocks = static_cast<int>((Nq + kQT * kBM - 1) / (kQT * kBM));
+  prm.n_full = static_cast<int>(sp.n_full);
+  prm.split = sp.split;
+  prm.o_part = sp.split > 1 ? reinterpret_cast<float*>(part) : nullptr;
+  prm.ml_part = sp.split > 1 ? reinterpret_cast<float2*>(part + sp.o_bytes) : nullptr;
+  prm.counters = counters;
   prm.scale_log2 = scale_log2;
-  const dim3 grid(static_cast<unsigned>((Nq + kQT * kBM - 1) / (kQT * kBM)), static_cast<unsigned>(B * H));
+  VB200_REQUIRE(sp.n_full + sp.n_tail * sp.split < (1ll << 31), "too many work items");
+  const dim3 grid(static_cast<unsigned>(sp.n_full + sp.n_tail * sp.split));
   // The register split inside the kernel is only valid with exactly kLaunchRegs registers per
   // thread at launch: refuse to launch anything else.
   {

@@ -73,7 +73,7 @@ def mass_bias_attention_into(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         bias = bias.contiguous()
         bias_dt = C.dtype_code(bias.dtype)
     lib = C.lib()
-    ws_bytes = lib.vb200_mass_bias_attention_workspace_size(Nk)
+    ws_bytes = lib.vb200_mass_bias_attention_split_workspace_size(B, H, Nq, Nk)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     rc = lib.vb200_mass_bias_attention(
         dt, q.data_ptr(), k.data_ptr(), v.data_ptr(), C.ptr(bias), bias_dt, out.data_ptr(),

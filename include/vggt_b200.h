@@ -64,6 +64,14 @@ VB200_API int vb200_device_error_flags(unsigned* flags, int clear);
  *   128-key tile: the bias operand of the QK product, or the padded fp32 bias of the fp32
  *   path), 256-byte aligned. */
 VB200_API size_t vb200_mass_bias_attention_workspace_size(int64_t Nk);
+/* Workspace that also lets the tensor-core launch split its last, partially filled wave of
+ * (256-query block, head) items into key ranges on the current device: the bytes above plus
+ * fp32 partial results (O, running max and sum) of the split items and their arrival
+ * counters.  The split pieces are merged in a fixed order, so results do not depend on
+ * timing; they can differ from the unsplit launch in the last fp32 bits before rounding.
+ * With a workspace of vb200_mass_bias_attention_workspace_size(Nk) bytes the launch runs
+ * unsplit. */
+VB200_API size_t vb200_mass_bias_attention_split_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t Nk);
 VB200_API int vb200_mass_bias_attention(int dtype, const void* q, const void* k, const void* v,
                               const void* log_key_mass, int bias_dtype, void* out, int64_t B,
                               int64_t H, int64_t Nq, int64_t Nk, int64_t D,

@@ -129,3 +129,46 @@ def test_exp2_polynomial_against_exact(pkg, cuda_device):
     rel = ((got[main] - exact[main]).abs() / exact[main]).max().item()
     assert rel <= 1e-4, rel
     assert torch.all(got[~main] >= 0) and torch.all(got[~main] < 1e-37)
+
+
+def _abi_call(pkg, qt, kt, vt, lm, out, ws_bytes):
+    """One launch through the C ABI with a workspace of ws_bytes."""
+    import ctypes
+    lib = pkg.load_library()
+    i64x3 = ctypes.c_int64 * 3
+    st = lambda t: i64x3(*t.stride()[:3])  # noqa: E731
+    B, H, Nq, _ = qt.shape
+    Nk = kt.shape[2]
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=qt.device)
+    rc = lib.vb200_mass_bias_attention(1, qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), lm.data_ptr(), 0,
+                                       out.data_ptr(), B, H, Nq, Nk, 64, st(qt), st(kt), st(vt), st(out),
+                                       ws.data_ptr(), ws_bytes, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.vb200_last_error()
+    torch.cuda.synchronize()
+    return out.clone()
+
+
+def test_split_last_wave(pkg, oracle, cuda_device):
+    """More (query block, head) items than one wave of SMs, with a partial last wave: that
+    wave's items run as key-range pieces merged by the last piece to finish.  The result
+    matches the oracle, is bit-identical from run to run (fixed merge order), and agrees with
+    the unsplit launch (workspace without room for the pieces) to within bf16 rounding."""
+    B, H, Nq, Nk = 1, 16, 2600, 1100  # 11 query blocks x 16 heads = 176 items, 9 key tiles
+    q, k, v, lm = _inputs(23, B, H, Nq, Nk, "bf16", oracle)
+    qt, kt, vt = (torch.from_numpy(t).to(cuda_device, torch.bfloat16) for t in (q, k, v))
+    lmt = torch.from_numpy(lm).to(cuda_device)
+    lib = pkg.load_library()
+    base = lib.vb200_mass_bias_attention_workspace_size(Nk)
+    full = lib.vb200_mass_bias_attention_split_workspace_size(B, H, Nq, Nk)
+    assert full > base  # 176 items leave a partial wave on a 148-SM B200
+    out = torch.empty(B, Nq, H, 64, device=cuda_device, dtype=torch.bfloat16).transpose(1, 2)
+    split1 = _abi_call(pkg, qt, kt, vt, lmt, out, full)
+    split2 = _abi_call(pkg, qt, kt, vt, lmt, out, full)
+    plain = _abi_call(pkg, qt, kt, vt, lmt, out, base)
+    assert torch.equal(split1, split2)
+    ref = oracle.mass_bias_attention(q, k, v, lm, dtype="bf16", round_p=True)
+    assert_close(to_np(split1), ref, "bf16")
+    assert_close(to_np(plain), ref, "bf16")
+    diff = (split1.float() - plain.float()).abs().max().item()
+    assert diff <= 2.0 ** -6 * plain.float().abs().max().item(), diff
+    assert pkg.device_error_flags() == 0
