@@ -23,7 +23,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-__all__ = ["FrameShard", "frame_shard", "gather_merged", "PeerExchange", "ShardedGlobalBlock"]
+__all__ = ["FrameShard", "frame_shard", "gather_merged", "PeerExchange", "ShardedGlobalBlock", "StepGraph"]
 
 
 @dataclass(frozen=True)
@@ -227,3 +227,49 @@ class ShardedGlobalBlock:
         out = plan.restore(y)
         self._end(e)
         return out
+
+
+class StepGraph:
+    """One `ShardedGlobalBlock.step` over a fixed input buffer, recorded as a CUDA graph.
+
+    A step is some twenty kernels, several of them only a few microseconds long on a rank's
+    share of the frames; launched one by one from Python the host becomes the bottleneck and
+    the GPU idles between kernels.  Replaying the recorded graph submits the whole step at
+    once.  The caller refills `tokens` (same shape, dtype and address) before each `replay()`;
+    the result lands in `out`, a buffer owned by the graph that the next replay overwrites.
+
+    Recording runs `warmup` eager steps first on a side stream (they create the cuBLAS handle,
+    the peer-exchange buffers, cached plan tables), then records one step.  With world > 1
+    every rank must construct its StepGraph at the same point: the recorded step contains the
+    exchange's cross-GPU barriers.  `pool` lets several graphs that never run concurrently
+    share one memory pool (`torch.cuda.graph_pool_handle()`).  `launches` is the number of
+    this library's kernels in one replay."""
+
+    def __init__(self, block: ShardedGlobalBlock, tokens: torch.Tensor, warmup: int = 2, pool=None):
+        from . import _clib
+        self.block, self.tokens = block, tokens
+        dev = tokens.device
+        timers, block.timers = block.timers, None
+        try:
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                for _ in range(warmup):
+                    block.step(tokens)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            n0 = _clib.lib().vb200_launch_count()
+            with torch.cuda.graph(self.graph, pool=pool):
+                self.out = block.step(tokens)
+            self.launches = int(_clib.lib().vb200_launch_count() - n0)
+        finally:
+            block.timers = timers
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.out
+
+    def release(self) -> None:
+        """Drop the graph (do this before destroying the process group)."""
+        self.graph = None
+        self.out = None

@@ -252,6 +252,54 @@ def projection_stress(pkg, dev, hbm_peak: float) -> dict:
             "peak_gbs": hbm_peak}
 
 
+def long_sequence(pkg, attn, dev, world: int, rank: int, steps: int, flush) -> dict:
+    """Config 4 (long sequence) at this N: 256 frames x 1029 tokens (263,424), merge 8x to
+    32,928 merged keys, query rows sharded over the ranks (each rank 256 / N frames, its
+    compact queries over all merged keys after the peer-memory all-gather).  Same block and
+    weights as the headline; each step a replay of the recorded step graph; max over ranks."""
+    import torch
+    import torch.distributed as dist
+    frames, merge = 256, 8
+    block = pkg.parallel.ShardedGlobalBlock(attn, frames=frames, tokens_per_frame=TOKENS_PER_FRAME,
+                                            patch_token_start=SPECIAL, merge_factor=merge,
+                                            group_frames=GROUP_FRAMES, world=world, rank=rank)
+    sh = block.shard
+    gen = torch.Generator(device=dev).manual_seed(4 + rank)
+    tokens = torch.randn(1, sh.token_end - sh.token_begin, DIM, device=dev, generator=gen).to(torch.bfloat16)
+    graph = pkg.parallel.StepGraph(block, tokens)
+    graph.replay()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    if world > 1:
+        dist.barrier(device_ids=[dev.index])
+    torch.cuda.synchronize()
+    for a, b in ev:
+        flush.zero_()
+        a.record()
+        graph.replay()
+        b.record()
+    torch.cuda.synchronize()
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    graph.release()
+    if pkg.device_error_flags() != 0:
+        raise RuntimeError("device error flags set during the long-sequence steps")
+    K_total = frames * TOKENS_PER_FRAME // merge
+    q_local = K_total // world
+    flops = 4.0 * q_local * K_total * 64 * HEADS * world  # whole job
+    ms = total_ms / steps
+    return {"workload": f"config 4: {frames} frames x {TOKENS_PER_FRAME} tokens ({frames * TOKENS_PER_FRAME:,}), "
+                        f"merge {merge}x to {K_total:,} merged keys, compact-query, query rows sharded x{world}; "
+                        "256 MB L2 flush between steps (outside the step events)",
+            "n_gpus": world, "steps": steps, "ms_per_step": ms, "frames_per_s": frames / (ms / 1e3),
+            "attention_flops_per_step": flops,
+            "step_tflops_attention_only": flops / (ms / 1e3) / 1e12,
+            "note": "whole block step (plan, qkv, compact, all-gather, attention, proj, restore); "
+                    "attention FLOPs divided by the whole step time"}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -326,25 +374,48 @@ def run_ours(args) -> None:
     if pkg.device_error_flags() != 0:
         raise RuntimeError("device error flags set during warm-up")
 
-    # ---- timed device steps (inputs resident in HBM) ----
-    block.timers = {}
+    # Each step is recorded once as a CUDA graph and replayed (the step's ~20 launches from
+    # Python would otherwise leave the GPU idle between short kernels).  One graph over the
+    # resident input, two over the double-buffered inputs of the end-to-end loop.
+    pool = torch.cuda.graph_pool_handle()
+    dbuf = [torch.empty_like(tokens) for _ in range(2)]
+    for b in dbuf:
+        b.copy_(tokens)
+    graph_dev = pkg.parallel.StepGraph(block, tokens, pool=pool)
+    graph_e2e = [pkg.parallel.StepGraph(block, b, pool=pool) for b in dbuf]
+    torch.cuda.synchronize()
+    if pkg.device_error_flags() != 0:
+        raise RuntimeError("device error flags set while recording the step graphs")
+
+    # ---- timed device steps (inputs resident in HBM): graph replays ----
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    launches0 = lib.vb200_launch_count()
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clocks:
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record()
-            block.step(tokens)
+            graph_dev.replay()
             ev[i][1].record()
         torch.cuda.synchronize()
     barrier()
-    launches = lib.vb200_launch_count() - launches0
+    launches = graph_dev.launches * args.steps
     step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+
+    # ---- per-phase timing: eager steps with CUDA events around each phase ----
+    # The GPU first sleeps (~50 ms) so that the host queues every step before the GPU starts
+    # them: the events then time the GPU's work, not the host's launch rate.
+    block.timers = {}
+    barrier()
+    torch.cuda._sleep(100_000_000)
+    for i in range(min(args.steps, 10)):
+        flush.zero_()
+        block.step(tokens)
+    torch.cuda.synchronize()
+    barrier()
     timers = {k: [a.elapsed_time(b) for a, b in v] for k, v in block.timers.items()}
     block.timers = None
-    total_ms = sum(step_ms)
 
     # ---- timed end-to-end steps through the public API (host buffers, copies inside) ----
     # Pipelined as a serving loop would run it: step i+1's tokens are copied from pinned host
@@ -353,9 +424,9 @@ def run_ours(args) -> None:
     # copy is inside the timed region; the L2 flush still precedes every step.
     comp = torch.cuda.current_stream(dev)
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    dbuf = [torch.empty_like(tokens) for _ in range(2)]
     in_ready = [torch.cuda.Event() for _ in range(args.steps)]
     done = [torch.cuda.Event() for _ in range(args.steps)]
+    copied = [torch.cuda.Event() for _ in range(args.steps)]
     e2e_0, e2e_1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
@@ -373,12 +444,14 @@ def run_ours(args) -> None:
                 in_ready[i + 1].record(s_in)
         flush.zero_()
         comp.wait_event(in_ready[i])
-        out = block.step(dbuf[i % 2])
+        if i >= 2:
+            comp.wait_event(copied[i - 2])  # this graph's output buffer has been read back
+        out = graph_e2e[i % 2].replay()
         done[i].record(comp)
         s_out.wait_event(done[i])
         with torch.cuda.stream(s_out):
             host_out.copy_(out[0], non_blocking=True)
-        out.record_stream(s_out)
+            copied[i].record(s_out)
     comp.wait_stream(s_out)
     e2e_1.record(comp)
     torch.cuda.synchronize()
@@ -437,14 +510,20 @@ def run_ours(args) -> None:
                 "pipelined": "h2d of step i+1 and d2h of step i-1 overlap step i (copy streams, "
                              "double-buffered device input); the first h2d and last d2h are inside the "
                              "timed region"},
+        "step_submission": "each step is a recorded CUDA graph of the block's kernels, replayed per step; "
+                           "phase_ms and attention_ms come from eager steps with per-phase CUDA events",
         "gpu_launches": int(launches),
     }
+    line["components"]["long_sequence_config4"] = long_sequence(pkg, attn, dev, world, rank,
+                                                                max(3, min(args.steps, 10)), flush)
     if world == 1:
         line["components"]["projection_config5"] = projection_stress(pkg, dev, hbm_peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
+    for g in [graph_dev, *graph_e2e]:
+        g.release()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
