@@ -649,6 +649,14 @@ struct StageSlotMeta {
   int src;
   float w;
 };
+// Destinations of the compacted k|v rows in other GPUs' memory (peer-mapped buffers): row j
+// of this call lands at row row0 + j of every listed buffer, k then v ([rows, 2C]).
+constexpr int kMaxKvPeers = 16;
+struct KvPeers {
+  uint64_t dst[kMaxKvPeers];
+  long long row0, stride;  // stride in elements
+  int world;               // 0: no peer writes
+};
 static_assert(2 * kStageSlots * 8 + kStageSlots * sizeof(StageSlotMeta) <= kStageHeaderBytes, "stage header");
 
 template <typename T>
@@ -659,7 +667,7 @@ __global__ void __launch_bounds__(416, 2)
                               int corners, const int32_t* __restrict__ seg_offsets,
                               const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
                               const float* __restrict__ normalizer, int pool_mask, T* __restrict__ out,
-                              long long os) {
+                              long long os, const __grid_constant__ KvPeers peers) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int n_cons = 3 * C / 8;  // consumer threads, a whole number of warps (C % 256 == 0)
   const int heads2 = 2 * C / 64;
@@ -819,8 +827,18 @@ __global__ void __launch_bounds__(416, 2)
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] = __fdiv_rn(acc[q], norm);
     }
-    store_vec<T>(out + j * os + t * C + col, acc);
+    uint4 raw;
+    T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) e[q] = from_f32<T>(acc[q]);
+    *reinterpret_cast<uint4*>(out + j * os + t * C + col) = raw;
+    if (t > 0) {
+      // the k|v all-gather, fused: posted stores straight into every rank's key/value buffer
+      const long long off = (peers.row0 + j) * peers.stride + (t - 1) * C + col;
+      for (int r = 0; r < peers.world; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(peers.dst[r]) + off) = raw;
+    }
   }
+  if (peers.world > 0) __threadfence_system();  // peer stores before whatever the stream signals next
 }
 
 // Per-head LayerNorm of the q block of qkv rows (query-preserving plans keep every query).
@@ -1309,12 +1327,12 @@ extern "C" size_t vb200_compact_qkv_workspace_size(int64_t rows, int64_t C) {
   return align_up(static_cast<size_t>(rows > 0 ? rows : 1) * static_cast<size_t>(2 * C / 64) * sizeof(float2), 256);
 }
 
-extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C,
-                                 const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
-                                 int64_t M, int64_t corners, const int32_t* seg_offsets,
-                                 const int32_t* entry_src, const float* entry_w, const float* normalizer,
-                                 int pool_mask, void* out, int64_t os, void* workspace,
-                                 size_t workspace_bytes, void* stream) {
+namespace {
+int compact_qkv_impl(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C, const float* ln_weight,
+                     const float* ln_bias, float eps, const int64_t* keep, int64_t M, int64_t corners,
+                     const int32_t* seg_offsets, const int32_t* entry_src, const float* entry_w,
+                     const float* normalizer, int pool_mask, void* out, int64_t os, void* workspace,
+                     size_t workspace_bytes, const KvPeers& peers, void* stream) {
   VB200_REQUIRE(dtype == VB200_BF16 || dtype == VB200_F16, "compact_qkv: dtype must be bf16 or fp16 (got %d)", dtype);
   VB200_REQUIRE(C > 0 && C % 256 == 0, "compact_qkv: channels per tensor must be a multiple of 256 (got %lld)",
                 (long long)C);
@@ -1356,7 +1374,8 @@ extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64
                    "cudaFuncSetAttribute");                                                                      \
   compact_qkv_staged_kernel<T><<<grid, threads, smem, st>>>(                                                     \
       static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, stats, keep, M,             \
-      static_cast<int>(corners), seg_offsets, entry_src, entry_w, normalizer, pool_mask, static_cast<T*>(out), os)
+      static_cast<int>(corners), seg_offsets, entry_src, entry_w, normalizer, pool_mask, static_cast<T*>(out), os, \
+      peers)
     if (dtype == VB200_BF16) {
       VB200_CQKV_STAGED(__nv_bfloat16);
     } else {
@@ -1366,6 +1385,7 @@ extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64
     VB200_CHECK_LAUNCH("compact_qkv_staged_kernel");
     return VB200_OK;
   }
+  VB200_REQUIRE(peers.world == 0, "compact_qkv_peer: peer destinations need C <= 1024");
 #define VB200_CQKV(T)                                                                                     \
   compact_qkv_kernel<T><<<row_blocks(M * 3 * (C / 256)), kWarpsPerBlock * 32, 0, st>>>(                   \
       static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, stats, keep, M,      \
@@ -1375,6 +1395,43 @@ extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64
 #undef VB200_CQKV
   VB200_CHECK_LAUNCH("compact_qkv_kernel");
   return VB200_OK;
+}
+}  // namespace
+
+extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C,
+                                 const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
+                                 int64_t M, int64_t corners, const int32_t* seg_offsets,
+                                 const int32_t* entry_src, const float* entry_w, const float* normalizer,
+                                 int pool_mask, void* out, int64_t os, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  KvPeers none{};
+  return compact_qkv_impl(dtype, qkv, rows, xs, C, ln_weight, ln_bias, eps, keep, M, corners, seg_offsets, entry_src,
+                          entry_w, normalizer, pool_mask, out, os, workspace, workspace_bytes, none, stream);
+}
+
+extern "C" int vb200_compact_qkv_peer(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C,
+                                      const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
+                                      int64_t M, int64_t corners, const int32_t* seg_offsets,
+                                      const int32_t* entry_src, const float* entry_w, const float* normalizer,
+                                      int pool_mask, void* out, int64_t os, const uint64_t* kv_dst_ptrs, int world,
+                                      int64_t kv_row0, int64_t kv_row_stride, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  VB200_REQUIRE(world >= 1 && world <= kMaxKvPeers, "compact_qkv_peer: world must be in [1, %d] (got %d)",
+                kMaxKvPeers, world);
+  VB200_REQUIRE(kv_dst_ptrs != nullptr && kv_row0 >= 0 && kv_row_stride >= 2 * C && kv_row_stride % 8 == 0,
+                "compact_qkv_peer: bad destination layout (row stride %lld elements for C=%lld)",
+                (long long)kv_row_stride, (long long)C);
+  KvPeers peers{};
+  for (int r = 0; r < world; ++r) {
+    VB200_REQUIRE(kv_dst_ptrs[r] != 0 && (kv_dst_ptrs[r] & 15u) == 0,
+                  "compact_qkv_peer: destination of rank %d is null or not 16-byte aligned", r);
+    peers.dst[r] = kv_dst_ptrs[r];
+  }
+  peers.world = world;
+  peers.row0 = kv_row0;
+  peers.stride = kv_row_stride;
+  return compact_qkv_impl(dtype, qkv, rows, xs, C, ln_weight, ln_bias, eps, keep, M, corners, seg_offsets, entry_src,
+                          entry_w, normalizer, pool_mask, out, os, workspace, workspace_bytes, peers, stream);
 }
 
 extern "C" int vb200_head_layernorm(int dtype, const void* x, int64_t rows, int64_t xs, int64_t C,

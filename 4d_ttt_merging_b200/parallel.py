@@ -4,11 +4,13 @@ Each rank owns a contiguous run of frames, aligned to the planner's frame groups
 merge plan of a rank is exactly the restriction of the single-GPU plan (sources only take
 supports inside their own frame group).  Per global layer a rank
 
-  1. builds its plan (merge step) and projects / compacts its own tokens (no exchange),
-  2. all-gathers the merged K and V ([K_local, C] bf16 each) and the log-mass vector
-     ([K_local] fp32) — the only exchange of the layer: peer loads over NVLink from
-     symmetric memory between two device barriers (PeerExchange), or NCCL
-     all_gather_into_tensor where peer-mapped memory is unavailable,
+  1. builds its plan (merge step) and projects its own tokens,
+  2. compacts them and all-gathers the merged K and V ([K_local, C] bf16 each) and the
+     log-mass vector ([K_local] fp32) — the only exchange of the layer.  With peer-mapped
+     symmetric memory (PeerExchange) the compaction kernel itself stores every merged k|v
+     row into all ranks' K|V buffers (posted NVLink writes overlapping the compaction)
+     between two device barriers; otherwise the compaction is followed by an NCCL
+     all_gather_into_tensor,
   3. runs mass-bias attention of its own compact queries over all merged keys,
   4. projects and restores its own tokens.
 
@@ -110,8 +112,29 @@ class PeerExchange:
         self.log_mass_all = torch.empty(self.world * rows, dtype=torch.float32, device=device)
         self._lib, self._clib = _clib.lib(), _clib
 
+    def kv_peers(self):
+        """Destinations of this rank's merged k|v rows for `compact_qkv(kv_peers=...)`: every
+        rank's full K|V buffer at this rank's row offset."""
+        return self._kv_dst, self.world, self.rank * self.rows, 2 * self.C
+
+    def begin(self):
+        """Device barrier before the fused compaction writes into other ranks' buffers: every
+        rank has finished reading its previous full K|V buffer and has published log_mass."""
+        self.handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
+
+    def finish(self):
+        """After the fused compaction: gather every rank's log-mass, then a device barrier (all
+        ranks' k|v writes have landed).  -> (kv, log_mass) in rank order."""
+        stream = self._clib.stream_of(self.kv.device)
+        rows = self.rows
+        self._clib.check(self._lib.vb200_peer_gather(self._lm_src, self.world, 1, rows * 4, rows * 4,
+                                                     self.log_mass_all.data_ptr(), rows * 4, stream), "peer_gather")
+        self.handle.barrier(channel=1, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        return self.kv, self.log_mass_all
+
     def exchange(self):
-        """-> (kv [world*rows, 2C], log_mass [world*rows]) in rank order, on the current stream."""
+        """Unfused form: -> (kv [world*rows, 2C], log_mass [world*rows]) in rank order, on the
+        current stream, from this rank's compacted rows in `packed`."""
         C, es, rows = self.C, self.es, self.rows
         stream = self._clib.stream_of(self.kv.device)
         self.handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
@@ -201,21 +224,27 @@ class ShardedGlobalBlock:
             self._ln = _ln_params(attn.q_norm, attn.k_norm)
         lw, lb, eps = self._ln if self._ln is not None else (None, None, 1e-5)
         xchg = self._exchange(plan.kept_tokens, C, qkv.dtype, qkv.device) if self.world > 1 else None
-        # [K_local, 3C]: q | k | v, written straight into the peer-readable buffer when sharded
-        packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111,
-                                  out=None if xchg is None else xchg.packed)
-        self._end(e)
         log_mass = plan.key_log_mass.reshape(-1)
-        K_local = packed.shape[0]
-        kv = packed[:, C:]
-        if self.world > 1:
-            e = self._ev("all_gather")
-            if xchg is not None:
-                xchg.log_mass.copy_(log_mass)
-                kv, log_mass = xchg.exchange()
-            else:
-                kv, log_mass = gather_merged([kv, log_mass], self.group)
+        if xchg is not None:
+            # fused all-gather: the compaction stores every merged k|v row into all ranks'
+            # K|V buffers, between two device barriers
+            xchg.log_mass.copy_(log_mass)
+            xchg.begin()
+            packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111, out=xchg.packed,
+                                      kv_peers=xchg.kv_peers())
             self._end(e)
+            e = self._ev("all_gather")
+            kv, log_mass = xchg.finish()
+            self._end(e)
+        else:
+            packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111)  # [K_local, 3C]: q | k | v
+            self._end(e)
+            kv = packed[:, C:]
+            if self.world > 1:
+                e = self._ev("all_gather")
+                kv, log_mass = gather_merged([kv, log_mass], self.group)
+                self._end(e)
+        K_local = packed.shape[0]
         e = self._ev("attention")
         view = lambda t: t.view(1, t.shape[0], H, C // H).transpose(1, 2)
         o = mass_bias_attention(view(packed[:, :C]), view(kv[:, :C]), view(kv[:, C:]), log_mass)

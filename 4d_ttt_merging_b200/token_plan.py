@@ -212,13 +212,15 @@ class WeightedBilinearTokenPlan:
 
     def compact_qkv(self, qkv: torch.Tensor, ln_weight: torch.Tensor | None = None,
                     ln_bias: torch.Tensor | None = None, eps: float = 1e-5,
-                    pool_mask: int = 0b111, out: torch.Tensor | None = None) -> torch.Tensor:
+                    pool_mask: int = 0b111, out: torch.Tensor | None = None, kv_peers=None) -> torch.Tensor:
         """Fused q/k LayerNorm + Q||K||V compaction of a [N, 3C] (or [1, N, 3C]) qkv buffer in
         one kernel (``vb200_compact_qkv``); returns [M, 3C].  ``ln_weight`` / ``ln_bias`` are
         [2, 64] fp32 (q then k) or None.  Bit t of ``pool_mask`` pools tensor t (q, k, v);
         a clear bit keeps the physical row only (compact_key semantics).  ``out``: an optional
         [M, 3C] destination (rows 16-byte aligned, unit channel stride), e.g. a buffer that other
-        GPUs read."""
+        GPUs read.  ``kv_peers`` = (pointer array, world, row0, row_stride): also store the k|v
+        part of every merged row into those peer-mapped [rows, 2C] buffers at row row0 + j
+        (``vb200_compact_qkv_peer``, the fused all-gather of the sharded layer)."""
         x = qkv[0] if qkv.ndim == 3 else qkv
         C.require_cuda(x, "compact_qkv")
         if x.stride(-1) != 1 or x.data_ptr() % 16 or (x.stride(0) * x.element_size()) % 16:
@@ -238,12 +240,18 @@ class WeightedBilinearTokenPlan:
         lib = C.lib()
         ws_bytes = lib.vb200_compact_qkv_workspace_size(x.shape[0], c) if lw is not None else 0
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
-        rc = lib.vb200_compact_qkv(
-            C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), c, C.ptr(lw), C.ptr(lb), float(eps),
-            self._keep_flat.data_ptr(), self.kept_tokens, csr.corners, csr.seg_offsets.data_ptr(),
-            csr.entry_src.data_ptr(), csr.entry_w.data_ptr(), self._normalizer_flat.data_ptr(), int(pool_mask),
-            out.data_ptr(), out.stride(0), ws.data_ptr(), ws_bytes, C.stream_of(x.device))
-        C.check(rc, "compact_qkv")
+        args = (C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), c, C.ptr(lw), C.ptr(lb), float(eps),
+                self._keep_flat.data_ptr(), self.kept_tokens, csr.corners, csr.seg_offsets.data_ptr(),
+                csr.entry_src.data_ptr(), csr.entry_w.data_ptr(), self._normalizer_flat.data_ptr(), int(pool_mask),
+                out.data_ptr(), out.stride(0))
+        if kv_peers is None:
+            rc = lib.vb200_compact_qkv(*args, ws.data_ptr(), ws_bytes, C.stream_of(x.device))
+            C.check(rc, "compact_qkv")
+        else:
+            ptrs, world, row0, row_stride = kv_peers
+            rc = lib.vb200_compact_qkv_peer(*args, ptrs, int(world), int(row0), int(row_stride), ws.data_ptr(),
+                                            ws_bytes, C.stream_of(x.device))
+            C.check(rc, "compact_qkv_peer")
         return out
 
     def compact_key(self, value: torch.Tensor) -> torch.Tensor:

@@ -167,6 +167,23 @@ VB200_API int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_
                                 const int32_t* entry_src, const float* entry_w, const float* normalizer,
                                 int pool_mask, void* out, int64_t out_row_stride, void* workspace,
                                 size_t workspace_bytes, void* stream);
+/* vb200_compact_qkv with the k|v all-gather of the query-sharded layer fused in: besides out,
+ * the k and v parts of merged row j ([2C] elements, k then v) are stored into each of the
+ * `world` buffers kv_dst_ptrs[r] (peer-mapped memory of the other GPUs, this GPU's own buffer
+ * included) at row kv_row0 + j, row stride kv_row_stride elements; the stores are posted
+ * NVLink writes from the consumer threads, overlapping the compaction, followed by a
+ * system-scope fence.  The caller orders them between cross-GPU barriers (every rank has
+ * finished reading the buffers before; every rank's writes have landed after).  Needs
+ * C <= 1024.  Replaces the compaction + NCCL all-gather of merged K/V of the sharded layer
+ * (the reference's aggregator runs the layer on one GPU: aggregator.py:901-1215). */
+VB200_API int vb200_compact_qkv_peer(int dtype, const void* qkv, int64_t rows, int64_t row_stride, int64_t C,
+                                     const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
+                                     int64_t M, int64_t corners, const int32_t* seg_offsets,
+                                     const int32_t* entry_src, const float* entry_w, const float* normalizer,
+                                     int pool_mask, void* out, int64_t out_row_stride,
+                                     const uint64_t* kv_dst_ptrs, int world, int64_t kv_row0,
+                                     int64_t kv_row_stride, void* workspace, size_t workspace_bytes,
+                                     void* stream);
 /* Per-64-channel-head LayerNorm of rows (the dense queries of query-preserving plans and the
  * special queries): out[r] = LN(x[r]).  C % 256 == 0. */
 VB200_API int vb200_head_layernorm(int dtype, const void* x, int64_t rows, int64_t row_stride, int64_t C,

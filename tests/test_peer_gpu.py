@@ -47,3 +47,33 @@ def test_peer_push_to_every_rank(pkg, cuda_device):
     expect = torch.cat([m[:, cols:2 * cols] for m in mine])
     for f in full:
         assert torch.equal(f, expect)
+
+
+def test_compact_qkv_peer_writes_every_rank(pkg, cuda_device):
+    """The compaction with the fused k|v all-gather: `out` equals the plain compaction bit for
+    bit, and every destination buffer (three local buffers standing in for the ranks) holds the
+    merged k|v rows at the given row offset, other rows untouched."""
+    dev = cuda_device
+    g = torch.Generator(device="cpu").manual_seed(3)
+    frames, tpf, dim = 4, 100, 256
+    tok = torch.randn(1, frames * tpf, dim, generator=g).to(dev, torch.bfloat16)
+    plan = pkg.build_uniform_convex_plan(tok, frames=frames, tokens_per_frame=tpf, patch_token_start=5,
+                                         merge_factor=4, group_frames=4)
+    qkv = torch.randn(frames * tpf, 3 * dim, generator=g).to(dev, torch.bfloat16)
+    lw = (1 + 0.1 * torch.randn(2, 64, generator=g)).to(dev)
+    lb = (0.1 * torch.randn(2, 64, generator=g)).to(dev)
+    ref = plan.compact_qkv(qkv, lw, lb, 1e-6)
+    M = plan.kept_tokens
+    world, row0, stride = 3, 7, 2 * dim + 64
+    sentinel = 12345.0
+    bufs = [torch.full((row0 + M + 5, stride), sentinel, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+    ptrs = _u64([b.data_ptr() for b in bufs])
+    out = torch.empty_like(ref)
+    got = plan.compact_qkv(qkv, lw, lb, 1e-6, out=out, kv_peers=(ptrs, world, row0, stride))
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    for b in bufs:
+        assert torch.equal(b[row0:row0 + M, :2 * dim], ref[:, dim:])
+        assert torch.all(b[:row0] == sentinel) and torch.all(b[row0 + M:] == sentinel)
+        assert torch.all(b[:, 2 * dim:] == sentinel)
+    assert pkg.device_error_flags() == 0
