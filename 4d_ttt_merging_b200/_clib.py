@@ -65,7 +65,7 @@ _SIGNATURES = {
     "vb200_compact_qkv_peer": (
         _c_int,
         [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_float, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp,
-         _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_i64, _c_i64, _c_vp, _c_size, _c_vp],
+         _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_vp, _c_int, _c_int, _c_i64, _c_i64, _c_vp, _c_size, _c_vp],
     ),
     "vb200_head_layernorm": (
         _c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_float, _c_vp, _c_i64, _c_vp],

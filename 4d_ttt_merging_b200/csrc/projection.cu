@@ -656,7 +656,16 @@ struct KvPeers {
   uint64_t dst[kMaxKvPeers];
   long long row0, stride;  // stride in elements
   int world;               // 0: no peer writes
+  int multicast;           // 1: dst[0] is a multicast (NVLS) address covering every rank's buffer
 };
+
+// One 16-byte store through a multicast address: the NVLink switch writes it into the memory of
+// every GPU bound to the multicast object.
+__device__ __forceinline__ void multimem_st16(void* p, const uint4& v) {
+  asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
 static_assert(2 * kStageSlots * 8 + kStageSlots * sizeof(StageSlotMeta) <= kStageHeaderBytes, "stage header");
 
 template <typename T>
@@ -832,13 +841,23 @@ __global__ void __launch_bounds__(416, 2)
 #pragma unroll
     for (int q = 0; q < 8; ++q) e[q] = from_f32<T>(acc[q]);
     *reinterpret_cast<uint4*>(out + j * os + t * C + col) = raw;
-    if (t > 0) {
+    if (t > 0 && peers.world > 0) {
       // the k|v all-gather, fused: posted stores straight into every rank's key/value buffer
+      // (one multicast store, or one store per rank)
       const long long off = (peers.row0 + j) * peers.stride + (t - 1) * C + col;
-      for (int r = 0; r < peers.world; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(peers.dst[r]) + off) = raw;
+      if (peers.multicast) {
+        multimem_st16(reinterpret_cast<T*>(peers.dst[0]) + off, raw);
+      } else {
+        for (int r = 0; r < peers.world; ++r)
+          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(peers.dst[r]) + off) = raw;
+      }
     }
   }
-  if (peers.world > 0) __threadfence_system();  // peer stores before whatever the stream signals next
+  if (peers.world > 0) {
+    // peer / multicast stores ordered before whatever the stream signals next
+    if (peers.multicast) asm volatile("fence.proxy.alias;" ::: "memory");
+    __threadfence_system();
+  }
 }
 
 // Per-head LayerNorm of the q block of qkv rows (query-preserving plans keep every query).
@@ -1414,7 +1433,7 @@ extern "C" int vb200_compact_qkv_peer(int dtype, const void* qkv, int64_t rows, 
                                       int64_t M, int64_t corners, const int32_t* seg_offsets,
                                       const int32_t* entry_src, const float* entry_w, const float* normalizer,
                                       int pool_mask, void* out, int64_t os, const uint64_t* kv_dst_ptrs, int world,
-                                      int64_t kv_row0, int64_t kv_row_stride, void* workspace,
+                                      int multicast, int64_t kv_row0, int64_t kv_row_stride, void* workspace,
                                       size_t workspace_bytes, void* stream) {
   VB200_REQUIRE(world >= 1 && world <= kMaxKvPeers, "compact_qkv_peer: world must be in [1, %d] (got %d)",
                 kMaxKvPeers, world);
@@ -1422,12 +1441,14 @@ extern "C" int vb200_compact_qkv_peer(int dtype, const void* qkv, int64_t rows, 
                 "compact_qkv_peer: bad destination layout (row stride %lld elements for C=%lld)",
                 (long long)kv_row_stride, (long long)C);
   KvPeers peers{};
-  for (int r = 0; r < world; ++r) {
+  const int n_dst = multicast ? 1 : world;
+  for (int r = 0; r < n_dst; ++r) {
     VB200_REQUIRE(kv_dst_ptrs[r] != 0 && (kv_dst_ptrs[r] & 15u) == 0,
                   "compact_qkv_peer: destination of rank %d is null or not 16-byte aligned", r);
     peers.dst[r] = kv_dst_ptrs[r];
   }
   peers.world = world;
+  peers.multicast = multicast ? 1 : 0;
   peers.row0 = kv_row0;
   peers.stride = kv_row_stride;
   return compact_qkv_impl(dtype, qkv, rows, xs, C, ln_weight, ln_bias, eps, keep, M, corners, seg_offsets, entry_src,

@@ -20,6 +20,7 @@ the same key sequence as a single GPU would: results do not depend on the rank c
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
@@ -111,11 +112,26 @@ class PeerExchange:
         self._lm_src = u64(*[p + packed_bytes for p in ptrs])
         self.log_mass_all = torch.empty(self.world * rows, dtype=torch.float32, device=device)
         self._lib, self._clib = _clib.lib(), _clib
+        # multicast (NVLS) address of the K|V region when the allocation is bound to a multicast
+        # object and VB200_PEER_MULTICAST=1.  Off by default: on 8 B200s one multimem store per
+        # row part measured slower than one posted store per rank (0.54 vs 0.49 ms per config-2
+        # step).
+        mc = 0
+        if os.environ.get("VB200_PEER_MULTICAST", "0") == "1":
+            mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)  # 0: no multicast object
+        self._kv_mc = (ctypes.c_uint64 * 1)(mc + kv_off) if mc else None
+
+    @property
+    def multicast(self) -> bool:
+        return self._kv_mc is not None
 
     def kv_peers(self):
         """Destinations of this rank's merged k|v rows for `compact_qkv(kv_peers=...)`: every
-        rank's full K|V buffer at this rank's row offset."""
-        return self._kv_dst, self.world, self.rank * self.rows, 2 * self.C
+        rank's full K|V buffer at this rank's row offset (through the multicast address when
+        there is one, else one pointer per rank)."""
+        if self._kv_mc is not None:
+            return self._kv_mc, self.world, self.rank * self.rows, 2 * self.C, 1
+        return self._kv_dst, self.world, self.rank * self.rows, 2 * self.C, 0
 
     def begin(self):
         """Device barrier before the fused compaction writes into other ranks' buffers: every
@@ -167,8 +183,10 @@ class ShardedGlobalBlock:
         self._ln = None     # fp32 q/k LayerNorm parameters, [2, 64] each
         self._xchg = None   # PeerExchange (world > 1, CUDA), built on the first step
         self._xchg_failed = False
+        self._side = None   # side stream of the qkv GEMM
 
     def _ev(self, name):
+        """Start a phase timer on the current stream (phases on different streams overlap)."""
         if self.timers is None:
             return None
         e = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -210,12 +228,27 @@ class ShardedGlobalBlock:
         from .ops import mass_bias_attention
         attn = self.attn
         H = attn.num_heads
+        # The plan (a chain of small kernels) and the qkv GEMM both read only the tokens: the
+        # GEMM runs on a side stream, concurrently with the plan, and joins before compaction.
+        cur = torch.cuda.current_stream(tokens.device) if tokens.is_cuda else None
+        if cur is not None:
+            if self._side is None or self._side.device != tokens.device:
+                self._side = torch.cuda.Stream(tokens.device)
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                e = self._ev("qkv_gemm")
+                qkv = attn.qkv_projection(tokens)
+                self._end(e)
         e = self._ev("merge")
         plan = self.plan(tokens)
         self._end(e)
-        e = self._ev("qkv_gemm")
-        qkv = attn.qkv_projection(tokens)
-        self._end(e)
+        if cur is None:
+            e = self._ev("qkv_gemm")
+            qkv = attn.qkv_projection(tokens)
+            self._end(e)
+        else:
+            cur.wait_stream(self._side)
+            qkv.record_stream(cur)
         B, N, C3 = qkv.shape
         C = C3 // 3
         e = self._ev("compact")

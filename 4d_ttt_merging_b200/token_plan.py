@@ -218,9 +218,10 @@ class WeightedBilinearTokenPlan:
         [2, 64] fp32 (q then k) or None.  Bit t of ``pool_mask`` pools tensor t (q, k, v);
         a clear bit keeps the physical row only (compact_key semantics).  ``out``: an optional
         [M, 3C] destination (rows 16-byte aligned, unit channel stride), e.g. a buffer that other
-        GPUs read.  ``kv_peers`` = (pointer array, world, row0, row_stride): also store the k|v
-        part of every merged row into those peer-mapped [rows, 2C] buffers at row row0 + j
-        (``vb200_compact_qkv_peer``, the fused all-gather of the sharded layer)."""
+        GPUs read.  ``kv_peers`` = (pointer array, world, row0, row_stride[, multicast]): also
+        store the k|v part of every merged row into those peer-mapped [rows, 2C] buffers at row
+        row0 + j (``vb200_compact_qkv_peer``, the fused all-gather of the sharded layer); with
+        multicast set the array holds one multicast address covering every rank's buffer."""
         x = qkv[0] if qkv.ndim == 3 else qkv
         C.require_cuda(x, "compact_qkv")
         if x.stride(-1) != 1 or x.data_ptr() % 16 or (x.stride(0) * x.element_size()) % 16:
@@ -248,9 +249,10 @@ class WeightedBilinearTokenPlan:
             rc = lib.vb200_compact_qkv(*args, ws.data_ptr(), ws_bytes, C.stream_of(x.device))
             C.check(rc, "compact_qkv")
         else:
-            ptrs, world, row0, row_stride = kv_peers
-            rc = lib.vb200_compact_qkv_peer(*args, ptrs, int(world), int(row0), int(row_stride), ws.data_ptr(),
-                                            ws_bytes, C.stream_of(x.device))
+            ptrs, world, row0, row_stride = kv_peers[:4]
+            multicast = int(kv_peers[4]) if len(kv_peers) > 4 else 0
+            rc = lib.vb200_compact_qkv_peer(*args, ptrs, int(world), multicast, int(row0), int(row_stride),
+                                            ws.data_ptr(), ws_bytes, C.stream_of(x.device))
             C.check(rc, "compact_qkv_peer")
         return out
 

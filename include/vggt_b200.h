@@ -172,7 +172,9 @@ VB200_API int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_
  * `world` buffers kv_dst_ptrs[r] (peer-mapped memory of the other GPUs, this GPU's own buffer
  * included) at row kv_row0 + j, row stride kv_row_stride elements; the stores are posted
  * NVLink writes from the consumer threads, overlapping the compaction, followed by a
- * system-scope fence.  The caller orders them between cross-GPU barriers (every rank has
+ * system-scope fence.  multicast != 0: kv_dst_ptrs[0] is instead the address of the buffers
+ * in a multicast object (NVLS) that binds every rank's buffer, and each row part is written
+ * once with multimem.st (the switch replicates it to all GPUs).  The caller orders them between cross-GPU barriers (every rank has
  * finished reading the buffers before; every rank's writes have landed after).  Needs
  * C <= 1024.  Replaces the compaction + NCCL all-gather of merged K/V of the sharded layer
  * (the reference's aggregator runs the layer on one GPU: aggregator.py:901-1215). */
@@ -181,7 +183,7 @@ VB200_API int vb200_compact_qkv_peer(int dtype, const void* qkv, int64_t rows, i
                                      int64_t M, int64_t corners, const int32_t* seg_offsets,
                                      const int32_t* entry_src, const float* entry_w, const float* normalizer,
                                      int pool_mask, void* out, int64_t out_row_stride,
-                                     const uint64_t* kv_dst_ptrs, int world, int64_t kv_row0,
+                                     const uint64_t* kv_dst_ptrs, int world, int multicast, int64_t kv_row0,
                                      int64_t kv_row_stride, void* workspace, size_t workspace_bytes,
                                      void* stream);
 /* Per-64-channel-head LayerNorm of rows (the dense queries of query-preserving plans and the
