@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       bool ok = true;
       mbar_arrive_expect_tx(bar(kBarQFull), kQT * kTileBytes);
-      for (int t = 0; t < kQT; ++t)
+      for (int t = 0; t < kQT; ++t)  // an empty query tile loads zeros (rows past Nq)
         tma_load_4d(sbase + kOffQ + t * kTileBytes, &tmap_q, bar(kBarQFull), 0, (q_block * kQT + t) * kBM,
                     head, batch);
       for (int j = 0; j < n_tiles && ok; ++j) {
@@ -300,11 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       issue_qk_group(tmem + t * 128, q_desc + t * (kTileBytes >> 4), k_desc + so, qx_desc, kx_desc + so, idesc_qk,
                      bar(kBarSFull + t));
     };
-    // O_t += P_t V_j (P_t from TMEM); the last tile's group also frees the K/V stage
+    // O_t += P_t V_j (P_t from TMEM); the CTA's last query tile's group also frees the K/V stage
+    // the last block of a ragged Nq may leave query tile 1 empty: its MMAs are skipped
+    const bool single_qt = (q_block * kQT + 1) * kBM >= p.Nq;
     auto issue_pv = [=](int t, int j) {
       const uint64_t so = static_cast<uint64_t>((j % kStages) * (kStageStride >> 4));
       issue_pv_group(tmem + kTmemO + t * kHD, tmem + kTmemP + t * kHD, v_desc + so, idesc_pv, j > 0 ? 1u : 0u,
-                     bar(kBarODone + t), bar(kBarKVEmpty + j % kStages), t == kQT - 1 ? 1u : 0u);
+                     bar(kBarODone + t), bar(kBarKVEmpty + j % kStages), (t == kQT - 1 || single_qt) ? 1u : 0u);
     };
     auto wait_all = [&](int b, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, &g_attn_err));
@@ -312,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = wait_all(kBarQFull, 0) && wait_all(kBarKVFull + 0, 0);
     if (ok) {
       tc_fence_after();
-      for (int t = 0; t < kQT; ++t) issue_qk(t, 0);
+      for (int t = 0; t < kQT; ++t)
+        if (t == 0 || !single_qt) issue_qk(t, 0);
     }
     for (int j = 0; j < n_tiles && ok; ++j) {
       if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
@@ -320,6 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Per query tile: the next scores as soon as S_t(j) is in registers, then O_t += P_t V_j.
       // Tile by tile (QK_0, PV_0, QK_1, PV_1) measured 2-7% faster than both QKs first.
       for (int t = 0; t < kQT && ok; ++t) {
+        if (t > 0 && single_qt) break;
         if (j + 1 < n_tiles) {
           ok = wait_all(kBarSFree + t, j & 1);
           if (!ok) break;
@@ -356,8 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_run = -INFINITY;
     float l_run = 0.f;
     bool ok = true;
+    // an empty query tile (rows past Nq only) skips everything but the barriers
+    const bool active = t == 0 || (q_block * kQT + 1) * kBM < p.Nq;
 
-    for (int j = 0; j < n_tiles; ++j) {
+    for (int j = 0; j < (active ? n_tiles : 0); ++j) {
       ok = ok && !*abort_flag;
       if (ok) ok = mbar_wait(bar(kBarSFull + t), j & 1, &g_attn_err);
       ok = __all_sync(0xffffffffu, ok);  // warp-uniform before warp-collective TMEM access
@@ -452,12 +458,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     red_mine[(n_tiles & 1) * kBM] = l_run;
     named_bar_sync(pair_bar, 256);
     const float l_tot = l_run + red_other[(n_tiles & 1) * kBM];
-    if (ok) {
+    if (ok && active) {
       ok = mbar_wait(bar(kBarODone + t), (n_tiles - 1) & 1, &g_attn_err);
       ok = __all_sync(0xffffffffu, ok);
     }
     uint32_t o[kHD / 2];
-    if (ok) {
+    if (ok && active) {
       tc_fence_after();
       tmem_ld32x32b_x32_nowait(o_addr, o);
       tmem_wait_ld();
@@ -486,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // arrives last merges all pieces in piece order (deterministic for any arrival order).
       const long long slot0 = static_cast<long long>(item - p.n_full) * p.split;
       const long long rowi = (slot0 + piece) * kQT * kBM + t * kBM + row;  // this piece's row record
-      if (ok) {
+      if (ok && active) {
         float4* dst = reinterpret_cast<float4*>(p.o_part + rowi * kHD + h * (kHD / 2));
 #pragma unroll
         for (int i = 0; i < kHD / 8; ++i)

@@ -67,6 +67,7 @@ struct TopkParams {
   int k;
   int k_blocks;         // D / 64
   int tile_n;           // basis rows per tile (multiple of 16, <= kBN)
+  int split;            // CTAs per query block, each over a contiguous range of basis tiles
 };
 
 // One k-block (K = 64) of the score tile: four K=16 steps, both descriptors advancing 32 bytes
@@ -159,7 +160,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long row0 = q0 + static_cast<long long>(blockIdx.x) * kBM;
   if (row0 >= q1) return;  // uniform across the CTA, before any barrier or TMEM use
   const int tile_n = p.tile_n;
-  const int n_tiles = static_cast<int>((b1 - b0 + tile_n - 1) / tile_n);
+  // this CTA's basis tiles [t_begin, t_begin + n_tiles) (all of them unless the search is split)
+  const int n_tiles_all = static_cast<int>((b1 - b0 + tile_n - 1) / tile_n);
+  const int t_begin = static_cast<int>(static_cast<long long>(n_tiles_all) * blockIdx.z / p.split);
+  const int n_tiles = static_cast<int>(static_cast<long long>(n_tiles_all) * (blockIdx.z + 1) / p.split) - t_begin;
   const int kb = p.k_blocks;
   const uint32_t b_bytes = static_cast<uint32_t>(tile_n) * kBK * 2;
   auto bar = [&](int i) -> uint32_t { return sbase + kOffBar + 8 * i; };
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(bar(kBarFull + s), kABytes + b_bytes);
           tma_load_2d(st, &tmap_q, bar(kBarFull + s), k * kBK, static_cast<int32_t>(row0));
           tma_load_2d(st + kABytes, &tmap_b, bar(kBarFull + s), k * kBK,
-                      static_cast<int32_t>(b0 + static_cast<long long>(t) * tile_n));
+                      static_cast<int32_t>(b0 + static_cast<long long>(t_begin + t) * tile_n));
         }
       }
     }
@@ -247,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ab = t & 1;
       if (!mbar_wait(bar(kBarAccFull + ab), (t >> 1) & 1, &g_merge_err)) { ok = false; break; }
       tc_fence_after();
-      const long long col0 = b0 + static_cast<long long>(t) * tile_n;
+      const long long col0 = b0 + static_cast<long long>(t_begin + t) * tile_n;
       const long long remaining = b1 - col0;
       const int valid = remaining < tile_n ? static_cast<int>(remaining) : tile_n;
 #pragma unroll 1
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[16];
         tmem_ld32x32b_x16(tmem + lane_off + ab * kBN + c * 16, r);
         if constexpr (kKeys) {
-          const int gcol = t * tile_n + c * 16;  // group-local column of r[0]
+          const int gcol = (t_begin + t) * tile_n + c * 16;  // group-local column of r[0]
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const uint32_t key = score_key(__uint_as_float(r[i]), gcol + i);
@@ -274,7 +278,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(bar(kBarAccEmpty + ab));
     }
     if (!ok) *abort_flag = 1;
+    bool piece_written = false;
     if constexpr (kKeys) {
+      if (p.split > 1) {
+        // split search: this piece's four keys go to slot z of the row's 48 output bytes
+        // (slot 0: the row of `values`, slots 1-2: the halves of the row of `indices`);
+        // topk_merge_kernel combines the slots and writes the final row
+        const long long grow = row0 + row;
+        if (grow < q1) {
+          uint4* slot = blockIdx.z == 0 ? reinterpret_cast<uint4*>(p.values) + grow
+                                        : reinterpret_cast<uint4*>(p.indices) + 2 * grow + (blockIdx.z - 1);
+          *slot = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+        }
+        piece_written = true;
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         tv[i] = kk[i] ? key_score(kk[i]) : -INFINITY;
@@ -282,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     const long long grow = row0 + row;
-    if (grow < q1) {
+    if (grow < q1 && !piece_written) {
 #pragma unroll
       for (int i = 0; i < K; ++i) {
         p.values[grow * K + i] = tv[i];
@@ -299,6 +316,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Combines the per-piece top-4 keys of a split search (see sim_topk_kernel): one thread per
+// query row inserts every piece's keys into one running top-4 (the keys' order is the
+// search's order, so the result equals the unsplit search) and writes values and indices.
+__global__ void topk_merge_kernel(const __grid_constant__ GroupTable groups, float* values, int64_t* indices,
+                                  int split) {
+  const int g = blockIdx.y;
+  const long long q0 = groups.q_begin[g], q1 = groups.q_begin[g + 1];
+  const long long b0 = groups.b_begin[g];
+  const long long r = q0 + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= q1) return;
+  uint4 sl[3];
+  sl[0] = reinterpret_cast<const uint4*>(values)[r];
+  if (split > 1) sl[1] = reinterpret_cast<const uint4*>(indices)[2 * r];
+  if (split > 2) sl[2] = reinterpret_cast<const uint4*>(indices)[2 * r + 1];
+  uint32_t kk[4] = {0u, 0u, 0u, 0u};
+  for (int z = 0; z < split; ++z) {
+    key_insert(kk, sl[z].x);
+    key_insert(kk, sl[z].y);
+    key_insert(kk, sl[z].z);
+    key_insert(kk, sl[z].w);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    values[r * 4 + i] = kk[i] ? key_score(kk[i]) : -INFINITY;
+    indices[r * 4 + i] = kk[i] ? static_cast<int64_t>(b0 + (0xFFFF - static_cast<int>(kk[i] & 0xFFFFu))) : -1;
+  }
+}
+
 int make_rows_map(CUtensorMap* map, const void* base, long long rows, long long D, long long stride,
                   int box_rows) {
   uint64_t dims[2] = {static_cast<uint64_t>(D), static_cast<uint64_t>(rows)};
@@ -306,6 +351,35 @@ int make_rows_map(CUtensorMap* map, const void* base, long long rows, long long 
   uint32_t box[2] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(box_rows)};
   return encode_tiled_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box,
                           CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int sm_count_cached() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+  if (dev < 64 && cached[dev] > 0) return cached[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+// Pieces per query block for a launch of `ctas` CTAs over n_tiles basis tiles, one CTA per SM:
+// time ~ waves x (tiles per piece + ramp), plus about one tile for the merge launch when split;
+// at most 3 pieces (their keys fill the 48 output bytes of a row).
+int choose_split(long long ctas, int n_tiles, int sms) {
+  if (sms <= 0 || ctas <= 0) return 1;
+  int best = 1;
+  double best_t = 0.0;
+  for (int s = 1; s <= 3 && s <= n_tiles; ++s) {
+    const long long waves = (ctas * s + sms - 1) / sms;
+    const double t = static_cast<double>(waves) * ((n_tiles + s - 1) / s + 0.5) + (s > 1 ? 1.0 : 0.0);
+    if (s == 1 || t < best_t - 1e-9) {
+      best_t = t;
+      best = s;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -363,8 +437,9 @@ extern "C" int vb200_sim_topk(const void* query, int64_t q_row_stride, const voi
   if ((rc = make_rows_map(&tq, query, R, D, q_row_stride, kBM)) != VB200_OK) return rc;
   if (Nb > 0 && (rc = make_rows_map(&tb, basis, Nb, D, b_row_stride, tile_n)) != VB200_OK) return rc;
   if (Nb == 0) tb = tq;  // never read: every group then has zero basis tiles
-  TopkParams prm{values, indices, k, static_cast<int>(D / kBK), tile_n};
-  auto kernel = k == 1 ? sim_topk_kernel<1, false> : (max_nb <= 65536 ? sim_topk_kernel<4, true> : sim_topk_kernel<4, false>);
+  const bool keys4 = k == 4 && max_nb <= 65536;
+  TopkParams prm{values, indices, k, static_cast<int>(D / kBK), tile_n, 1};
+  auto kernel = k == 1 ? sim_topk_kernel<1, false> : (keys4 ? sim_topk_kernel<4, true> : sim_topk_kernel<4, false>);
   VB200_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
                    "cudaFuncSetAttribute");
   for (int64_t g0 = 0; g0 < groups; g0 += kMaxGroups) {
@@ -377,9 +452,19 @@ extern "C" int vb200_sim_topk(const void* query, int64_t q_row_stride, const voi
     }
     for (int64_t i = 0; i < ng; ++i) max_rows = std::max(max_rows, tab.q_begin[i + 1] - tab.q_begin[i]);
     if (max_rows == 0) continue;
-    const dim3 grid(static_cast<unsigned>((max_rows + kBM - 1) / kBM), static_cast<unsigned>(ng));
+    const long long ctas = ((max_rows + kBM - 1) / kBM) * ng;
+    // the split search keeps its per-piece keys in the 16-byte aligned output rows
+    const bool aligned = (reinterpret_cast<uintptr_t>(values) & 15u) == 0 && (reinterpret_cast<uintptr_t>(indices) & 15u) == 0;
+    prm.split = keys4 && aligned ? choose_split(ctas, static_cast<int>(n_tiles_max), sm_count_cached()) : 1;
+    const dim3 grid(static_cast<unsigned>((max_rows + kBM - 1) / kBM), static_cast<unsigned>(ng),
+                    static_cast<unsigned>(prm.split));
     kernel<<<grid, kThreads, kSmemBytes, st>>>(tq, tb, tab, prm);
     VB200_CHECK_LAUNCH("sim_topk_kernel");
+    if (prm.split > 1) {
+      const dim3 mgrid(static_cast<unsigned>((max_rows + 127) / 128), static_cast<unsigned>(ng));
+      topk_merge_kernel<<<mgrid, 128, 0, st>>>(tab, values, indices, prm.split);
+      VB200_CHECK_LAUNCH("topk_merge_kernel");
+    }
   }
   return VB200_OK;
 }
