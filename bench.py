@@ -5,9 +5,13 @@ dim 1024, 16 heads x 64, bf16, random-init weights (seed 0); input 32 frames of 
 (32,928 tokens ~ N(0,1)); merge 4x to 8,232 merged keys by the four-support convex planner
 (tcgen05 top-4 retrieval inside 4-frame groups, fused Gram + projected-gradient fit, mass =
 1 + pooled weights); then compact Q/K/V -> mass-bias attention -> proj -> top-4 restore.
-A step is that whole pass.  With N GPUs the 32 frames are split over the ranks (query-row
-sharding aligned to frame groups; merged K/V and log-mass all-gathered with NCCL): total
-work is fixed, so scaling is "strong".
+A step is that whole pass, submitted as one recorded CUDA graph.  With N GPUs the 32 frames
+are split over the ranks (query-row sharding aligned to frame groups; the compaction kernel
+writes every merged K/V row into all ranks' buffers over NVLink peer memory, the log-mass is
+gathered by peer loads): total work is fixed, so scaling is "strong".
+
+Components reported beside the headline: config 4 (256 frames, merge 8x, query rows sharded
+over the N ranks) at every N, and config 5 (top-4 projection bandwidth stress) at N = 1.
 
 Metric: frames/s of the whole job (value), with the attention TFLOP/s and projection GB/s of
 the same timed steps reported beside it.  Timing: W untimed warm-up steps; K timed steps,
@@ -15,6 +19,7 @@ each bracketed by CUDA events on the compute stream with an L2 flush (256 MB wri
 steps outside the events; barrier + synchronize around the loop; max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --projection-only     # config 5 alone on one GPU (for profiling its kernels)
 """
 from __future__ import annotations
 
@@ -536,10 +541,18 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--projection-only", action="store_true",
+                    help="run only the config-5 projection stress on one GPU and print its JSON")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    if args.impl == "reference":
+    if args.projection_only:
+        import torch
+        pkg = importlib.import_module("4d_ttt_merging_b200")
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        print(json.dumps(projection_stress(pkg, dev, _peaks()[0])), flush=True)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
