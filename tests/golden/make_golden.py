@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the CPU oracle to the reference implementation.
 
 Runs the reference's own PyTorch code (shuang-yang18/4D_TTT_merging, imported read-only from
-REFERENCE_ROOT, default /root/reference) on CPU with seeded inputs and stores inputs and
+the checkout named by --reference or REFERENCE_ROOT) on CPU with seeded inputs and stores inputs and
 outputs in ``tests/golden/golden.npz``.  It is run once in the build container; the GPU box
 never needs the reference.  Cases:
 
