@@ -33,6 +33,8 @@ _SIGNATURES = {
     "vb200_device_error_flags": (_c_int, [ctypes.POINTER(ctypes.c_uint), _c_int]),
     "vb200_mass_bias_attention_workspace_size": (_c_size, [_c_i64]),
     "vb200_mass_bias_attention_split_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
+    "vb200_mass_bias_attention_plan": (_c_int, [_c_i64, _c_i64, _c_i64, _c_i64, _c_int, _p_i64]),
+    "vb200_sim_topk_split": (_c_int, [_c_i64, _c_int, _c_int]),
     "vb200_mass_bias_attention": (
         _c_int,
         [_c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,

@@ -781,6 +781,18 @@ SplitPlan plan_split(long long B, long long H, long long Nq, int n_tiles, int n_
 
 }  // namespace
 
+extern "C" int vb200_mass_bias_attention_plan(int64_t B, int64_t H, int64_t Nq, int64_t Nk, int sms, int64_t* out) {
+  VB200_REQUIRE(out != nullptr && B >= 1 && H >= 1 && Nq >= 0 && Nk >= 1 && sms >= 0,
+                "mass_bias_attention_plan: bad arguments");
+  const SplitPlan sp = plan_split(B, H, Nq, static_cast<int>((Nk + kBN - 1) / kBN), sms);
+  out[0] = sp.items;
+  out[1] = sp.n_full;
+  out[2] = sp.n_tail;
+  out[3] = sp.split;
+  out[4] = static_cast<int64_t>(sp.o_bytes + sp.ml_bytes + sp.cnt_bytes);
+  return VB200_OK;
+}
+
 extern "C" size_t vb200_mass_bias_attention_split_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t Nk) {
   const size_t base = vb200_mass_bias_attention_workspace_size(Nk);
   if (B < 1 || H < 1 || Nq < 1 || Nk < 1) return base;

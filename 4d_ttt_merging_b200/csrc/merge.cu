@@ -398,6 +398,10 @@ unsigned merge_error_word(int clear) {
 
 using namespace vb200;
 
+extern "C" int vb200_sim_topk_split(int64_t ctas, int n_tiles, int sms) {
+  return choose_split(ctas, n_tiles, sms);
+}
+
 extern "C" int vb200_sim_topk(const void* query, int64_t q_row_stride, const void* basis,
                               int64_t b_row_stride, int64_t R, int64_t Nb, int64_t D, int k,
                               const int64_t* q_begin, const int64_t* b_begin, int64_t groups,

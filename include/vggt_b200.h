@@ -72,6 +72,11 @@ VB200_API size_t vb200_mass_bias_attention_workspace_size(int64_t Nk);
  * With a workspace of vb200_mass_bias_attention_workspace_size(Nk) bytes the launch runs
  * unsplit. */
 VB200_API size_t vb200_mass_bias_attention_split_workspace_size(int64_t B, int64_t H, int64_t Nq, int64_t Nk);
+/* The launch plan of the tensor-core attention for `sms` SMs (host arithmetic only, no device
+ * call): out[0] work items ((256-query block, head) pairs), out[1] items run whole, out[2]
+ * items of the last partial wave split into key ranges, out[3] key ranges per split item,
+ * out[4] extra workspace bytes for the split (beyond workspace_size(Nk)). */
+VB200_API int vb200_mass_bias_attention_plan(int64_t B, int64_t H, int64_t Nq, int64_t Nk, int sms, int64_t* out);
 VB200_API int vb200_mass_bias_attention(int dtype, const void* q, const void* k, const void* v,
                               const void* log_key_mass, int bias_dtype, void* out, int64_t B,
                               int64_t H, int64_t Nq, int64_t Nk, int64_t D,
@@ -236,6 +241,11 @@ VB200_API int vb200_peer_push(const void* src, int64_t rows, int64_t src_stride_
 VB200_API int vb200_row_normalize_bf16(int dtype, const void* x, int64_t x_rows, int64_t x_row_stride, const int64_t* rows,
                              int64_t R, int64_t C, float eps, void* out, int64_t out_row_stride,
                              void* stream);
+
+/* Basis-range pieces per query block that vb200_sim_topk uses for a launch of `ctas` CTAs over
+ * n_tiles basis tiles on `sms` SMs (host arithmetic only; 1 = unsplit, at most 3; a split search
+ * stores per-piece keys in the output rows and merges them in a second small kernel). */
+VB200_API int vb200_sim_topk_split(int64_t ctas, int n_tiles, int sms);
 
 /* Cosine-similarity GEMM with a fused running top-k epilogue (k = 1 or 4).
  * score[r, n] = bf16_round( <query[r], basis[n]> ) over D channels (fp32 accumulation on

@@ -87,3 +87,41 @@ def test_peer_exchange_argument_checks(pkg):
     assert rc == pkg._clib.EINVAL and b"multiples of 4" in lib.vb200_last_error()
     rc = lib.vb200_peer_push(8, 1, 16, 16, one, 1, 0, 16, None)  # source not 16-byte aligned
     assert rc == pkg._clib.EINVAL and b"16-byte" in lib.vb200_last_error()
+
+
+def _attention_plan(lib, B, H, Nq, Nk, sms):
+    out = (ctypes.c_int64 * 5)()
+    assert lib.vb200_mass_bias_attention_plan(B, H, Nq, Nk, sms, out) == 0
+    return list(out)
+
+
+def test_attention_launch_plan(pkg):
+    """The last-wave key split of the attention launch (host arithmetic, no GPU)."""
+    lib = pkg.load_library()
+    # config 2: 33 query blocks x 16 heads = 528 items on 148 SMs -> 3 whole waves + 84 split
+    items, n_full, n_tail, split, extra = _attention_plan(lib, 1, 16, 8232, 8232, 148)
+    assert (items, n_full, n_tail) == (528, 444, 84) and 2 <= split <= 4 and extra > 0
+    # the split is what the cost model says: ceil(tail * s / SMs) rounds of (1/s + 3/65)
+    cost = lambda s: -(-84 * s // 148) * (1 / s + 3 / 65)  # noqa: E731
+    assert cost(split) == min(cost(s) for s in range(1, 5))
+    # a whole number of waves, or a single key tile: nothing to split
+    assert _attention_plan(lib, 1, 148, 256, 8232, 148)[3] == 1
+    assert _attention_plan(lib, 1, 16, 8232, 100, 148)[3] == 1
+    # N = 8 shard of config 2: 5 query blocks x 16 heads = 80 items, fewer than the SMs
+    items, n_full, n_tail, split, _ = _attention_plan(lib, 1, 16, 1029, 8232, 148)
+    assert (items, n_full, n_tail) == (80, 0, 80) and split > 1
+    # the workspace query agrees with the plan
+    assert lib.vb200_mass_bias_attention_split_workspace_size(1, 16, 8232, 8232) == \
+        lib.vb200_mass_bias_attention_workspace_size(8232) + _attention_plan(lib, 1, 16, 8232, 8232, 148)[4] \
+        or lib.vb200_mass_bias_attention_split_workspace_size(1, 16, 8232, 8232) == \
+        lib.vb200_mass_bias_attention_workspace_size(8232)  # no device here: SM count unknown -> unsplit
+
+
+def test_topk_split_choice(pkg):
+    lib = pkg.load_library()
+    assert lib.vb200_sim_topk_split(200, 5, 148) == 1   # config 2, 8 frame groups: enough CTAs
+    assert lib.vb200_sim_topk_split(25, 5, 148) == 3    # one frame group (N = 8 shard)
+    assert lib.vb200_sim_topk_split(25, 1, 148) == 1    # a single basis tile cannot split
+    assert lib.vb200_sim_topk_split(25, 2, 148) == 1    # halving 2 tiles does not pay for the merge launch
+    assert lib.vb200_sim_topk_split(25, 3, 148) == 3
+    assert lib.vb200_sim_topk_split(10, 5, 0) == 1      # unknown SM count
