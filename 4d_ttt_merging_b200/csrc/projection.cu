@@ -628,7 +628,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
 // on neighbouring merged rows, whose sources overlap and stay in L2.  Per item a consumer thread
 // reads 16 bytes and one float2 of statistics from shared memory and does 4 packed FMAs; the
 // copy engine keeps up to kStageSlots rows in flight per CTA without holding registers.
-constexpr int kStageSlots = 16;
+// Ring slots per CTA.  Measured on config 2 (compact_qkv incl. statistics, 16 channels per
+// thread): 16 slots x 2 CTAs/SM 171 us, 10 x 3 159 us, 8 x 3 146 us, 8 x 4 138 us (8-channel
+// threads, 16 x 2: 165 us).  Many small CTAs beat deep rings.
+constexpr int kStageSlots = 8;
 constexpr int kIssueLanes = 4;  // producer lanes that issue copies together
 constexpr int kStageHeaderBytes = 512;
 
@@ -668,8 +671,10 @@ __device__ __forceinline__ void multimem_st16(void* p, const uint4& v) {
 }
 static_assert(2 * kStageSlots * 8 + kStageSlots * sizeof(StageSlotMeta) <= kStageHeaderBytes, "stage header");
 
-template <typename T>
-__global__ void __launch_bounds__(416, 2)
+// kCh channels per consumer thread: 16 when 3C/16 threads make whole warps (C = 512, 1024),
+// else 8 (C = 256); 16 halves the per-item bookkeeping (slot wait, vote, release) per channel.
+template <typename T, int kCh>
+__global__ void __launch_bounds__(kCh == 8 ? 416 : 224, kCh == 8 ? 2 : 4)
     compact_qkv_staged_kernel(const T* __restrict__ qkv, long long rows, long long xs, int C,
                               const float* __restrict__ ln_w, const float* __restrict__ ln_b,
                               const float2* __restrict__ stats, const int64_t* __restrict__ keep, long long M,
@@ -678,7 +683,7 @@ __global__ void __launch_bounds__(416, 2)
                               const float* __restrict__ normalizer, int pool_mask, T* __restrict__ out,
                               long long os, const __grid_constant__ KvPeers peers) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int n_cons = 3 * C / 8;  // consumer threads, a whole number of warps (C % 256 == 0)
+  const int n_cons = 3 * C / kCh;  // consumer threads, a whole number of warps
   const int heads2 = 2 * C / 64;
   const uint32_t row_bytes = static_cast<uint32_t>(3 * C * sizeof(T));
   const uint32_t stat_bytes = ln_w != nullptr ? static_cast<uint32_t>(heads2 * sizeof(float2)) : 0u;
@@ -777,12 +782,13 @@ __global__ void __launch_bounds__(416, 2)
   }
 
   // ------------------------------- consumers -------------------------------
-  // Thread i owns channels [8i, 8i + 8) of the q|k|v row (one tensor, one LayerNorm head).
-  // Each item is released as soon as the warp has read it; each 16-bit pair becomes an fp32 pair
-  // for one packed FMA.
+  // Thread i owns channels [kCh i, kCh i + kCh) of the q|k|v row (one tensor, one LayerNorm
+  // head).  Each item is released as soon as the warp has read it; each 16-bit pair becomes an
+  // fp32 pair for one packed FMA.
+  constexpr int kVecs = kCh / 8;  // 16-byte vectors per thread
   const int i = threadIdx.x;
-  const int t = i / (C / 8);             // tensor: 0 q, 1 k, 2 v
-  const int col = (i - t * (C / 8)) * 8;  // channel within the tensor
+  const int t = i / (C / kCh);               // tensor: 0 q, 1 k, 2 v
+  const int col = (i - t * (C / kCh)) * kCh;  // channel within the tensor
   const bool ln = ln_w != nullptr && t < 2;
   const bool pooled_t = (pool_mask >> t) & 1;
   const int stat_idx = t * (C / 64) + col / 64;
@@ -792,9 +798,9 @@ __global__ void __launch_bounds__(416, 2)
     const int e0 = pooled_any ? seg_offsets[j * corners] : 0;
     const int e1 = pooled_any ? seg_offsets[(j + 1) * corners] : 0;
     const int n_items = e1 - e0 + 1;
-    uint64_t acc2[4];
+    uint64_t acc2[kCh / 2];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc2[q] = 0ull;  // (+0.0f, +0.0f)
+    for (int q = 0; q < kCh / 2; ++q) acc2[q] = 0ull;  // (+0.0f, +0.0f)
     float csum = 0.f, wsum = 0.f;
     for (int u = 0; u < n_items; ++u) {
       const long long it = item + u;
@@ -811,45 +817,54 @@ __global__ void __launch_bounds__(416, 2)
           a *= st.y;  // w r
           csum = fmaf(a, st.x, csum);
         }
-        const uint4 r0 = *reinterpret_cast<const uint4*>(base + static_cast<size_t>(i) * 16);
+        uint4 r0[kVecs];
+#pragma unroll
+        for (int v = 0; v < kVecs; ++v) r0[v] = reinterpret_cast<const uint4*>(base)[i * kVecs + v];
         const uint64_t a2 = pk2(a, a);
-        acc2[0] = ffma2(a2, unpack2<T>(r0.x), acc2[0]);
-        acc2[1] = ffma2(a2, unpack2<T>(r0.y), acc2[1]);
-        acc2[2] = ffma2(a2, unpack2<T>(r0.z), acc2[2]);
-        acc2[3] = ffma2(a2, unpack2<T>(r0.w), acc2[3]);
+#pragma unroll
+        for (int v = 0; v < kVecs; ++v) {
+          acc2[4 * v + 0] = ffma2(a2, unpack2<T>(r0[v].x), acc2[4 * v + 0]);
+          acc2[4 * v + 1] = ffma2(a2, unpack2<T>(r0[v].y), acc2[4 * v + 1]);
+          acc2[4 * v + 2] = ffma2(a2, unpack2<T>(r0[v].z), acc2[4 * v + 2]);
+          acc2[4 * v + 3] = ffma2(a2, unpack2<T>(r0[v].w), acc2[4 * v + 3]);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
     }
     item += n_items;
     if (!ok) break;
-    float acc[8];
+    float acc[kCh];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) upk2(acc2[q], acc[2 * q], acc[2 * q + 1]);
+    for (int q = 0; q < kCh / 2; ++q) upk2(acc2[q], acc[2 * q], acc[2 * q + 1]);
     if (ln) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
+      for (int q = 0; q < kCh; ++q)
         acc[q] = fmaf(__ldg(ln_w + t * 64 + col % 64 + q), acc[q] - csum, __ldg(ln_b + t * 64 + col % 64 + q) * wsum);
     }
     if (pooled_t) {
       const float norm = normalizer[j];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] = __fdiv_rn(acc[q], norm);
+      for (int q = 0; q < kCh; ++q) acc[q] = __fdiv_rn(acc[q], norm);
     }
-    uint4 raw;
-    T* e = reinterpret_cast<T*>(&raw);
+    uint4 raw[kVecs];
+    T* e = reinterpret_cast<T*>(raw);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) e[q] = from_f32<T>(acc[q]);
-    *reinterpret_cast<uint4*>(out + j * os + t * C + col) = raw;
+    for (int q = 0; q < kCh; ++q) e[q] = from_f32<T>(acc[q]);
+#pragma unroll
+    for (int v = 0; v < kVecs; ++v) reinterpret_cast<uint4*>(out + j * os + t * C + col)[v] = raw[v];
     if (t > 0 && peers.world > 0) {
       // the k|v all-gather, fused: posted stores straight into every rank's key/value buffer
       // (one multicast store, or one store per rank)
       const long long off = (peers.row0 + j) * peers.stride + (t - 1) * C + col;
-      if (peers.multicast) {
-        multimem_st16(reinterpret_cast<T*>(peers.dst[0]) + off, raw);
-      } else {
-        for (int r = 0; r < peers.world; ++r)
-          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(peers.dst[r]) + off) = raw;
+#pragma unroll
+      for (int v = 0; v < kVecs; ++v) {
+        if (peers.multicast) {
+          multimem_st16(reinterpret_cast<T*>(peers.dst[0]) + off + 8 * v, raw[v]);
+        } else {
+          for (int r = 0; r < peers.world; ++r)
+            reinterpret_cast<uint4*>(reinterpret_cast<T*>(peers.dst[r]) + off)[v] = raw[v];
+        }
       }
     }
   }
@@ -1379,26 +1394,37 @@ int compact_qkv_impl(int dtype, const void* qkv, int64_t rows, int64_t xs, int64
     VB200_CHECK_LAUNCH("head_stats_kernel");
   }
   if (C <= 1024) {
-    // staged path: one producer warp + 3C/256 consumer warps per CTA, two CTAs per SM
-    const int threads = static_cast<int>(3 * C / 8) + 32;
+    // staged path: one producer warp + 3C/kCh consumer threads per CTA; four CTAs per SM with
+    // 16-channel threads, two with 8
+    const int ch = (3 * C / 16) % 32 == 0 ? 16 : 8;
+    const int threads = static_cast<int>(3 * C / ch) + 32;
     const size_t smem = kStageHeaderBytes +
                         static_cast<size_t>(kStageSlots) * (3 * C * 2 + (ln_weight ? 2 * C / 64 * sizeof(float2) : 0));
     int dev = 0, sms = 0;
     VB200_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
     VB200_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
-    const unsigned grid = static_cast<unsigned>(M < 2ll * sms ? M : 2ll * sms);
-#define VB200_CQKV_STAGED(T)                                                                                     \
-  VB200_CHECK_CUDA(cudaFuncSetAttribute(compact_qkv_staged_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                        static_cast<int>(smem)),                                                 \
-                   "cudaFuncSetAttribute");                                                                      \
-  compact_qkv_staged_kernel<T><<<grid, threads, smem, st>>>(                                                     \
-      static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, stats, keep, M,             \
-      static_cast<int>(corners), seg_offsets, entry_src, entry_w, normalizer, pool_mask, static_cast<T*>(out), os, \
-      peers)
+    const long long per_sm = ch == 16 ? 4 : 2;
+    const unsigned grid = static_cast<unsigned>(M < per_sm * sms ? M : per_sm * sms);
+#define VB200_CQKV_STAGED(T, CH)                                                                               \
+  VB200_CHECK_CUDA(cudaFuncSetAttribute(compact_qkv_staged_kernel<T, CH>,                                      \
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),  \
+                   "cudaFuncSetAttribute");                                                                    \
+  compact_qkv_staged_kernel<T, CH><<<grid, threads, smem, st>>>(                                               \
+      static_cast<const T*>(qkv), rows, xs, static_cast<int>(C), ln_weight, ln_bias, stats, keep, M,           \
+      static_cast<int>(corners), seg_offsets, entry_src, entry_w, normalizer, pool_mask, static_cast<T*>(out), \
+      os, peers)
     if (dtype == VB200_BF16) {
-      VB200_CQKV_STAGED(__nv_bfloat16);
+      if (ch == 16) {
+        VB200_CQKV_STAGED(__nv_bfloat16, 16);
+      } else {
+        VB200_CQKV_STAGED(__nv_bfloat16, 8);
+      }
     } else {
-      VB200_CQKV_STAGED(__half);
+      if (ch == 16) {
+        VB200_CQKV_STAGED(__half, 16);
+      } else {
+        VB200_CQKV_STAGED(__half, 8);
+      }
     }
 #undef VB200_CQKV_STAGED
     VB200_CHECK_LAUNCH("compact_qkv_staged_kernel");
