@@ -8,7 +8,9 @@ make that equal to the single-GPU block, using the numpy oracle for the math:
   * gather_merged concatenates in rank order over a real process group;
   * planning each shard alone gives exactly the restriction of the global plan, and the
     gathered merged keys are the global merged keys in the global order, so the sharded block
-    reproduces the single-process block row for row.
+    reproduces the single-process block row for row;
+  * a rank that exits between steps makes the others' next exchange end with an error
+    instead of a hang (failure detection on the host, no GPU involved).
 """
 from __future__ import annotations
 
@@ -138,3 +140,39 @@ def test_sharded_block_equals_single_process(tmp_path):
         np.testing.assert_allclose(r["kc_all"], kc_g, rtol=0, atol=1e-5)
         np.testing.assert_allclose(r["lm_all"], lm_g, rtol=0, atol=1e-6)
         np.testing.assert_allclose(r["y"], y_full[shard.token_begin:shard.token_end], rtol=0, atol=1e-5)
+
+
+def _failing_rank_main(rank: int, world: int, init_file: str, out_dir: str) -> None:
+    """Rank 1 dies right after joining (no collective in flight); rank 0 then runs the layer's
+    all-gather and must get an error back (peer gone, or the short process-group timeout), not
+    wait forever."""
+    import time
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # a rank that exits between steps
+    pkg = _pkg()
+    t0 = time.monotonic()
+    try:
+        pkg.parallel.gather_merged([torch.zeros(4, 8), torch.zeros(4)])
+        outcome = "completed"
+    except Exception as err:  # noqa: BLE001 - any error is the expected outcome
+        outcome = f"error {type(err).__name__}"
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as fh:
+        fh.write(f"{outcome} {time.monotonic() - t0:.1f}")
+    os._exit(0)
+
+
+def test_dead_rank_ends_the_exchange_with_an_error(tmp_path):
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_failing_rank_main, args=(r, 2, str(tmp_path / "init"), str(tmp_path)))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(not p.is_alive() for p in procs), "a rank is still waiting"
+    assert procs[1].exitcode == 3 and procs[0].exitcode == 0
+    outcome = (tmp_path / "rank0.txt").read_text().split()
+    assert outcome[0] == "error", outcome
+    assert float(outcome[-1]) < 60.0
