@@ -53,10 +53,11 @@ static_assert(kSoftmaxWarps * 32 * kRegsHigh + 128 * kRegsLow == kThreads * kLau
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // lazy rescale: P stays <= 2^8
 // Of every 8 exponent pairs, how many are computed on the FMA pipe (exp2_poly2) instead of
-// MUFU (16 exponentials per clock per SM).  Measured on the config-2 attention: 2 of 8 is
-// fastest (0: 459 us, 1: 414 us, 2: 407 us, 3: 457 us); beyond that the extra instructions
-// take issue slots from the MMA warp.
-constexpr int kPolyPairs = 2;
+// MUFU (16 exponentials per clock per SM).  Measured on the config-2 attention (split launch):
+// 1: 399 us, 2: 413 us, 3: 430 us; with the earlier per-tile max exchange 2 of 8 had been
+// fastest (0: 459, 1: 414, 2: 407, 3: 457 us).  Beyond that the extra instructions take issue
+// slots from the MMA warp.
+constexpr int kPolyPairs = 1;
 constexpr int kNamedBarPair = 1;  // named barriers 1, 2: the two warpgroups of query tile 0, 1
 constexpr int kNamedBarSoftmax = 3;  // all softmax warps (the split epilogue)
 // Key-range split of the last partial wave: at most this many pieces per (query block, head).
