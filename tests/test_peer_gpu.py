@@ -49,13 +49,14 @@ def test_peer_push_to_every_rank(pkg, cuda_device):
         assert torch.equal(f, expect)
 
 
-def test_compact_qkv_peer_writes_every_rank(pkg, cuda_device):
+@pytest.mark.parametrize("dim", [256, 1024])  # 8- and 16-channel consumer threads
+def test_compact_qkv_peer_writes_every_rank(pkg, cuda_device, dim):
     """The compaction with the fused k|v all-gather: `out` equals the plain compaction bit for
     bit, and every destination buffer (three local buffers standing in for the ranks) holds the
     merged k|v rows at the given row offset, other rows untouched."""
     dev = cuda_device
     g = torch.Generator(device="cpu").manual_seed(3)
-    frames, tpf, dim = 4, 100, 256
+    frames, tpf = 4, 100
     tok = torch.randn(1, frames * tpf, dim, generator=g).to(dev, torch.bfloat16)
     plan = pkg.build_uniform_convex_plan(tok, frames=frames, tokens_per_frame=tpf, patch_token_start=5,
                                          merge_factor=4, group_frames=4)
