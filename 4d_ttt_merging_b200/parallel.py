@@ -81,11 +81,15 @@ class PeerExchange:
 
     One symmetric allocation per GPU (PyTorch symmetric memory: the same-sized buffer on every
     GPU, mapped into every rank's address space) holds this rank's compacted q|k|v rows, its
-    log-mass vector and the full rank-ordered K|V buffer.  `exchange` runs a device-side
-    barrier (every rank has compacted, and has finished with its previous full buffer), then
-    `vb200_peer_push` stores this rank's K|V rows into every rank's full buffer (posted NVLink
-    writes) and `vb200_peer_gather` reads every rank's log-mass, then a second barrier (all
-    writes landed).  Ranks must have the same number of merged rows.  The barriers give up
+    log-mass vector and the full rank-ordered K|V buffer.
+
+    Fused form (what ShardedGlobalBlock uses): `begin` is a device barrier (every rank has
+    finished reading its previous full buffer and published its log-mass); the compaction
+    kernel then stores every merged k|v row into all ranks' full buffers itself (`kv_peers`:
+    posted NVLink writes, or one multicast store per row part when opted in); `finish` reads
+    every rank's log-mass with `vb200_peer_gather` and ends with a second barrier (all writes
+    landed).  Unfused form: `exchange` pushes the finished rows with `vb200_peer_push` between
+    the same two barriers.  Ranks must have the same number of merged rows.  The barriers give up
     after BARRIER_TIMEOUT_MS (a rank that never arrives ends the wait instead of spinning
     forever)."""
 
