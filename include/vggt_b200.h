@@ -62,7 +62,10 @@ VB200_API int vb200_device_error_flags(unsigned* flags, int clear);
  * strides: {batch, head, token} for each of q, k, v, out; the channel stride is 1.
  * workspace: device scratch of vb200_mass_bias_attention_workspace_size(Nk) bytes (4 KB per
  *   128-key tile: the bias operand of the QK product, or the padded fp32 bias of the fp32
- *   path), 256-byte aligned. */
+ *   path), 256-byte aligned; or vb200_mass_bias_attention_split_workspace_size bytes (below)
+ *   for the split launch.  The call rewrites everything it reads from the workspace, so
+ *   nothing carries over between calls, but calls that may run concurrently (other streams)
+ *   need separate workspaces. */
 VB200_API size_t vb200_mass_bias_attention_workspace_size(int64_t Nk);
 /* Workspace that also lets the tensor-core launch split its last, partially filled wave of
  * (256-query block, head) items into key ranges on the current device: the bytes above plus
