@@ -1039,9 +1039,12 @@ extern "C" int vb200_mass_bias_attention_noalloc(int dtype, const void* q, const
   const int rc = noalloc_scratch(&scratch);
   if (rc != VB200_OK) return rc;
   // The bias kernel rewrites every scratch entry the attention kernel reads (real keys and the
-  // -inf padding of the last tile), so nothing carries over from a previous call.
+  // -inf padding of the last tile), so nothing carries over from a previous call.  Only the
+  // bias operand's share of the array is offered as workspace: with no room for split partial
+  // results the launch is always the unsplit one, so the fixed array holds nothing but the bias
+  // and the result equals vb200_mass_bias_attention given workspace_size(Nk) bytes.
   return vb200_mass_bias_attention(dtype, q, k, v, log_key_mass, bias_dtype, out, B, H, Nq, Nk, D, qs, ks,
-                                   vs, os, scratch, kNoAllocBytes, stream);
+                                   vs, os, scratch, vb200_mass_bias_attention_workspace_size(Nk), stream);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -87,7 +87,9 @@ VB200_API int vb200_mass_bias_attention(int dtype, const void* q, const void* k,
                               const int64_t* v_strides, const int64_t* o_strides,
                               void* workspace, size_t workspace_bytes, void* stream);
 
-/* Same computation as vb200_mass_bias_attention, for callers that cannot allocate device
+/* Same computation as vb200_mass_bias_attention given the minimal workspace
+ * (vb200_mass_bias_attention_workspace_size(Nk) bytes): it always takes the unsplit launch,
+ * and its output is bit-identical to that call's.  It is for callers that cannot allocate device
  * memory: code that only holds raw device pointers handed over by another runtime (no
  * allocator to get a workspace from) and latency-critical loops that must not call
  * cudaMalloc / cudaFree, which synchronise the device.  It allocates nothing: its scratch (the

@@ -16,7 +16,7 @@ __all__ = [
     "round_bf16", "round_f16", "round_to", "bf16_to_f32_bits",
     "mass_bias_attention", "normalizer", "compact", "compact_key", "restore",
     "token_plan_compact", "token_plan_restore", "topk_scores", "similarity_topk",
-    "torch_cpu_rand", "fastvggt_plan", "projected_gradient", "active_set",
+    "torch_cpu_rand", "fastvggt_plan", "fastvggt_assign", "fastvggt_removed", "normalize_bf16", "projected_gradient", "active_set",
     "simplex_project", "layer_norm", "global_attention_forward",
 ]
 
@@ -281,6 +281,15 @@ def torch_cpu_rand(seed: int, count: int) -> np.ndarray:
     return ((raw & ((1 << 24) - 1)).astype(np.float64) * 2.0 ** -24).astype(np.float32)
 
 
+def normalize_bf16(x) -> np.ndarray:
+    """``F.normalize(x.float(), dim=-1).to(bfloat16)`` (token_merging.py:1102-1103): the row
+    norm in float64 rounded to fp32, clamped at 1e-12, the fp32 quotient rounded to bf16."""
+    x = np.asarray(x, dtype=np.float32)
+    x64 = x.astype(np.float64)
+    n = np.sqrt((x64 * x64).sum(axis=1, keepdims=True)).astype(np.float32)
+    return round_bf16((x / np.maximum(n, np.float32(1e-12))).astype(np.float32))
+
+
 def _patch_ids(frames, tokens_per_frame, patch_token_start):
     patches = tokens_per_frame - patch_token_start
     return (np.arange(frames)[:, None] * tokens_per_frame + patch_token_start + np.arange(patches)[None, :])
@@ -323,19 +332,32 @@ def fastvggt_plan(tokens, *, frames, tokens_per_frame, patch_token_start, patch_
         protected[np.arange(0, total, max(1, total // count))[:count]] = True
     source_indices = np.nonzero(~(destination | protected))[0]
     destination_indices = np.nonzero(destination)[0]
-    removed = min(int(total * merge_ratio), source_indices.size)
+    removed = fastvggt_removed(total, merge_ratio, source_indices.size)
     if removed == 0:
         return identity, identity, None, None, None, None
-
-    def normalize_bf16(x):
-        x64 = x.astype(np.float64)
-        n = np.sqrt((x64 * x64).sum(axis=1, keepdims=True)).astype(np.float32)
-        return round_bf16((x / np.maximum(n, 1e-12)).astype(np.float32))
 
     src = normalize_bf16(tokens[source_indices])
     dst = normalize_bf16(tokens[destination_indices])
     values, idx = similarity_topk(src, dst, 1)
     best, targets = values[:, 0], idx[:, 0]
+    keep, inverse = fastvggt_assign(best, targets, source_indices, destination_indices, total, removed)
+    return keep, inverse, best, targets, source_indices, destination_indices
+
+
+def fastvggt_removed(total: int, merge_ratio: float, sources: int) -> int:
+    """Number of merged sources, token_merging.py:1096."""
+    return min(int(total * merge_ratio), sources)
+
+
+def fastvggt_assign(best, targets, source_indices, destination_indices, total: int, removed: int):
+    """The ranking half of build_fastvggt_plan (token_merging.py:1112-1121): sources sorted by
+    their best score, descending and stable; the first ``removed`` are merged into their
+    argmax destination.  Returns (keep [total - removed], inverse [total])."""
+    best = np.asarray(best, dtype=np.float32)
+    targets = np.asarray(targets, dtype=np.int64)
+    source_indices = np.asarray(source_indices, dtype=np.int64)
+    destination_indices = np.asarray(destination_indices, dtype=np.int64)
+    identity = np.arange(total)
     ranked = np.argsort(-best, kind="stable")
     removed_source = source_indices[ranked[:removed]]
     target_original = destination_indices[targets[ranked[:removed]]]
@@ -346,7 +368,7 @@ def fastvggt_plan(tokens, *, frames, tokens_per_frame, patch_token_start, patch_
     original_to_compact[keep] = np.arange(keep.size)
     inverse = original_to_compact.copy()
     inverse[removed_source] = original_to_compact[target_original]
-    return keep, inverse, best, targets, source_indices, destination_indices
+    return keep, inverse
 
 
 # ------------------------------------------------------------------------------------------

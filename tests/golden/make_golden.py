@@ -73,8 +73,11 @@ def make_plan(WeightedBilinearTokenPlan, deterministic_weighted_normalizer, gen,
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("REFERENCE_ROOT"),
+                    help="reference checkout (default: $REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or REFERENCE_ROOT")
     sys.path.insert(0, args.reference)
     from vggt_omega.models.layers.attention import SelfAttention
     from vggt_omega.models.sparse_convex import _adaptive_fit, _convex_fit

@@ -2,15 +2,20 @@
 ABI.  It serves callers that cannot allocate device memory (raw pointers from another
 runtime, or loops that must not call cudaMalloc / cudaFree because those synchronise the
 device); its scratch is a fixed array inside the library.  The test compares it with the
-workspace entry point on two calls in a row — the second with fewer keys, so any scratch left
-over from the first call would show — and checks the size limit.
+workspace entry point on calls in a row — the second with fewer keys, so any scratch left
+over from the first call would show, and a last one with 131,072 keys, the most the fixed
+array holds — and checks the size limit.
+
+The fixed array only ever holds the bias operand, so the no-allocation call always takes the
+unsplit launch.  The first shape is one the split planner would split on a B200, so the
+comparison with the minimal-workspace call (which cannot split either) shows that form: the
+two outputs are bit-identical.
 
 Collected last (file name) so a run that stops at the first failure has run everything else."""
 from __future__ import annotations
 
 import ctypes
 
-import numpy as np
 import pytest
 import torch
 
@@ -25,22 +30,23 @@ def _strides(t):
     return (ctypes.c_int64 * 3)(*t.stride()[:3])
 
 
-def _inputs(seed, Nq, Nk, dev):
+def _inputs(seed, H, Nq, Nk, dev):
     g = torch.Generator(device="cpu").manual_seed(seed)
-    q = torch.randn(1, 4, Nq, 64, generator=g).to(dev, torch.bfloat16)
-    k = torch.randn(1, 4, Nk, 64, generator=g).to(dev, torch.bfloat16)
-    v = torch.randn(1, 4, Nk, 64, generator=g).to(dev, torch.bfloat16)
+    q = torch.randn(1, H, Nq, 64, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(1, H, Nk, 64, generator=g).to(dev, torch.bfloat16)
+    v = torch.randn(1, H, Nk, 64, generator=g).to(dev, torch.bfloat16)
     lm = torch.log(torch.randint(1, 20, (Nk,), generator=g).float()).to(dev)
     return q, k, v, lm
 
 
 def _with_workspace(lib, q, k, v, lm):
+    """The workspace entry point with the minimal workspace (bias operand only)."""
     out = torch.empty_like(q)
-    Nk = k.shape[2]
+    H, Nk = q.shape[1], k.shape[2]
     ws_bytes = lib.vb200_mass_bias_attention_workspace_size(Nk)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
     rc = lib.vb200_mass_bias_attention(1, q.data_ptr(), k.data_ptr(), v.data_ptr(), lm.data_ptr(), 0,
-                                       out.data_ptr(), 1, 4, q.shape[2], Nk, 64, _strides(q), _strides(k),
+                                       out.data_ptr(), 1, H, q.shape[2], Nk, 64, _strides(q), _strides(k),
                                        _strides(v), _strides(out), ws.data_ptr(), ws_bytes,
                                        torch.cuda.current_stream().cuda_stream)
     assert rc == 0, lib.vb200_last_error()
@@ -50,8 +56,8 @@ def _with_workspace(lib, q, k, v, lm):
 def _no_alloc(lib, q, k, v, lm):
     out = torch.empty_like(q)
     rc = lib.vb200_mass_bias_attention_noalloc(1, q.data_ptr(), k.data_ptr(), v.data_ptr(), lm.data_ptr(), 0,
-                                               out.data_ptr(), 1, 4, q.shape[2], k.shape[2], 64, _strides(q),
-                                               _strides(k), _strides(v), _strides(out),
+                                               out.data_ptr(), 1, q.shape[1], q.shape[2], k.shape[2], 64,
+                                               _strides(q), _strides(k), _strides(v), _strides(out),
                                                torch.cuda.current_stream().cuda_stream)
     assert rc == 0, lib.vb200_last_error()
     return out
@@ -59,12 +65,18 @@ def _no_alloc(lib, q, k, v, lm):
 
 def test_no_alloc_matches_workspace_entry_point(pkg, cuda_device):
     lib = pkg.load_library()
-    for seed, (Nq, Nk) in enumerate([(300, 2000), (257, 333)]):  # second call uses fewer keys
-        q, k, v, lm = _inputs(seed, Nq, Nk, cuda_device)
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    plan = (ctypes.c_int64 * 5)()
+    assert lib.vb200_mass_bias_attention_plan(1, 4, 300, 2000, sms, plan) == 0
+    assert plan[3] > 1  # a caller workspace with room for partials would split this shape
+    # second call uses fewer keys; the last fills the fixed array exactly
+    for seed, (H, Nq, Nk) in enumerate([(4, 300, 2000), (4, 257, 333), (1, 130, MAX_KEYS)]):
+        q, k, v, lm = _inputs(seed, H, Nq, Nk, cuda_device)
         ref = _with_workspace(lib, q, k, v, lm)
         got = _no_alloc(lib, q, k, v, lm)
         torch.cuda.synchronize()
         assert_close(to_np(got), to_np(ref), "bf16")
+        assert torch.equal(got, ref)  # same (unsplit) launch, same bits
     assert pkg.device_error_flags() == 0
 
 
