@@ -18,6 +18,10 @@ the same timed steps reported beside it.  Timing: W untimed warm-up steps; K tim
 each bracketed by CUDA events on the compute stream with an L2 flush (256 MB write) between
 steps outside the events; barrier + synchronize around the loop; max over ranks.
 
+The CPU baseline (`cpu_baseline`, rank 0 at N = 1) and the reference arm (`--impl reference`)
+time the reference's own PyTorch CPU path for the same config-2 step (oracle/torch_path.py:
+the reference's operators in its order and dtypes) with every host thread.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --projection-only     # config 5 alone on one GPU (for profiling its kernels)
 """
@@ -45,7 +49,6 @@ HEADS = 16
 MERGE_FACTOR = 4
 GROUP_FRAMES = 4
 METRIC = "global-attn block frames/s (mass-bias attention TFLOP/s, top-4 projection GB/s)"
-CPU_SAMPLE_FRAMES = 4  # one frame group
 
 
 def _peaks():
@@ -145,49 +148,70 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "source": "nvml" if self.rows else "nvidia-smi"}
 
 
-def _cpu_pipeline_inputs(seed: int = 0):
-    import numpy as np
-    oracle = importlib.import_module("oracle")
-    rng = np.random.default_rng(seed)
-    n = CPU_SAMPLE_FRAMES * TOKENS_PER_FRAME
-    tokens = rng.standard_normal((n, DIM)).astype(np.float32)
-    params = {
-        "qkv.weight": (rng.standard_normal((3 * DIM, DIM)) * 0.02).astype(np.float32),
-        "qkv.bias": (rng.standard_normal(3 * DIM) * 0.02).astype(np.float32),
-        "qkv.bias_mask": np.concatenate([np.ones(DIM), np.zeros(DIM), np.ones(DIM)]).astype(np.float32),
-        "q_norm.weight": np.ones(64, np.float32), "q_norm.bias": np.zeros(64, np.float32),
-        "k_norm.weight": np.ones(64, np.float32), "k_norm.bias": np.zeros(64, np.float32),
-        "proj.weight": (rng.standard_normal((DIM, DIM)) * 0.02).astype(np.float32),
-        "proj.bias": np.zeros(DIM, np.float32),
-    }
-    layout = oracle.pipeline.uniform_layout(CPU_SAMPLE_FRAMES, TOKENS_PER_FRAME, SPECIAL, MERGE_FACTOR, GROUP_FRAMES)
-    return oracle, tokens, params, layout
-
-
-def _cpu_threads() -> int:
+def _cpu_model() -> str:
     try:
-        from threadpoolctl import threadpool_info
-        info = threadpool_info()
-        return max((i.get("num_threads", 1) for i in info), default=1)
-    except Exception:
-        return os.cpu_count() or 1
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _reference_cpu_inputs(seed: int = 0):
+    """Config 2 for the reference's CPU path: the same 32 x 1029 tokens as the GPU arm (seeded
+    CPU normal draws rounded to bf16, then held in fp32 as the CPU path computes), random-init
+    block weights N(0, 0.02) with unit q/k LayerNorm scales, and the uniform keep layout."""
+    import torch
+    oracle = importlib.import_module("oracle")
+    torch_path = importlib.import_module("oracle.torch_path")
+    gen = torch.Generator(device="cpu").manual_seed(seed)
+    tokens = torch.randn(FRAMES * TOKENS_PER_FRAME, DIM, generator=gen).to(torch.bfloat16).float()
+    pg = torch.Generator(device="cpu").manual_seed(seed + 1)
+    rnd = lambda *shape: torch.randn(*shape, generator=pg) * 0.02
+    params = {
+        "qkv.weight": rnd(3 * DIM, DIM), "qkv.bias": rnd(3 * DIM),
+        "qkv.bias_mask": torch.cat([torch.ones(DIM), torch.zeros(DIM), torch.ones(DIM)]),
+        "q_norm.weight": torch.ones(64), "q_norm.bias": rnd(64),
+        "k_norm.weight": torch.ones(64), "k_norm.bias": rnd(64),
+        "proj.weight": rnd(DIM, DIM), "proj.bias": rnd(DIM),
+    }
+    layout = oracle.pipeline.uniform_layout(FRAMES, TOKENS_PER_FRAME, SPECIAL, MERGE_FACTOR, GROUP_FRAMES)
+    return torch_path, tokens, params, layout
+
+
+def _time_reference_cpu(warmup: int, steps: int):
+    """Time the reference's PyTorch CPU path (oracle/torch_path.py) on the whole config-2 block
+    with every host thread; -> (seconds per step list, threads)."""
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch_path, tokens, params, layout = _reference_cpu_inputs()
+    for _ in range(warmup):
+        torch_path.step(tokens, params, layout, heads=HEADS)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        torch_path.step(tokens, params, layout, heads=HEADS)
+        times.append(time.perf_counter() - t0)
+    return times, torch.get_num_threads()
+
+
+def _reference_sample(steps: int, warmup: int, threads: int, per_step: float) -> str:
+    return (f"the whole config-2 step ({FRAMES} frames x {TOKENS_PER_FRAME} tokens: plan + block) through the "
+            f"reference's PyTorch CPU operators (F.normalize, bf16 GEMM + topk(4), fp32 Gram + 32-step projected "
+            f"gradient, argsort/bincount/segment_reduce compaction, SDPA with the log-mass mask, Linear, "
+            f"value-dtype restore), fp32, torch {importlib.import_module('torch').__version__}, {threads} threads "
+            f"on {_cpu_model()}; {warmup} warm-up + {steps} timed, {per_step:.2f} s per step")
 
 
 def cpu_baseline(repeats: int = 2) -> dict:
-    """The oracle port of one step on a bounded sample (one 4-frame group), timed on this
-    host's cores; frames/s scaled from the sample."""
-    oracle, tokens, params, layout = _cpu_pipeline_inputs()
-    oracle.pipeline.block_step(tokens, params, layout)  # warm-up
-    times = []
-    for _ in range(repeats):
-        t0 = time.perf_counter()
-        oracle.pipeline.block_step(tokens, params, layout)
-        times.append(time.perf_counter() - t0)
+    """The reference's CPU path on the same config-2 step, timed on this host's cores: one
+    warm-up, then the median of ``repeats`` steps (a bounded sample of ~10-30 s)."""
+    times, threads = _time_reference_cpu(1, repeats)
     t = statistics.median(times)
-    return {"value": CPU_SAMPLE_FRAMES / t, "unit": "frames/s", "cores": _cpu_threads(), "kind": "port",
-            "sample": f"one {CPU_SAMPLE_FRAMES}-frame group ({CPU_SAMPLE_FRAMES * TOKENS_PER_FRAME} tokens) of the "
-                      f"same step (plan + block) in the numpy oracle, median of {repeats} after 1 warm-up, "
-                      f"{t:.2f} s per sample"}
+    return {"value": FRAMES / t, "unit": "frames/s", "cores": threads, "kind": "port",
+            "sample": _reference_sample(repeats, 1, threads, t) + " (median)"}
 
 
 def projection_stress(pkg, dev, hbm_peak: float) -> dict:
@@ -305,29 +329,33 @@ def long_sequence(pkg, attn, dev, world: int, rank: int, steps: int, flush) -> d
                     "attention FLOPs divided by the whole step time"}
 
 
+REFERENCE_MAX_STEPS = 3  # each reference step is seconds of CPU work: the run stays within a few minutes
+
+
 def run_reference(args) -> None:
+    """The reference arm: its PyTorch CPU path on the GPU arm's config, metric and unit, on
+    rank 0 only (other ranks exit without work).  Each step is the whole config-2 step; at
+    most REFERENCE_MAX_STEPS timed steps after at most one warm-up keep the run short."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    oracle, tokens, params, layout = _cpu_pipeline_inputs()
-    for _ in range(args.warmup):
-        oracle.pipeline.block_step(tokens, params, layout)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        oracle.pipeline.block_step(tokens, params, layout)
-        times.append(time.perf_counter() - t0)
+    steps = max(1, min(args.steps, REFERENCE_MAX_STEPS))
+    warmup = min(args.warmup, 1)
+    times, threads = _time_reference_cpu(warmup, steps)
     total = sum(times)
-    value = CPU_SAMPLE_FRAMES * args.steps / total
-    cores = _cpu_threads()
+    value = FRAMES * steps / total
+    sample = _reference_sample(steps, warmup, threads, total / steps)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "steps": steps, "steps_requested": args.steps, "warmup": warmup, "ms_per_step": 1e3 * total / steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config 2 sample: one 4-frame group of the single global-attention block "
-                               "(plan + compact + mass-bias attention + proj + restore), CPU oracle port"},
-        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": cores, "kind": "port",
-                         "sample": f"{CPU_SAMPLE_FRAMES} frames ({CPU_SAMPLE_FRAMES * TOKENS_PER_FRAME} tokens) per step"},
+        "config": {"workload": f"config 2: single global-attention block, {FRAMES} frames x {TOKENS_PER_FRAME} "
+                               f"tokens, dim {DIM}, {HEADS}x64 heads, merge {MERGE_FACTOR}x to "
+                               f"{FRAMES * TOKENS_PER_FRAME // MERGE_FACTOR} keys (uniform convex top-4 plan), "
+                               "reference PyTorch CPU path",
+                   "global_batch": 1, "tokens": FRAMES * TOKENS_PER_FRAME,
+                   "merged_keys": FRAMES * TOKENS_PER_FRAME // MERGE_FACTOR, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "frames/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
