@@ -80,6 +80,7 @@ _SIGNATURES = {
     "vb200_row_gather": (_c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp]),
     "vb200_peer_gather": (_c_int, [_c_vp, _c_int, _c_i64, _c_i64, _c_i64, _c_vp, _c_i64, _c_vp]),
     "vb200_peer_push": (_c_int, [_c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_int, _c_i64, _c_i64, _c_vp]),
+    "vb200_peer_barrier": (_c_int, [_c_vp, _c_int, _c_int, _c_vp, _c_i64, _c_vp]),
     "vb200_row_normalize_bf16": (
         _c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_float, _c_vp, _c_i64, _c_vp],
     ),

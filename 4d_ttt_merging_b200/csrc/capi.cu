@@ -98,7 +98,8 @@ int vb200_device_error_flags(unsigned* flags, int clear) {
   if (flags == nullptr) return vb200::set_error(VB200_EINVAL, "flags must not be NULL");
   VB200_CHECK_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
   *flags = vb200::attention_error_word(clear) | vb200::projection_error_word(clear) |
-           vb200::merge_error_word(clear) | vb200::plan_error_word(clear);
+           vb200::merge_error_word(clear) | vb200::plan_error_word(clear) |
+           vb200::peer_error_word(clear);
   VB200_CHECK_CUDA(cudaGetLastError(), "reading device error words");
   return VB200_OK;
 }

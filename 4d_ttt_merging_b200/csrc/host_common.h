@@ -27,6 +27,7 @@ unsigned attention_error_word(int clear);
 unsigned projection_error_word(int clear);
 unsigned merge_error_word(int clear);
 unsigned plan_error_word(int clear);
+unsigned peer_error_word(int clear);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

@@ -26,7 +26,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-__all__ = ["FrameShard", "frame_shard", "gather_merged", "PeerExchange", "ShardedGlobalBlock", "StepGraph"]
+__all__ = ["FrameShard", "frame_shard", "gather_merged", "agree_all", "PeerExchange", "ShardedGlobalBlock", "StepGraph"]
 
 
 @dataclass(frozen=True)
@@ -76,6 +76,14 @@ def gather_merged(tensors: list[torch.Tensor], group=None) -> list[torch.Tensor]
     return out
 
 
+def agree_all(ok: bool, group=None, device=None) -> bool:
+    """True only when ``ok`` holds on every rank of the group (one MIN all-reduce), so that
+    ranks whose local outcomes differ still take the same collective path."""
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(int(flag.item()))
+
+
 class PeerExchange:
     """The merged-K/V and log-mass all-gather of the sharded block over peer-mapped memory.
 
@@ -89,11 +97,17 @@ class PeerExchange:
     posted NVLink writes, or one multicast store per row part when opted in); `finish` reads
     every rank's log-mass with `vb200_peer_gather` and ends with a second barrier (all writes
     landed).  Unfused form: `exchange` pushes the finished rows with `vb200_peer_push` between
-    the same two barriers.  Ranks must have the same number of merged rows.  The barriers give up
-    after BARRIER_TIMEOUT_MS (a rank that never arrives ends the wait instead of spinning
-    forever)."""
+    the same two barriers.  Ranks must have the same number of merged rows.
+
+    The barriers are this library's own (`vb200_peer_barrier`): each rank stores an epoch into
+    its slot of every rank's signal pad (two pads, one per barrier, at the head of the
+    allocation) and waits for every slot of its own pad.  A wait gives up after
+    BARRIER_TIMEOUT_MS: the kernel sets device error bit 0 and returns, so a rank that never
+    arrives leaves the others with an error the host reads (`device_error_flags`) and a usable
+    CUDA context."""
 
     BARRIER_TIMEOUT_MS = 60_000
+    CHANNELS = 2  # begin / finish
 
     def __init__(self, group, rows: int, C: int, dtype: torch.dtype, device: torch.device):
         import torch.distributed._symmetric_memory as symm_mem
@@ -102,18 +116,27 @@ class PeerExchange:
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         self.es = es = torch.empty(0, dtype=dtype).element_size()
         up = lambda n: -(-n // 256) * 256
+        pad_bytes = up(self.CHANNELS * self.world * 4)
         packed_bytes, lm_bytes = up(rows * 3 * C * es), up(rows * 4)
         kv_bytes = self.world * rows * 2 * C * es
-        self.buf = symm_mem.empty(packed_bytes + lm_bytes + kv_bytes, dtype=torch.uint8, device=device)
+        self.buf = symm_mem.empty(pad_bytes + packed_bytes + lm_bytes + kv_bytes, dtype=torch.uint8, device=device)
         self.handle = symm_mem.rendezvous(self.buf, group)
-        self.packed = self.buf[:rows * 3 * C * es].view(dtype).view(rows, 3 * C)
-        self.log_mass = self.buf[packed_bytes:packed_bytes + rows * 4].view(torch.float32)
-        kv_off = packed_bytes + lm_bytes
+        self.pads = self.buf[:pad_bytes].view(torch.int32)
+        self.pads.zero_()
+        self.epoch = torch.zeros(self.CHANNELS, dtype=torch.int32, device=device)
+        p_off, lm_off = pad_bytes, pad_bytes + packed_bytes
+        self.packed = self.buf[p_off:p_off + rows * 3 * C * es].view(dtype).view(rows, 3 * C)
+        self.log_mass = self.buf[lm_off:lm_off + rows * 4].view(torch.float32)
+        kv_off = lm_off + lm_bytes
         self.kv = self.buf[kv_off:kv_off + kv_bytes].view(dtype).view(self.world * rows, 2 * C)
         ptrs = [int(p) for p in self.handle.buffer_ptrs]
         u64 = ctypes.c_uint64 * self.world
         self._kv_dst = u64(*[p + kv_off for p in ptrs])
-        self._lm_src = u64(*[p + packed_bytes for p in ptrs])
+        self._lm_src = u64(*[p + lm_off for p in ptrs])
+        self._pad = [u64(*[p + ch * self.world * 4 for p in ptrs]) for ch in range(self.CHANNELS)]
+        # every rank's pads are zero before any rank signals
+        torch.cuda.synchronize(device)
+        dist.barrier(group)
         self.log_mass_all = torch.empty(self.world * rows, dtype=torch.float32, device=device)
         self._lib, self._clib = _clib.lib(), _clib
         # multicast (NVLS) address of the K|V region when the allocation is bound to a multicast
@@ -137,10 +160,17 @@ class PeerExchange:
             return self._kv_mc, self.world, self.rank * self.rows, 2 * self.C, 1
         return self._kv_dst, self.world, self.rank * self.rows, 2 * self.C, 0
 
+    def barrier(self, channel: int):
+        """Cross-GPU barrier on the current stream (bounded; see the class docstring)."""
+        stream = self._clib.stream_of(self.epoch.device)
+        self._clib.check(self._lib.vb200_peer_barrier(self._pad[channel], self.world, self.rank,
+                                                      self.epoch[channel:].data_ptr(),
+                                                      self.BARRIER_TIMEOUT_MS * 1_000_000, stream), "peer_barrier")
+
     def begin(self):
         """Device barrier before the fused compaction writes into other ranks' buffers: every
         rank has finished reading its previous full K|V buffer and has published log_mass."""
-        self.handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        self.barrier(0)
 
     def finish(self):
         """After the fused compaction: gather every rank's log-mass, then a device barrier (all
@@ -149,7 +179,7 @@ class PeerExchange:
         rows = self.rows
         self._clib.check(self._lib.vb200_peer_gather(self._lm_src, self.world, 1, rows * 4, rows * 4,
                                                      self.log_mass_all.data_ptr(), rows * 4, stream), "peer_gather")
-        self.handle.barrier(channel=1, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        self.barrier(1)
         return self.kv, self.log_mass_all
 
     def exchange(self):
@@ -157,13 +187,13 @@ class PeerExchange:
         current stream, from this rank's compacted rows in `packed`."""
         C, es, rows = self.C, self.es, self.rows
         stream = self._clib.stream_of(self.kv.device)
-        self.handle.barrier(channel=0, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        self.barrier(0)
         self._clib.check(self._lib.vb200_peer_push(self.packed.data_ptr() + C * es, rows, 3 * C * es, 2 * C * es,
                                                    self._kv_dst, self.world, self.rank * rows, 2 * C * es, stream),
                          "peer_push")
         self._clib.check(self._lib.vb200_peer_gather(self._lm_src, self.world, 1, rows * 4, rows * 4,
                                                      self.log_mass_all.data_ptr(), rows * 4, stream), "peer_gather")
-        self.handle.barrier(channel=1, timeout_ms=self.BARRIER_TIMEOUT_MS)
+        self.barrier(1)
         return self.kv, self.log_mass_all
 
 
@@ -211,14 +241,19 @@ class ShardedGlobalBlock:
             return None
         x = self._xchg
         if x is None or x.rows != rows or x.C != C or x.packed.dtype != dtype:
+            group = self.group if self.group is not None else dist.group.WORLD
+            err = None
             try:
-                self._xchg = x = PeerExchange(self.group if self.group is not None else dist.group.WORLD,
-                                              rows, C, dtype, device)
-            except (RuntimeError, ImportError) as err:  # e.g. no CUDA virtual-memory IPC on this system
+                x = PeerExchange(group, rows, C, dtype, device)
+            except (RuntimeError, ImportError) as e:  # e.g. no CUDA virtual-memory IPC on this system
+                x, err = None, e
+            # every rank takes the same path: peer memory only where it worked on all of them
+            if not agree_all(x is not None, group, device):
                 import warnings
-                warnings.warn(f"peer-memory exchange unavailable ({err}); using NCCL all-gather")
+                warnings.warn(f"peer-memory exchange unavailable ({err or 'on another rank'}); using NCCL all-gather")
                 self._xchg_failed, self._xchg = True, None
                 return None
+            self._xchg = x
         return x
 
     def plan(self, tokens: torch.Tensor):

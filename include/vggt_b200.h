@@ -238,6 +238,16 @@ VB200_API int vb200_peer_gather(const uint64_t* src_ptrs, int world, int64_t row
 VB200_API int vb200_peer_push(const void* src, int64_t rows, int64_t src_stride_bytes, int64_t row_bytes,
                               const uint64_t* dst_ptrs, int world, int64_t dst_row0, int64_t dst_stride_bytes,
                               void* stream);
+/* Cross-GPU barrier that orders the exchange kernels above (no reference counterpart: the
+ * reference has no multi-GPU inference path).  pad_ptrs: HOST array of every rank's signal pad
+ * (world uint32 slots each, peer-mapped, zeroed on every rank before the first barrier);
+ * epoch: a uint32 in this rank's device memory, zero-initialised, advanced by every barrier
+ * (so a recorded CUDA graph replays correctly).  Each rank stores the new epoch into its slot
+ * of every pad (release, system scope) and waits until every slot of its own pad holds it
+ * (acquire).  The wait gives up after timeout_ns of global time: it then sets device error
+ * bit 0 (vb200_device_error_flags) and returns; the context stays usable. */
+VB200_API int vb200_peer_barrier(const uint64_t* pad_ptrs, int world, int rank, uint32_t* epoch,
+                                 int64_t timeout_ns, void* stream);
 
 /* ---- a9/a11: merge step ----------------------------------------------------------------------
  * Row L2 normalisation to bf16 (F.normalize(x.float(), dim=-1, eps).to(bfloat16)),

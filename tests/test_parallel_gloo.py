@@ -176,3 +176,25 @@ def test_dead_rank_ends_the_exchange_with_an_error(tmp_path):
     outcome = (tmp_path / "rank0.txt").read_text().split()
     assert outcome[0] == "error", outcome
     assert float(outcome[-1]) < 60.0
+
+
+def _agree_rank_main(rank: int, world: int, init_file: str, out_dir: str) -> None:
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        pkg = _pkg()
+        mixed = pkg.parallel.agree_all(rank != 1)  # rank 1's peer-memory setup "failed"
+        every = pkg.parallel.agree_all(True)
+        with open(os.path.join(out_dir, f"agree{rank}.txt"), "w") as fh:
+            fh.write(f"{int(mixed)} {int(every)}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ranks_agree_on_the_exchange_path(tmp_path):
+    """The peer-memory exchange is used only where it was set up on every rank: one rank's
+    failure sends all ranks to the NCCL path (no rank left waiting in a different collective)."""
+    world = 2
+    mp.spawn(_agree_rank_main, args=(world, str(tmp_path / "init"), str(tmp_path)), nprocs=world, join=True)
+    for rank in range(world):
+        assert (tmp_path / f"agree{rank}.txt").read_text() == "0 1"

@@ -78,3 +78,53 @@ def test_compact_qkv_peer_writes_every_rank(pkg, cuda_device, dim):
         assert torch.all(b[:row0] == sentinel) and torch.all(b[row0 + M:] == sentinel)
         assert torch.all(b[:, 2 * dim:] == sentinel)
     assert pkg.device_error_flags() == 0
+
+
+def _barrier(lib, pads, world, rank, epoch, timeout_ns):
+    ptrs = _u64([p.data_ptr() for p in pads])
+    rc = lib.vb200_peer_barrier(ptrs, world, rank, epoch.data_ptr(), timeout_ns,
+                                torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.vb200_last_error()
+
+
+def test_peer_barrier_single_rank_and_graph_replay(pkg, cuda_device):
+    """One rank: every barrier passes at once and advances the device-side epoch, also when
+    replayed from a recorded CUDA graph (the epoch is not baked into the launch)."""
+    lib = pkg.load_library()
+    pad = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    epoch = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    for _ in range(3):
+        _barrier(lib, [pad], 1, 0, epoch, 1_000_000_000)
+    torch.cuda.synchronize()
+    assert int(epoch) == 3 and int(pad) == 3
+    side = torch.cuda.Stream(cuda_device)
+    side.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            _barrier(lib, [pad], 1, 0, epoch, 1_000_000_000)
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(4):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert int(epoch) == 7 and int(pad) == 7
+    assert pkg.device_error_flags() == 0
+
+
+def test_peer_barrier_gives_up_with_an_error(pkg, cuda_device):
+    """Rank 0 of two, on one GPU: a local buffer stands in for rank 1's pad.  The barrier signals
+    'rank 1' and waits for a signal that nothing sends; after its 50 ms limit it sets error
+    bit 0 and returns.  The context stays usable: with the peer's signal already in place the
+    next barrier passes."""
+    lib = pkg.load_library()
+    pads = [torch.zeros(2, dtype=torch.int32, device=cuda_device) for _ in range(2)]  # rank 0's, rank 1's
+    epoch = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    _barrier(lib, pads, 2, 0, epoch, 50_000_000)
+    assert pkg.device_error_flags() & 1
+    assert int(pads[1][0]) == 1 and int(epoch) == 1  # the signal to rank 1 was sent
+    pads[0][1] = 2  # rank 1's next signal has arrived
+    _barrier(lib, pads, 2, 0, epoch, 50_000_000)
+    assert pkg.device_error_flags() == 0
+    assert int(pads[1][0]) == 2 and int(epoch) == 2
+    x = torch.arange(10, device=cuda_device)
+    assert int(x.sum()) == 45
