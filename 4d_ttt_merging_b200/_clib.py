@@ -77,6 +77,13 @@ _SIGNATURES = {
         [_c_int, _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64,
          _c_i64, _c_i64, _c_int, _c_vp],
     ),
+    "vb200_plan_hot_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_vp, _c_vp]),
+    "vb200_proj_gather_hot_capacity": (_c_int, [_c_int, _c_i64]),
+    "vb200_proj_gather_hot": (
+        _c_int,
+        [_c_int, _c_vp, _c_i64, _c_vp, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_i64,
+         _c_vp, _c_vp, _c_vp, _c_int, _c_vp],
+    ),
     "vb200_row_gather": (_c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp]),
     "vb200_peer_gather": (_c_int, [_c_vp, _c_int, _c_i64, _c_i64, _c_i64, _c_vp, _c_i64, _c_vp]),
     "vb200_peer_push": (_c_int, [_c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_int, _c_i64, _c_i64, _c_vp]),

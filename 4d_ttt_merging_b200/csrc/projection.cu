@@ -14,6 +14,7 @@
 // warp in a fixed order (keep row, then corner 0..3 partial sums, each in source order).
 #include <cub/cub.cuh>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -83,101 +84,242 @@ __global__ void row_gather_kernel(const uint8_t* __restrict__ x, long long x_row
 // ------------------------------------------------------------------------------------------
 // gather (restore): keep rows copied, source rows = sum_c w_c * y[parent_c]
 // ------------------------------------------------------------------------------------------
-template <typename T, int kMaxCorners>
-__global__ void proj_gather_kernel(const T* __restrict__ y, long long ys, const int64_t* __restrict__ keep,
-                                   long long K, const int64_t* __restrict__ src,
-                                   const int64_t* __restrict__ parent, const float* __restrict__ w,
-                                   long long S, int corners, T* __restrict__ out, long long os,
-                                   long long N_out, int C) {
-  constexpr int V = Vec<T>::N;
-  const long long r = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (r >= K + S) return;
-  const int nvec = C / V;
-  if (r < K) {
-    const int64_t dst = keep[r];
-    if (dst < 0 || dst >= N_out) {
-      if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
-      return;
-    }
-    const uint4* s = reinterpret_cast<const uint4*>(y + r * ys);
-    uint4* d = reinterpret_cast<uint4*>(out + dst * os);
-    for (int i = lane; i < nvec; i += 32) d[i] = __ldg(s + i);
-    return;
-  }
-  const long long sidx = r - K;
-  const int64_t dst = src[sidx];
+// Keep rows of the gather: out[keep[r]] = y[r], one warp per row, 16-byte vectors.
+template <typename T>
+__device__ __forceinline__ void gather_keep_row(const T* __restrict__ y, long long ys, const int64_t* __restrict__ keep,
+                                                long long r, T* __restrict__ out, long long os, long long N_out,
+                                                int nvec, int lane) {
+  const int64_t dst = keep[r];
   if (dst < 0 || dst >= N_out) {
     if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
     return;
   }
-  const T* prow[kMaxCorners];
-  float wc[kMaxCorners];
+  const uint4* s = reinterpret_cast<const uint4*>(y + r * ys);
+  uint4* d = reinterpret_cast<uint4*>(out + dst * os);
+  for (int i = lane; i < nvec; i += 32) d[i] = __ldg(s + i);
+}
+
+// Source rows [base, base + 32) of the gather, one warp.  Lane l first loads the indices of
+// source base + l (destination, parents, weights, staging slots: coalesced, one round trip for
+// 32 sources), then the warp walks the 32 sources with the indices broadcast by shuffles, so
+// each source costs one round trip for its parent rows alone.  All four parents' vectors of a
+// 32 x kGatherQ column block (a whole 1024-channel bf16 row, 8 KB per warp) are loaded before
+// any is used.  (Half rows at 64 registers, 32 warps per SM, measured slower: 1.11 vs 0.89 ms on
+// config 5.)  With
+// `hot` the parents that have a staging slot are read from that shared-memory copy.
+constexpr int kGatherQ = 4;
+
+template <typename T, bool kHot>
+__device__ __forceinline__ void gather_sources(const T* __restrict__ y, long long ys, long long K,
+                                               const int64_t* __restrict__ src, const int64_t* __restrict__ parent,
+                                               const float* __restrict__ w, long long S, int corners,
+                                               T* __restrict__ out, long long os, long long N_out, int C,
+                                               long long base, int lane, const int32_t* __restrict__ hot_slot,
+                                               const T* hot) {
+  constexpr int V = Vec<T>::N;
+  const int nvec = C / V;
+  // ---- per-lane indices of source base + lane ----
+  const long long sl = base + lane;
+  long long dst = -1;
+  int prow[4] = {0, 0, 0, 0};  // parent row of y, or ~slot when the row is staged
+  float wl[4] = {0.f, 0.f, 0.f, 0.f};
+  if (sl < S) {
+    dst = src[sl];
+    if (dst < 0 || dst >= N_out) {
+      atomicOr(&g_proj_err, kErrBadArgument);
+      dst = -1;
+    }
 #pragma unroll
-  for (int c = 0; c < kMaxCorners; ++c) {
-    if (c < corners) {
-      int64_t pc = parent[sidx * corners + c];
-      if (pc < 0 || pc >= K) {
-        if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
-        pc = 0;
+    for (int c = 0; c < 4; ++c) {
+      if (c < corners) {
+        int64_t pc = parent[sl * corners + c];
+        if (pc < 0 || pc >= K) {
+          atomicOr(&g_proj_err, kErrBadArgument);
+          pc = 0;
+        }
+        int slot = -1;
+        if constexpr (kHot) slot = hot_slot[pc];
+        prow[c] = slot >= 0 ? ~slot : static_cast<int>(pc);
+        wl[c] = round_t<T>(w[sl * corners + c]);  // weights.to(value.dtype)
       }
-      prow[c] = y + pc * ys;
-      wc[c] = round_t<T>(w[sidx * corners + c]);  // weights.to(value.dtype)
-    } else {
-      prow[c] = y;
-      wc[c] = 0.f;
     }
   }
-  T* drow = out + dst * os;
-  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    // bf16: the rounded products w_c * y come from packed bf16 multiplies (the exact product of
-    // two bf16 values fits in fp32, so one correctly rounded bf16 multiply equals rounding the
-    // fp32 product), then each pair is widened and summed in fp32 in corner order.
-    __nv_bfloat162 w2[kMaxCorners];
+  const int n = static_cast<int>(min(32ll, S - base));
+  for (int t = 0; t < n; ++t) {
+    const long long d = __shfl_sync(0xffffffffu, dst, t);
+    int pr[4];
+    float wc[4];
 #pragma unroll
-    for (int c = 0; c < kMaxCorners; ++c) w2[c] = __float2bfloat162_rn(wc[c]);
-    for (int i = lane; i < nvec; i += 32) {
-      uint4 raw[kMaxCorners];
+    for (int c = 0; c < 4; ++c) {
+      pr[c] = __shfl_sync(0xffffffffu, prow[c], t);
+      wc[c] = __shfl_sync(0xffffffffu, wl[c], t);
+    }
+    if (d < 0) continue;  // warp-uniform
+    T* drow = out + d * os;
+    for (int i0 = 0; i0 < nvec; i0 += 32 * kGatherQ) {
+      uint4 raw[4][kGatherQ];
 #pragma unroll
-      for (int c = 0; c < kMaxCorners; ++c)
-        if (c < corners) raw[c] = __ldg(reinterpret_cast<const uint4*>(prow[c] + i * V));
-      uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-      for (int c = 0; c < kMaxCorners; ++c) {
+      for (int c = 0; c < 4; ++c) {
         if (c < corners) {
-          const uint32_t* xw = reinterpret_cast<const uint32_t*>(&raw[c]);
+          const bool staged = kHot && pr[c] < 0;
+          const T* row = staged ? hot + static_cast<long long>(~pr[c]) * C : y + static_cast<long long>(pr[c]) * ys;
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const __nv_bfloat162 prod = __hmul2(w2[c], *reinterpret_cast<const __nv_bfloat162*>(&xw[h]));
-            const uint32_t pw = *reinterpret_cast<const uint32_t*>(&prod);
-            acc2[h] = fadd2(acc2[h], pk2(__uint_as_float(pw << 16), __uint_as_float(pw & 0xffff0000u)));
+          for (int q = 0; q < kGatherQ; ++q) {
+            const int i = i0 + lane + 32 * q;
+            if (i < nvec) {
+              if (staged) raw[c][q] = *reinterpret_cast<const uint4*>(row + i * V);
+              else raw[c][q] = __ldg(reinterpret_cast<const uint4*>(row + i * V));
+            }
           }
         }
       }
-      float acc[V];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) upk2(acc2[h], acc[2 * h], acc[2 * h + 1]);
-      store_vec<T>(drow + i * V, acc);
-    }
-  } else {
-  for (int i = lane; i < nvec; i += 32) {
-    float vals[kMaxCorners][V];
+      for (int q = 0; q < kGatherQ; ++q) {
+        const int i = i0 + lane + 32 * q;
+        if (i >= nvec) continue;
+        float acc[V];
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          // bf16: the rounded products w_c * y come from packed bf16 multiplies (the exact
+          // product of two bf16 values fits in fp32, so one correctly rounded bf16 multiply
+          // equals rounding the fp32 product), then each pair is widened and summed in fp32 in
+          // corner order.
+          uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-    for (int c = 0; c < kMaxCorners; ++c)
-      if (c < corners) load_vec<T>(prow[c] + i * V, vals[c]);
-    float acc[V];
+          for (int c = 0; c < 4; ++c) {
+            if (c < corners) {
+              const __nv_bfloat162 w2 = __float2bfloat162_rn(wc[c]);
+              const uint32_t* xw = reinterpret_cast<const uint32_t*>(&raw[c][q]);
 #pragma unroll
-    for (int e = 0; e < V; ++e) acc[e] = 0.f;
+              for (int h = 0; h < 4; ++h) {
+                const __nv_bfloat162 prod = __hmul2(w2, *reinterpret_cast<const __nv_bfloat162*>(&xw[h]));
+                const uint32_t pw = *reinterpret_cast<const uint32_t*>(&prod);
+                acc2[h] = fadd2(acc2[h], pk2(__uint_as_float(pw << 16), __uint_as_float(pw & 0xffff0000u)));
+              }
+            }
+          }
 #pragma unroll
-    for (int c = 0; c < kMaxCorners; ++c) {
-      if (c < corners) {
+          for (int h = 0; h < 4; ++h) upk2(acc2[h], acc[2 * h], acc[2 * h + 1]);
+        } else {
 #pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] += round_t<T>(__fmul_rn(wc[c], vals[c][e]));
+          for (int e = 0; e < V; ++e) acc[e] = 0.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (c < corners) {
+              const T* e8 = reinterpret_cast<const T*>(&raw[c][q]);
+#pragma unroll
+              for (int e = 0; e < V; ++e) acc[e] += round_t<T>(__fmul_rn(wc[c], to_f32<T>(e8[e])));
+            }
+          }
+        }
+        store_vec<T>(drow + i * V, acc);
       }
     }
-    store_vec<T>(drow + i * V, acc);
   }
+}
+
+// Plain form: warps [0, keep_warps) copy one keep row each; every further warp gathers 32
+// sources, every parent read from global memory (the merged table fits in L2, or the plan is
+// too small for the staging below to pay).
+template <typename T, int kMaxCorners>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    proj_gather_kernel(const T* __restrict__ y, long long ys, const int64_t* __restrict__ keep,
+                       long long K, const int64_t* __restrict__ src,
+                       const int64_t* __restrict__ parent, const float* __restrict__ w,
+                       long long S, int corners, T* __restrict__ out, long long os,
+                       long long N_out, int C) {
+  static_assert(kMaxCorners == 4, "four corners at most");
+  const long long wid = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid < K) {
+    gather_keep_row<T>(y, ys, keep, wid, out, os, N_out, C / Vec<T>::N, lane);
+    return;
   }
+  const long long base = (wid - K) * 32;
+  if (base >= S) return;
+  gather_sources<T, false>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, lane, nullptr, nullptr);
+}
+
+// Skewed plans: the most-referenced merged rows (hot_rows, chosen once per plan by
+// vb200_plan_hot_rows) are staged once per CTA in shared memory and every reference to them is
+// served from there, which takes their share of the 4 x 2 KB parent reads per token off the L2
+// (the bound of the plain kernel on config 5: ~8 GB of L2 reads per restore).  One CTA of
+// kHotWarps warps per SM walks the keep rows, then the 32-source batches, in grid stride.
+constexpr int kHotWarps = 16;
+constexpr int kMaxHotRows = 128;
+constexpr long long kHotSmemBytes = 200 * 1024;  // shared memory for staged rows per CTA
+
+template <typename T, int kMaxCorners>
+__global__ void __launch_bounds__(kHotWarps * 32, 1)
+    proj_gather_hot_kernel(const T* __restrict__ y, long long ys, const int64_t* __restrict__ keep, long long K,
+                           const int64_t* __restrict__ src, const int64_t* __restrict__ parent,
+                           const float* __restrict__ w, long long S, int corners, T* __restrict__ out, long long os,
+                           long long N_out, int C, const int32_t* __restrict__ hot_rows,
+                           const int32_t* __restrict__ hot_slot, const int32_t* __restrict__ n_hot_p,
+                           int max_hot) {
+  static_assert(kMaxCorners == 4, "four corners at most");
+  extern __shared__ __align__(16) uint8_t hot_smem[];
+  T* hot = reinterpret_cast<T*>(hot_smem);
+  const int n_hot = min(*n_hot_p, max_hot);
+  const int vecs = C * static_cast<int>(sizeof(T)) / 16;
+  for (int i = threadIdx.x; i < n_hot * vecs; i += blockDim.x) {
+    const int r = i / vecs, v = i - r * vecs;
+    const int row = hot_rows[r];
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (row >= 0 && row < K) val = __ldg(reinterpret_cast<const uint4*>(y + row * ys) + v);
+    reinterpret_cast<uint4*>(hot + static_cast<long long>(r) * C)[v] = val;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long long warp0 = static_cast<long long>(blockIdx.x) * kHotWarps + (threadIdx.x >> 5);
+  const long long nwarps = static_cast<long long>(gridDim.x) * kHotWarps;
+  for (long long r = warp0; r < K; r += nwarps) gather_keep_row<T>(y, ys, keep, r, out, os, N_out, C / Vec<T>::N, lane);
+  for (long long base = warp0 * 32; base < S; base += nwarps * 32)
+    gather_sources<T, true>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, lane, hot_slot, hot);
+}
+
+// Hot-row selection (one block): row j's reference count is its CSR length; counts are bucketed
+// by (log2, 3 mantissa bits), whole buckets are taken from the top while the total stays within
+// max_hot, and every row of a taken bucket gets a slot.  Which row lands in which slot does not
+// change any result (staged rows are exact copies).
+constexpr int kHotBuckets = 256;
+
+__device__ __forceinline__ int hot_bucket(int len) {
+  if (len <= 1) return 0;  // a row referenced once gains nothing from staging
+  const int lg = 31 - __clz(len);
+  const int mant = lg >= 3 ? (len >> (lg - 3)) & 7 : (len << (3 - lg)) & 7;
+  return min(kHotBuckets - 1, 1 + lg * 8 + mant);
+}
+
+__global__ void __launch_bounds__(1024)
+    plan_hot_rows_kernel(const int32_t* __restrict__ seg_offsets, long long M, int corners, int max_hot,
+                         int32_t* __restrict__ hot_rows, int32_t* __restrict__ hot_slot, int32_t* __restrict__ n_hot) {
+  __shared__ int hist[kHotBuckets];
+  __shared__ int cut, count;
+  for (int b = threadIdx.x; b < kHotBuckets; b += blockDim.x) hist[b] = 0;
+  if (threadIdx.x == 0) count = 0;
+  __syncthreads();
+  for (long long j = threadIdx.x; j < M; j += blockDim.x)
+    atomicAdd(&hist[hot_bucket(seg_offsets[(j + 1) * corners] - seg_offsets[j * corners])], 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int total = 0, b = kHotBuckets - 1;
+    for (; b > 0; --b) {
+      if (total + hist[b] > max_hot) break;
+      total += hist[b];
+    }
+    cut = b + 1;  // buckets >= cut are staged (bucket 0 never is)
+  }
+  __syncthreads();
+  for (long long j = threadIdx.x; j < M; j += blockDim.x) {
+    int slot = -1;
+    if (hot_bucket(seg_offsets[(j + 1) * corners] - seg_offsets[j * corners]) >= cut) {
+      slot = atomicAdd(&count, 1);
+      hot_rows[slot] = static_cast<int32_t>(j);
+    }
+    hot_slot[j] = slot;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *n_hot = count;
 }
 
 template <typename T>
@@ -191,18 +333,29 @@ __global__ void zero_rows_kernel(T* out, long long os, long long N, int C) {
 }
 
 // ------------------------------------------------------------------------------------------
-// scatter, long rows: a merged row with more than kScatterChunk CSR entries (skewed plans: a
-// Zipf-popular parent can own a tenth of all entries) is reduced as a fixed two-level tree.
-// Level 0: one warp per chunk of kScatterChunk consecutive entries writes the chunk's fp32 sum
-// of w * x (sequential within the chunk).  Level 1: a row with more than kScatterGroup chunks
-// gets one warp per group of kScatterGroup consecutive chunk sums.  proj_scatter_kernel then adds
-// the keep row and the row's level-1 sums (or, for shorter rows, its level-0 sums) in order.
-// The result is deterministic and no warp walks more than ~kScatterChunk rows or ~kScatterGroup
-// partial sums (up to rows of kScatterChunk * kScatterGroup^2 entries).
+// scatter (compact): out[j] = (keep_j + sum_c part_c) / normalizer_j, part_c = the fp32 sum of
+// w * x over the sources whose corner-c parent is j, in source order (the CSR order).
+//
+// The kernels read whole source rows: lane l of a warp owns 16-byte vectors l, l + 32, l + 64,
+// l + 96 of a 32 x 4-vector column block (one 1024-channel bf16 row), so each CSR entry is one
+// 2 KB row read, and kScatterInFlight entries are loaded before any is summed (8 KB in flight
+// per warp).  Memory-level parallelism, not bandwidth, bounded the earlier one-vector-per-pass
+// form (ncu: long-scoreboard stalls, 20-30% of warps active).
+//
+// Skewed plans: a merged row with more than kScatterChunk CSR entries (a Zipf-popular parent can
+// own a tenth of all entries) is reduced as a fixed two-level tree.  Level 0: one warp per chunk
+// of kScatterChunk consecutive entries writes the chunk's fp32 sum (sequential within the
+// chunk).  Level 1: a row with more than kScatterGroup chunks gets one warp per group of
+// kScatterGroup consecutive chunk sums.  scatter_finish_kernel then adds the keep row and the
+// row's level-1 sums (or level-0 sums) in order.  Level 0 and the short rows run in ONE launch
+// (scatter_work_kernel), so the GPU stays full while the long rows' chunks are summed.  The
+// result is deterministic (fixed order) and no warp walks more than kScatterChunk rows or
+// kScatterGroup partial sums (up to rows of kScatterChunk * kScatterGroup^2 entries).
 // ------------------------------------------------------------------------------------------
-constexpr int kScatterChunk = 256;   // entries per level-0 chunk
+constexpr int kScatterChunk = 128;   // entries per level-0 chunk (and the long-row threshold)
 constexpr int kScatterGroup = 64;    // level-0 partials per level-1 sum
-constexpr int kScatterInFlight = 4;
+constexpr int kScatterInFlight = 4;  // entries loaded before any is summed
+constexpr int kScatterQ = 4;         // 16-byte vectors per lane per column block
 
 __global__ void scatter_count_kernel(const int32_t* __restrict__ seg_offsets, long long M, int corners,
                                      int32_t* __restrict__ nchunk, int32_t* __restrict__ ngroup) {
@@ -274,75 +427,128 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   }
 }
 
+// One 16-byte vector of T as fp32 pairs (V / 2 pairs).
 template <typename T>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
-    scatter_chunk_kernel(const T* __restrict__ x, long long x_rows, long long xs,
-                         const int32_t* __restrict__ seg_offsets, long long M, int corners,
-                         const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
-                         const int32_t* __restrict__ chunk_base, float* __restrict__ partials, int C) {
-  constexpr int V = Vec<T>::N;
-  const long long c = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (c >= chunk_base[M]) return;
-  long long lo = 0, hi = M;  // the row j with chunk_base[j] <= c < chunk_base[j + 1]
-  while (hi - lo > 1) {
-    const long long mid = (lo + hi) / 2;
-    if (chunk_base[mid] <= c) lo = mid;
-    else hi = mid;
-  }
-  const long long j = lo;
-  const int r0 = seg_offsets[j * corners], r1 = seg_offsets[(j + 1) * corners];
-  const int e0 = r0 + static_cast<int>(c - chunk_base[j]) * kScatterChunk;
-  const int e1 = e0 + kScatterChunk < r1 ? e0 + kScatterChunk : r1;
-  float* pr = partials + c * C;
-  for (int col = lane * V; col < C; col += 32 * V) {
-    float part[V];
+__device__ __forceinline__ void widen_pairs(const uint4& raw, uint64_t (&p)[Vec<T>::N / 2]) {
+  const uint32_t* wv = reinterpret_cast<const uint32_t*>(&raw);
+  if constexpr (sizeof(T) == 4) {
+    p[0] = pk2(__uint_as_float(wv[0]), __uint_as_float(wv[1]));
+    p[1] = pk2(__uint_as_float(wv[2]), __uint_as_float(wv[3]));
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
 #pragma unroll
-    for (int q = 0; q < V; ++q) part[q] = 0.f;
-    // kScatterInFlight source rows in flight per lane: all loads first, then the FMAs in entry
-    // order (the sum stays sequential within the chunk)
-    for (int eb = e0; eb < e1; eb += kScatterInFlight) {
-      float v[kScatterInFlight][V];
-      float w[kScatterInFlight];
+    for (int h = 0; h < 4; ++h) p[h] = pk2(__uint_as_float(wv[h] << 16), __uint_as_float(wv[h] & 0xffff0000u));
+  } else {
 #pragma unroll
-      for (int u = 0; u < kScatterInFlight; ++u) {
-        int su = 0;
-        w[u] = 0.f;
-        if (eb + u < e1) {
-          su = __ldg(entry_src + eb + u);
-          w[u] = __ldg(entry_w + eb + u);
-          if (su < 0 || su >= x_rows) { su = 0; w[u] = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-        }
-        load_vec<T>(x + static_cast<long long>(su) * xs + col, v[u]);
-      }
-#pragma unroll
-      for (int u = 0; u < kScatterInFlight; ++u) {
-        if (eb + u < e1) {
-#pragma unroll
-          for (int q = 0; q < V; ++q) part[q] = __fadd_rn(part[q], __fmul_rn(w[u], v[u][q]));
-        }
-      }
+    for (int h = 0; h < 4; ++h) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[h]));
+      p[h] = pk2(f.x, f.y);
     }
-#pragma unroll
-    for (int q = 0; q < V; ++q) pr[col + q] = part[q];
   }
 }
 
-// ------------------------------------------------------------------------------------------
-// scatter (compact): out[j] = (keep_j + sum_c part_c) / normalizer_j
-// ------------------------------------------------------------------------------------------
+// part[q] (V/2 fp32 pairs per owned vector q) += w_e * x[src_e] for CSR entries [e0, e1), in
+// entry order; each product rounded to fp32 before the add (the reference multiplies, then
+// sums).  The lane's vectors of the column block starting at col0: (lane + 32 q) * V.
 template <typename T>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32, 4)
-    proj_scatter_kernel(const T* __restrict__ x, long long x_rows, long long xs, const int64_t* __restrict__ keep,
+__device__ __forceinline__ void scatter_entries(const T* __restrict__ x, long long x_rows, long long xs,
+                                                const int32_t* __restrict__ entry_src,
+                                                const float* __restrict__ entry_w, int e0, int e1, int col0,
+                                                int C, int lane, uint64_t (&part)[kScatterQ][Vec<T>::N / 2]) {
+  constexpr int V = Vec<T>::N;
+  for (int eb = e0; eb < e1; eb += kScatterInFlight) {
+    uint4 raw[kScatterInFlight][kScatterQ];
+    float w[kScatterInFlight];
+#pragma unroll
+    for (int u = 0; u < kScatterInFlight; ++u) {
+      int su = 0;
+      w[u] = 0.f;
+      if (eb + u < e1) {
+        su = __ldg(entry_src + eb + u);
+        w[u] = __ldg(entry_w + eb + u);
+        if (su < 0 || su >= x_rows) {
+          su = 0;
+          w[u] = 0.f;
+          if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+        }
+      }
+      const T* row = x + static_cast<long long>(su) * xs;
+#pragma unroll
+      for (int q = 0; q < kScatterQ; ++q) {
+        const int col = col0 + (lane + 32 * q) * V;
+        if (eb + u < e1 && col < C) raw[u][q] = __ldg(reinterpret_cast<const uint4*>(row + col));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kScatterInFlight; ++u) {
+      if (eb + u < e1) {
+        const uint64_t w2 = pk2(w[u], w[u]);
+#pragma unroll
+        for (int q = 0; q < kScatterQ; ++q) {
+          if (col0 + (lane + 32 * q) * V < C) {
+            uint64_t xv[V / 2];
+            widen_pairs<T>(raw[u][q], xv);
+#pragma unroll
+            for (int h = 0; h < V / 2; ++h) part[q][h] = fadd2(part[q][h], fmul2(w2, xv[h]));
+          }
+        }
+      }
+    }
+  }
+}
+
+// Level 0 and short rows in one launch: warps [0, chunk_warps) sum the level-0 chunks of long
+// rows (warps past the real chunk count exit); warp chunk_warps + j reduces short row j
+// completely (keep row + corner partial sums in corner order, divided by the normaliser).
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
+    scatter_work_kernel(const T* __restrict__ x, long long x_rows, long long xs, const int64_t* __restrict__ keep,
                         long long M, int corners, const int32_t* __restrict__ seg_offsets,
                         const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
-                        const float* __restrict__ normalizer, T* __restrict__ out, long long os,
-                        int C, const int32_t* __restrict__ chunk_base, const float* __restrict__ partials,
-                        const int32_t* __restrict__ group_base, const float* __restrict__ partials1) {
+                        const float* __restrict__ normalizer, T* __restrict__ out, long long os, int C,
+                        const int32_t* __restrict__ chunk_base, float* __restrict__ partials,
+                        long long chunk_warps) {
   constexpr int V = Vec<T>::N;
-  const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const long long w = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  if (w < chunk_warps) {
+    const long long c = w;
+    if (c >= chunk_base[M]) return;
+    long long lo = 0, hi = M;  // the row j with chunk_base[j] <= c < chunk_base[j + 1]
+    while (hi - lo > 1) {
+      const long long mid = (lo + hi) / 2;
+      if (chunk_base[mid] <= c) lo = mid;
+      else hi = mid;
+    }
+    const long long j = lo;
+    const int r0 = seg_offsets[j * corners], r1 = seg_offsets[(j + 1) * corners];
+    const int e0 = r0 + static_cast<int>(c - chunk_base[j]) * kScatterChunk;
+    const int e1 = e0 + kScatterChunk < r1 ? e0 + kScatterChunk : r1;
+    float* pr = partials + c * C;
+    for (int col0 = 0; col0 < C; col0 += 32 * kScatterQ * V) {
+      uint64_t part[kScatterQ][V / 2];
+#pragma unroll
+      for (int q = 0; q < kScatterQ; ++q)
+#pragma unroll
+        for (int h = 0; h < V / 2; ++h) part[q][h] = 0ull;
+      scatter_entries<T>(x, x_rows, xs, entry_src, entry_w, e0, e1, col0, C, lane, part);
+#pragma unroll
+      for (int q = 0; q < kScatterQ; ++q) {
+        const int col = col0 + (lane + 32 * q) * V;
+        if (col < C) {
+#pragma unroll
+          for (int h = 0; h < V / 2; ++h) {
+            float a, b;
+            upk2(part[q][h], a, b);
+            *reinterpret_cast<float2*>(pr + col + 2 * h) = make_float2(a, b);
+          }
+        }
+      }
+    }
+    return;
+  }
+  const long long j = w - chunk_warps;
   if (j >= M) return;
+  if (chunk_base != nullptr && chunk_base[j + 1] > chunk_base[j]) return;  // long row: finished later
   const float norm = normalizer[j];
   const T* krow = nullptr;
   if (keep != nullptr) {
@@ -353,79 +559,97 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 4)
       atomicOr(&g_proj_err, kErrBadArgument);
     }
   }
-  T* drow = out + j * os;
   const int32_t* seg = seg_offsets + j * corners;
-  if (chunk_base != nullptr && chunk_base[j + 1] > chunk_base[j]) {
-    // long row: keep row + its level-1 sums (or its level-0 chunk sums), in order
-    const bool grouped = group_base[j + 1] > group_base[j];
-    const float* src = grouped ? partials1 : partials;
-    const int k0 = grouped ? group_base[j] : chunk_base[j];
-    const int k1 = grouped ? group_base[j + 1] : chunk_base[j + 1];
-    for (int col = lane * V; col < C; col += 32 * V) {
-      float kv[V];
-      if (krow != nullptr) {
-        load_vec<T>(krow + col, kv);
+  T* drow = out + j * os;
+  // the row's accumulator lives in shared memory (each lane its own words), so the registers
+  // hold only the in-flight source rows and the current corner's partial sums
+  __shared__ uint64_t acc_s[kWarpsPerBlock][kScatterQ][V / 2][32];
+  uint64_t (&acc)[kScatterQ][V / 2][32] = acc_s[threadIdx.x >> 5];
+  for (int col0 = 0; col0 < C; col0 += 32 * kScatterQ * V) {
+#pragma unroll
+    for (int q = 0; q < kScatterQ; ++q) {
+      const int col = col0 + (lane + 32 * q) * V;
+      uint64_t k2[V / 2];
+      if (krow != nullptr && col < C) {
+        widen_pairs<T>(__ldg(reinterpret_cast<const uint4*>(krow + col)), k2);
       } else {
 #pragma unroll
-        for (int e = 0; e < V; ++e) kv[e] = 0.f;
+        for (int h = 0; h < V / 2; ++h) k2[h] = 0ull;
       }
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < V; ++e) acc[e] = kv[e];
-      sum_partials<2>(src, k0, k1, C, col, acc, V);
-      float out_v[V];
-#pragma unroll
-      for (int e = 0; e < V; ++e) out_v[e] = __fdiv_rn(acc[e], norm);
-      store_vec<T>(drow + col, out_v);
-    }
-    return;
-  }
-
-  // short row: one 16-byte vector of channels per lane per pass, kScatterInFlight source rows
-  // in flight; per corner an fp32 partial sum in entry order, added to the keep row in corner
-  // order, then divided by the normaliser
-  for (int col = lane * V; col < C; col += 32 * V) {
-    float acc[V];
-    if (krow != nullptr) {
-      load_vec<T>(krow + col, acc);
-    } else {
-#pragma unroll
-      for (int q = 0; q < V; ++q) acc[q] = 0.f;
+      for (int h = 0; h < V / 2; ++h) acc[q][h][lane] = k2[h];
     }
     for (int c = 0; c < corners; ++c) {
       const int e0 = seg[c], e1 = seg[c + 1];
       if (e0 == e1) continue;
-      float part[V];
+      uint64_t part[kScatterQ][V / 2];
 #pragma unroll
-      for (int q = 0; q < V; ++q) part[q] = 0.f;
-      for (int eb = e0; eb < e1; eb += kScatterInFlight) {
-        float v[kScatterInFlight][V];
-        float w[kScatterInFlight];
+      for (int q = 0; q < kScatterQ; ++q)
 #pragma unroll
-        for (int u = 0; u < kScatterInFlight; ++u) {
-          int su = 0;
-          w[u] = 0.f;
-          if (eb + u < e1) {
-            su = __ldg(entry_src + eb + u);
-            w[u] = __ldg(entry_w + eb + u);
-            if (su < 0 || su >= x_rows) { su = 0; w[u] = 0.f; if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument); }
-          }
-          load_vec<T>(x + static_cast<long long>(su) * xs + col, v[u]);
-        }
+        for (int h = 0; h < V / 2; ++h) part[q][h] = 0ull;
+      scatter_entries<T>(x, x_rows, xs, entry_src, entry_w, e0, e1, col0, C, lane, part);
 #pragma unroll
-        for (int u = 0; u < kScatterInFlight; ++u) {
-          if (eb + u < e1) {
+      for (int q = 0; q < kScatterQ; ++q)
 #pragma unroll
-            for (int q = 0; q < V; ++q) part[q] = __fadd_rn(part[q], __fmul_rn(w[u], v[u][q]));
-          }
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < V; ++q) acc[q] = __fadd_rn(acc[q], part[q]);
+        for (int h = 0; h < V / 2; ++h) acc[q][h][lane] = fadd2(acc[q][h][lane], part[q][h]);
     }
+#pragma unroll
+    for (int q = 0; q < kScatterQ; ++q) {
+      const int col = col0 + (lane + 32 * q) * V;
+      if (col < C) {
+        float o[V];
+#pragma unroll
+        for (int h = 0; h < V / 2; ++h) {
+          float a, b;
+          upk2(acc[q][h][lane], a, b);
+          o[2 * h] = __fdiv_rn(a, norm);
+          o[2 * h + 1] = __fdiv_rn(b, norm);
+        }
+        store_vec<T>(drow + col, o);
+      }
+    }
+  }
+}
+
+// Long rows: keep row + the row's level-1 sums (or its level-0 chunk sums), in order, divided by
+// the normaliser.  One warp per merged row; short rows exit.
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    scatter_finish_kernel(const T* __restrict__ x, long long x_rows, long long xs, const int64_t* __restrict__ keep,
+                          long long M, const float* __restrict__ normalizer, T* __restrict__ out, long long os,
+                          int C, const int32_t* __restrict__ chunk_base, const float* __restrict__ partials,
+                          const int32_t* __restrict__ group_base, const float* __restrict__ partials1) {
+  constexpr int V = Vec<T>::N;
+  const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= M || chunk_base[j + 1] == chunk_base[j]) return;
+  const float norm = normalizer[j];
+  const T* krow = nullptr;
+  if (keep != nullptr) {
+    const int64_t kr = keep[j];
+    if (kr >= 0 && kr < x_rows) {
+      krow = x + kr * xs;
+    } else if (lane == 0) {
+      atomicOr(&g_proj_err, kErrBadArgument);
+    }
+  }
+  const bool grouped = group_base[j + 1] > group_base[j];
+  const float* src = grouped ? partials1 : partials;
+  const int k0 = grouped ? group_base[j] : chunk_base[j];
+  const int k1 = grouped ? group_base[j + 1] : chunk_base[j + 1];
+  T* drow = out + j * os;
+  for (int col = lane * V; col < C; col += 32 * V) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (krow != nullptr) {
+      float kv[V];
+      load_vec<T>(krow + col, kv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) acc[e] = kv[e];
+    }
+    sum_partials<4>(src, k0, k1, C, col, acc, V);
     float o[V];
 #pragma unroll
-    for (int q = 0; q < V; ++q) o[q] = __fdiv_rn(acc[q], norm);
+    for (int e = 0; e < V; ++e) o[e] = __fdiv_rn(acc[e], norm);
     store_vec<T>(drow + col, o);
   }
 }
@@ -1161,7 +1385,7 @@ extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int
   }
   if (K + S == 0) return VB200_OK;
 #define VB200_GATHER(T)                                                                      \
-  proj_gather_kernel<T, 4><<<row_blocks(K + S), kWarpsPerBlock * 32, 0, st>>>(               \
+  proj_gather_kernel<T, 4><<<row_blocks(K + (S + 31) / 32), kWarpsPerBlock * 32, 0, st>>>(  \
       static_cast<const T*>(y), ys, keep, K, src, parent, w, S, static_cast<int>(corners), \
       static_cast<T*>(out), os, N_out, static_cast<int>(C))
   if (dtype == VB200_F32) VB200_GATHER(float);
@@ -1169,6 +1393,68 @@ extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int
   else VB200_GATHER(__half);
 #undef VB200_GATHER
   VB200_CHECK_LAUNCH("proj_gather_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_plan_hot_rows(const int32_t* seg_offsets, int64_t M, int64_t corners, int max_hot,
+                                   int32_t* hot_rows, int32_t* hot_slot, int32_t* n_hot, void* stream) {
+  VB200_REQUIRE(M >= 0 && corners >= 1 && max_hot >= 0, "plan_hot_rows: bad sizes");
+  VB200_REQUIRE(seg_offsets && hot_slot && n_hot && (max_hot == 0 || hot_rows), "plan_hot_rows: null pointer");
+  plan_hot_rows_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(seg_offsets, M, static_cast<int>(corners),
+                                                                          max_hot, hot_rows, hot_slot, n_hot);
+  VB200_CHECK_LAUNCH("plan_hot_rows_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_proj_gather_hot_capacity(int dtype, int64_t C) {
+  const int es = elem_size(dtype);
+  if (C <= 0) return 0;
+  const long long row = C * es;
+  return static_cast<int>(std::min<long long>(kMaxHotRows, kHotSmemBytes / row));
+}
+
+extern "C" int vb200_proj_gather_hot(int dtype, const void* y, int64_t ys, const int64_t* keep, int64_t K,
+                                     const int64_t* src, const int64_t* parent, const float* w, int64_t S,
+                                     int64_t corners, void* out, int64_t os, int64_t N_out, int64_t C,
+                                     const int32_t* hot_rows, const int32_t* hot_slot, const int32_t* n_hot,
+                                     int max_hot, void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "proj_gather_hot: bad dtype %d",
+                dtype);
+  VB200_REQUIRE(K >= 0 && S >= 0 && N_out >= 0 && C >= 0, "proj_gather_hot: negative size");
+  VB200_REQUIRE(corners >= 1 && corners <= 4, "proj_gather_hot: corners must be in [1, 4] (got %lld)",
+                (long long)corners);
+  if (C == 0 || N_out == 0 || K + S == 0) return VB200_OK;
+  VB200_REQUIRE(out != nullptr && (K == 0 || (y && keep)) && (S == 0 || (src && parent && w)),
+                "proj_gather_hot: null pointer");
+  VB200_REQUIRE(hot_slot && n_hot && hot_rows, "proj_gather_hot: null hot-row table");
+  VB200_REQUIRE(S == 0 || K > 0, "proj_gather_hot: sources need at least one compact row to read");
+  const int cap = vb200_proj_gather_hot_capacity(dtype, C);
+  VB200_REQUIRE(max_hot >= 0 && max_hot <= cap, "proj_gather_hot: max_hot %d exceeds the shared-memory capacity %d",
+                max_hot, cap);
+  int rc;
+  if (K > 0 && (rc = check_rows(dtype, y, ys, C, "proj_gather_hot input")) != VB200_OK) return rc;
+  if ((rc = check_rows(dtype, out, os, C, "proj_gather_hot output")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = static_cast<size_t>(max_hot) * static_cast<size_t>(C) * elem_size(dtype);
+  int dev = 0, sms = 0;
+  VB200_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  VB200_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+  const long long rows = K + S;
+  const unsigned grid = static_cast<unsigned>(std::max<long long>(1, std::min<long long>(sms, (rows + kHotWarps - 1) / kHotWarps)));
+#define VB200_GATHER_HOT(T)                                                                                \
+  do {                                                                                                     \
+    VB200_CHECK_CUDA(cudaFuncSetAttribute(proj_gather_hot_kernel<T, 4>,                                    \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)), \
+                     "cudaFuncSetAttribute");                                                              \
+    proj_gather_hot_kernel<T, 4><<<grid, kHotWarps * 32, smem, st>>>(                                      \
+        static_cast<const T*>(y), ys, keep, K, src, parent, w, S, static_cast<int>(corners),               \
+        static_cast<T*>(out), os, N_out, static_cast<int>(C), hot_rows, hot_slot, n_hot, max_hot);         \
+  } while (0)
+  if (dtype == VB200_F32) VB200_GATHER_HOT(float);
+  else if (dtype == VB200_BF16) VB200_GATHER_HOT(__nv_bfloat16);
+  else VB200_GATHER_HOT(__half);
+#undef VB200_GATHER_HOT
+  VB200_CHECK_LAUNCH("proj_gather_hot_kernel");
   return VB200_OK;
 }
 
@@ -1242,36 +1528,36 @@ extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int6
   VB200_CHECK_CUDA(cub::DeviceScan::ExclusiveSum(ws + lay.scan_tmp, scan_bytes, ngroup, group_base,
                                                  static_cast<int>(M + 1), st),
                    "cub::DeviceScan::ExclusiveSum");
-  if (n_entries > kScatterChunk) {
-#define VB200_CHUNKS(T)                                                                              \
-  scatter_chunk_kernel<T><<<row_blocks(lay.bound), kWarpsPerBlock * 32, 0, st>>>(                     \
-      static_cast<const T*>(x), x_rows, xs, seg_offsets, M, static_cast<int>(corners), entry_src, entry_w, \
-      chunk_base, partials, static_cast<int>(C))
-    if (dtype == VB200_F32) VB200_CHUNKS(float);
-    else if (dtype == VB200_BF16) VB200_CHUNKS(__nv_bfloat16);
-    else VB200_CHUNKS(__half);
-#undef VB200_CHUNKS
-    VB200_CHECK_LAUNCH("scatter_chunk_kernel");
-    const int V = dtype == VB200_F32 ? 4 : 8;
-    if (V == 8) {
-      scatter_group_kernel<8><<<row_blocks(lay.bound1), kWarpsPerBlock * 32, 0, st>>>(
-          M, chunk_base, group_base, partials, partials1, static_cast<int>(C));
-    } else {
-      scatter_group_kernel<4><<<row_blocks(lay.bound1), kWarpsPerBlock * 32, 0, st>>>(
-          M, chunk_base, group_base, partials, partials1, static_cast<int>(C));
-    }
-    VB200_CHECK_LAUNCH("scatter_group_kernel");
+  const bool tree = n_entries > kScatterChunk;  // some row may be long
+  const long long chunk_warps = tree ? lay.bound : 0;
+#define VB200_WORK(T)                                                                                    \
+  scatter_work_kernel<T><<<row_blocks(chunk_warps + M), kWarpsPerBlock * 32, 0, st>>>(                    \
+      static_cast<const T*>(x), x_rows, xs, keep, M, static_cast<int>(corners), seg_offsets, entry_src, entry_w, \
+      normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials, chunk_warps)
+  if (dtype == VB200_F32) VB200_WORK(float);
+  else if (dtype == VB200_BF16) VB200_WORK(__nv_bfloat16);
+  else VB200_WORK(__half);
+#undef VB200_WORK
+  VB200_CHECK_LAUNCH("scatter_work_kernel");
+  if (!tree) return VB200_OK;
+  const int V = dtype == VB200_F32 ? 4 : 8;
+  if (V == 8) {
+    scatter_group_kernel<8><<<row_blocks(lay.bound1), kWarpsPerBlock * 32, 0, st>>>(
+        M, chunk_base, group_base, partials, partials1, static_cast<int>(C));
+  } else {
+    scatter_group_kernel<4><<<row_blocks(lay.bound1), kWarpsPerBlock * 32, 0, st>>>(
+        M, chunk_base, group_base, partials, partials1, static_cast<int>(C));
   }
-#define VB200_SCATTER(T)                                                                      \
-  proj_scatter_kernel<T><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                      \
-      static_cast<const T*>(x), x_rows, xs, keep, M, static_cast<int>(corners), seg_offsets, entry_src, \
-      entry_w, normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials, group_base, \
-      partials1)
-  if (dtype == VB200_F32) VB200_SCATTER(float);
-  else if (dtype == VB200_BF16) VB200_SCATTER(__nv_bfloat16);
-  else VB200_SCATTER(__half);
-#undef VB200_SCATTER
-  VB200_CHECK_LAUNCH("proj_scatter_kernel");
+  VB200_CHECK_LAUNCH("scatter_group_kernel");
+#define VB200_FINISH(T)                                                                            \
+  scatter_finish_kernel<T><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                          \
+      static_cast<const T*>(x), x_rows, xs, keep, M, normalizer, static_cast<T*>(out), os, static_cast<int>(C), \
+      chunk_base, partials, group_base, partials1)
+  if (dtype == VB200_F32) VB200_FINISH(float);
+  else if (dtype == VB200_BF16) VB200_FINISH(__nv_bfloat16);
+  else VB200_FINISH(__half);
+#undef VB200_FINISH
+  VB200_CHECK_LAUNCH("scatter_finish_kernel");
   return VB200_OK;
 }
 

@@ -256,6 +256,20 @@ def build_plan_csr(parent: torch.Tensor, weights: torch.Tensor, kept: int,
     return PlanCSR(seg, esrc[: S * corners], ew[: S * corners], mass[:kept], log_mass[:kept], corners, kept)
 
 
+def plan_hot_rows(csr: PlanCSR, max_hot: int):
+    """The plan's most-referenced merged rows (at most ``max_hot``), chosen on the device from
+    the CSR lengths (``vb200_plan_hot_rows``): -> (hot_rows int32 [max_hot], hot_slot int32 [M],
+    n_hot int32 [1], max_hot), the staging table of ``vb200_proj_gather_hot``."""
+    dev = csr.seg_offsets.device
+    hot_rows = torch.empty(max(max_hot, 1), device=dev, dtype=torch.int32)
+    hot_slot = torch.empty(max(csr.kept, 1), device=dev, dtype=torch.int32)
+    n_hot = torch.empty(1, device=dev, dtype=torch.int32)
+    rc = C.lib().vb200_plan_hot_rows(csr.seg_offsets.data_ptr(), csr.kept, csr.corners, int(max_hot),
+                                     hot_rows.data_ptr(), hot_slot.data_ptr(), n_hot.data_ptr(), C.stream_of(dev))
+    C.check(rc, "plan_hot_rows")
+    return hot_rows, hot_slot, n_hot, int(max_hot)
+
+
 def deterministic_weighted_normalizer(parent_compact: torch.Tensor, weights: torch.Tensor,
                                       kept_tokens: int) -> torch.Tensor:
     """Return physical-plus-source mass [1, K, 1] without atomic additions."""

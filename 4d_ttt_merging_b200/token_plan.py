@@ -52,17 +52,35 @@ def _scatter(x2d: torch.Tensor, keep: torch.Tensor | None, csr: PlanCSR, normali
     return out
 
 
+# Restores with at least this many (source, corner) references stage the plan's most-referenced
+# merged rows in shared memory (vb200_proj_gather_hot); smaller ones read every parent from
+# global memory, where the merged table fits in L2 anyway.
+HOT_GATHER_MIN_REFERENCES = 1 << 19
+
+
 def _gather(y2d: torch.Tensor, keep: torch.Tensor, src: torch.Tensor | None, parent: torch.Tensor | None,
-            weights: torch.Tensor | None, n_out: int, zero_fill: bool) -> torch.Tensor:
+            weights: torch.Tensor | None, n_out: int, zero_fill: bool, hot=None) -> torch.Tensor:
     out = torch.empty((n_out, y2d.shape[1]), device=y2d.device, dtype=y2d.dtype)
     S = 0 if src is None else src.numel()
     corners = 4 if parent is None else parent.shape[-1]
-    rc = C.lib().vb200_proj_gather(
+    lib, stream = C.lib(), C.stream_of(y2d.device)
+    if hot is None:
+        rc = lib.vb200_proj_gather(
+            C.dtype_code(y2d.dtype), y2d.data_ptr(), y2d.stride(0), keep.data_ptr(), keep.numel(),
+            C.ptr(src), C.ptr(parent), C.ptr(weights), S, corners, out.data_ptr(), out.stride(0), n_out,
+            y2d.shape[1], int(zero_fill), stream,
+        )
+        C.check(rc, "proj_gather")
+        return out
+    if zero_fill:
+        out.zero_()
+    hot_rows, hot_slot, n_hot, max_hot = hot
+    rc = lib.vb200_proj_gather_hot(
         C.dtype_code(y2d.dtype), y2d.data_ptr(), y2d.stride(0), keep.data_ptr(), keep.numel(),
         C.ptr(src), C.ptr(parent), C.ptr(weights), S, corners, out.data_ptr(), out.stride(0), n_out,
-        y2d.shape[1], int(zero_fill), C.stream_of(y2d.device),
+        y2d.shape[1], hot_rows.data_ptr(), hot_slot.data_ptr(), n_hot.data_ptr(), max_hot, stream,
     )
-    C.check(rc, "proj_gather")
+    C.check(rc, "proj_gather_hot")
     return out
 
 
@@ -184,6 +202,7 @@ class WeightedBilinearTokenPlan:
         C.require_cuda(self.keep, "WeightedBilinearTokenPlan")
         self._keep_flat = _idx(self.keep)
         self._normalizer_flat = self.normalizer.reshape(-1).to(torch.float32).contiguous()
+        self._hot = None
         if self.csr is None:
             self.csr = build_plan_csr(
                 self.source_parent_compact[0], self.source_pool_weights[0], self.kept_tokens,
@@ -273,13 +292,27 @@ class WeightedBilinearTokenPlan:
         from .ops import row_gather
         return row_gather(_as_rows(value), _idx(self.query_keep)).unsqueeze(0)
 
+    def _hot_rows(self, value: torch.Tensor):
+        """The staged-row table of the main restore (built once per plan and row width): the
+        merged rows with the most references, chosen from the plan's CSR on the device."""
+        c, dtype = value.shape[-1], value.dtype
+        key = (c, dtype)
+        if self._hot is None or self._hot[0] != key:
+            from .ops import plan_hot_rows
+            cap = C.lib().vb200_proj_gather_hot_capacity(C.dtype_code(dtype), c)
+            self._hot = (key, plan_hot_rows(self.csr, cap))
+        return self._hot[1]
+
     def _restore_with(self, value: torch.Tensor, keep: torch.Tensor, src: torch.Tensor | None,
-                      parent: torch.Tensor | None, weights: torch.Tensor | None) -> torch.Tensor:
+                      parent: torch.Tensor | None, weights: torch.Tensor | None, main: bool = False) -> torch.Tensor:
         C.require_cuda(value, "WeightedBilinearTokenPlan.restore")
         y = _as_rows(value)
         keep = _idx(keep)
         has_src = src is not None and src.numel() > 0
         covered = keep.numel() + (src.numel() if has_src else 0)
+        hot = None
+        if main and has_src and parent.numel() >= HOT_GATHER_MIN_REFERENCES:
+            hot = self._hot_rows(y)
         out = _gather(
             y, keep,
             _idx(src) if has_src else None,
@@ -287,6 +320,7 @@ class WeightedBilinearTokenPlan:
             weights.reshape(-1, weights.shape[-1]).to(torch.float32).contiguous() if has_src else None,
             self.original_tokens,
             zero_fill=covered != self.original_tokens,
+            hot=hot,
         )
         return out.unsqueeze(0)
 
@@ -304,7 +338,7 @@ class WeightedBilinearTokenPlan:
         if value.shape[0] != 1:
             raise RuntimeError("weighted bilinear compaction currently supports inference batch size one")
         return self._restore_with(value, self.keep, self.source_original, self.source_parent_compact,
-                                  self.source_restore_weights)
+                                  self.source_restore_weights, main=True)
 
     def restore_query(self, value: torch.Tensor) -> torch.Tensor:
         """Restore a tensor compacted with :meth:`compact_query`."""

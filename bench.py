@@ -23,7 +23,7 @@ time the reference's own PyTorch CPU path for the same config-2 step (oracle/tor
 the reference's operators in its order and dtypes) with every host thread.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-  python bench.py --projection-only     # config 5 alone on one GPU (for profiling its kernels)
+  python bench.py --projection-only [--projection-tokens N]   # config 5 alone on one GPU (profiling)
 """
 from __future__ import annotations
 
@@ -214,15 +214,16 @@ def cpu_baseline(repeats: int = 2) -> dict:
             "sample": _reference_sample(repeats, 1, threads, t) + " (median)"}
 
 
-def projection_stress(pkg, dev, hbm_peak: float) -> dict:
+def projection_stress(pkg, dev, hbm_peak: float, N: int = 1 << 20, reps: int = 5) -> dict:
     """Config 5 (top-4 projection bandwidth stress) on one GPU: N = 1,048,576 tokens,
     M = 65,536 evenly spaced merged tokens, D = 1024 bf16.  Each source draws four distinct
     parents Zipf(1.1) over the merged tokens (ranks mapped to ids by a seeded permutation), with
     Dirichlet(1,1,1,1) weights; sampled on the GPU.  Times the scatter (tokens -> merged,
     `plan.compact`) and the gather (merged -> tokens, `plan.restore`) with CUDA events; GB/s
-    counts compulsory HBM bytes (every token row and merged row once, plus the plan arrays)."""
+    counts compulsory HBM bytes (every token row and merged row once, plus the plan arrays).
+    ``N`` scales the case down for profiling (M = N / 16, same distributions)."""
     import torch
-    N, M, D, corners = 1 << 20, 1 << 16, 1024, 4
+    M, D, corners = N // 16, 1024, 4
     g = torch.Generator(device=dev).manual_seed(5)
     keep = torch.arange(M, device=dev, dtype=torch.long) * (N // M)
     mask = torch.ones(N, dtype=torch.bool, device=dev)
@@ -266,15 +267,15 @@ def projection_stress(pkg, dev, hbm_peak: float) -> dict:
             ms.append(e0.elapsed_time(e1))
         return statistics.median(ms)
 
-    scatter_ms = timed(lambda: plan.compact(x))
-    gather_ms = timed(lambda: plan.restore(y))
+    scatter_ms = timed(lambda: plan.compact(x), reps)
+    gather_ms = timed(lambda: plan.restore(y), reps)
     meta = S * corners * (4 + 4) + M * 4 * 2
     scatter_bytes = N * D * 2 + M * D * 2 + meta
     gather_bytes = M * D * 2 + N * D * 2 + S * corners * (8 + 8 + 4) + M * 8
     sgbs = scatter_bytes / (scatter_ms / 1e3) / 1e9
     ggbs = gather_bytes / (gather_ms / 1e3) / 1e9
     del x, y, plan
-    return {"workload": "config 5: N=1,048,576 tokens, M=65,536 merged, D=1024 bf16, Zipf(1.1) parents, "
+    return {"workload": f"config 5: N={N:,} tokens, M={M:,} merged, D=1024 bf16, Zipf(1.1) parents, "
                         "Dirichlet(1,1,1,1) weights, 1 GPU",
             "scatter_ms": scatter_ms, "scatter_gbs": sgbs, "scatter_frac": sgbs / hbm_peak,
             "gather_ms": gather_ms, "gather_gbs": ggbs, "gather_frac": ggbs / hbm_peak,
@@ -572,6 +573,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--projection-only", action="store_true",
                     help="run only the config-5 projection stress on one GPU and print its JSON")
+    ap.add_argument("--projection-tokens", type=int, default=1 << 20,
+                    help="tokens of the --projection-only case (merged = tokens / 16; smaller for ncu captures)")
+    ap.add_argument("--projection-reps", type=int, default=5, help="timed repetitions of --projection-only")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -580,7 +584,8 @@ def main() -> None:
         pkg = importlib.import_module("4d_ttt_merging_b200")
         dev = torch.device("cuda", 0)
         torch.cuda.set_device(dev)
-        print(json.dumps(projection_stress(pkg, dev, _peaks()[0])), flush=True)
+        print(json.dumps(projection_stress(pkg, dev, _peaks()[0], N=args.projection_tokens,
+                                           reps=args.projection_reps)), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

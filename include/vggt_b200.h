@@ -213,6 +213,25 @@ VB200_API int vb200_proj_gather(int dtype, const void* y, int64_t y_row_stride, 
                       int64_t K, const int64_t* src, const int64_t* parent, const float* w,
                       int64_t S, int64_t corners, void* out, int64_t out_row_stride,
                       int64_t N_out, int64_t C, int zero_fill, void* stream);
+/* Same result as vb200_proj_gather (bit for bit, zero_fill excluded: the caller zeroes rows that
+ * neither keep nor src covers), for skewed plans: the merged rows listed in hot_rows (n_hot[0]
+ * of them, at most max_hot, a DEVICE int32) are copied once per CTA into shared memory and
+ * every reference to them is read from there; hot_slot [K] maps a merged row to its slot or -1.
+ * The table comes from vb200_plan_hot_rows.  max_hot must not exceed
+ * vb200_proj_gather_hot_capacity(dtype, C) (staged rows take max_hot * C elements of shared
+ * memory per CTA).  Replaces the same reference function as vb200_proj_gather. */
+VB200_API int vb200_proj_gather_hot(int dtype, const void* y, int64_t y_row_stride, const int64_t* keep,
+                                    int64_t K, const int64_t* src, const int64_t* parent, const float* w,
+                                    int64_t S, int64_t corners, void* out, int64_t out_row_stride,
+                                    int64_t N_out, int64_t C, const int32_t* hot_rows, const int32_t* hot_slot,
+                                    const int32_t* n_hot, int max_hot, void* stream);
+VB200_API int vb200_proj_gather_hot_capacity(int dtype, int64_t C);
+/* The staging table of vb200_proj_gather_hot from a plan CSR (vb200_plan_csr_build): the merged
+ * rows with the most (source, corner) references, at most max_hot of them, chosen on the device
+ * (one block; whole reference-count buckets from the top).  hot_rows [max_hot], hot_slot [M],
+ * n_hot [1], all device int32. */
+VB200_API int vb200_plan_hot_rows(const int32_t* seg_offsets, int64_t M, int64_t corners, int max_hot,
+                                  int32_t* hot_rows, int32_t* hot_slot, int32_t* n_hot, void* stream);
 
 /* ---- a5/a10: plain row gather -----------------------------------------------------------------
  * out[i] = x[index[i]] for i < R; an index outside [0, x_rows) sets device error bit 1 and

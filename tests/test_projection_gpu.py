@@ -154,3 +154,46 @@ def test_row_ops(pkg, oracle, cuda_device):
     assert np.mean(to_np(nb) == ref) > 0.999
     g = pkg.row_gather(xt.bfloat16(), rows)
     assert torch.equal(g, xt.bfloat16()[rows])
+
+
+@pytest.mark.parametrize("dtype,C", [("bf16", 1024), ("bf16", 256), ("f16", 256), ("f32", 256)])
+def test_hot_row_gather_matches_plain(pkg, oracle, cuda_device, dtype, C, monkeypatch):
+    """Zipf(1.1)-skewed plan: the gather that stages the most-referenced merged rows in shared
+    memory (vb200_proj_gather_hot) gives the plain gather's output bit for bit (and, for 16-bit
+    types, the oracle's value-dtype restore exactly); the staged rows are exactly the rows with
+    the most references; plan.restore takes this path above HOT_GATHER_MIN_REFERENCES."""
+    from importlib import import_module
+    tp = import_module("4d_ttt_merging_b200.token_plan")
+    N, M = 16384, 1024
+    keep, src, parent, w = oracle.zipf_plan(7, N, M)
+    plan = _plan(pkg, keep, src, parent, w, N, dev=cuda_device)
+    lib = pkg.load_library()
+    cap = lib.vb200_proj_gather_hot_capacity(pkg._clib.dtype_code(TORCH_DTYPE[dtype]), C)
+    assert cap >= 64
+    hot_rows, hot_slot, n_hot, max_hot = pkg.ops.plan_hot_rows(plan.csr, cap)
+    n = int(n_hot)
+    assert 0 < n <= max_hot
+    counts = np.bincount(parent.ravel(), minlength=M)
+    slots = hot_slot.cpu().numpy()
+    staged = np.sort(hot_rows[:n].cpu().numpy())
+    np.testing.assert_array_equal(staged, np.nonzero(slots >= 0)[0])
+    np.testing.assert_array_equal(slots[staged][np.argsort(slots[staged])], np.arange(n))
+    assert counts[slots >= 0].min() > counts[slots < 0].max()  # the most-referenced rows
+    rng = np.random.default_rng(3)
+    y = oracle.round_to(rng.standard_normal((M, C)).astype(np.float32), dtype)
+    yt = torch.from_numpy(y).to(cuda_device, TORCH_DTYPE[dtype])
+    args = (yt, plan._keep_flat, plan.source_original.reshape(-1), plan.source_parent_compact[0].contiguous(),
+            plan.source_restore_weights[0].contiguous(), N, False)
+    plain = tp._gather(*args)
+    hot = tp._gather(*args, hot=(hot_rows, hot_slot, n_hot, max_hot))
+    torch.cuda.synchronize()
+    assert torch.equal(hot, plain)
+    ref = oracle.restore(y, keep, src, parent, w, N, dtype=dtype)
+    if dtype == "f32":
+        np.testing.assert_allclose(to_np(hot), ref, rtol=1e-6, atol=1e-6)
+    else:
+        np.testing.assert_array_equal(to_np(hot), ref)
+    monkeypatch.setattr(tp, "HOT_GATHER_MIN_REFERENCES", 1)
+    assert torch.equal(plan.restore(yt[None])[0], plain)
+    assert plan._hot is not None
+    assert pkg.device_error_flags() == 0
