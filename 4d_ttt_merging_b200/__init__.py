@@ -29,7 +29,7 @@ from .ops import (
     streaming_top4,
 )
 from .token_plan import TokenPlan, WeightedBilinearTokenPlan
-from .planners import build_fastvggt_plan, build_uniform_convex_plan
+from .planners import build_fastvggt_plan, build_ttt_protected_uniform_convex_plan, build_uniform_convex_plan
 from .attention_block import GlobalAttention, compute_attention
 from .install import install, uninstall
 from . import parallel
@@ -38,6 +38,7 @@ __all__ = [
     "GlobalAttention",
     "PlanCSR",
     "build_fastvggt_plan",
+    "build_ttt_protected_uniform_convex_plan",
     "build_uniform_convex_plan",
     "compute_attention",
     "install",

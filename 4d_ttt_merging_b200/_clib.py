@@ -105,6 +105,10 @@ _SIGNATURES = {
         _c_int,
         [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_int, _c_vp],
     ),
+    "vb200_support_certificate": (
+        _c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp],
+    ),
+    "vb200_row_max_dot": (_c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_int, _c_i64, _c_i64, _c_vp, _c_vp]),
     "vb200_four_support_projected_gradient": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_int, _c_vp]),
     "vb200_four_support_active_set": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_float, _c_vp]),
 }

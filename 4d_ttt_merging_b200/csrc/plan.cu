@@ -287,6 +287,129 @@ __global__ void __launch_bounds__(kFitWarps * 32)
   alpha[sl * 4 + 3] = a3;
 }
 
+// 16 channels of a feature row as fp32 (two 16-byte loads for 16-bit types, four for fp32).
+template <typename T>
+__device__ __forceinline__ void load16(const T* __restrict__ p, float (&v)[16]) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(p) + h);
+      v[4 * h] = f.x; v[4 * h + 1] = f.y; v[4 * h + 2] = f.z; v[4 * h + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p) + h);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[8 * h + q] = to_f32<T>(e[q]);
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Certificate of a four-support convex fit (the reference's solve epilogue,
+// sparse_convex.py:575-583 and :316-319): reconstruction r = sum_c alpha_c * support_c (fp32
+// products added in support order), cosine = <x, r> / (max(|x|, 1e-8) max(|r|, 1e-8)),
+// residual = |x - r|, reconstruction norm = |r|.  One warp per source, 16 channels per lane
+// per pass, fp32 sums reduced across the warp.
+template <typename T>
+__global__ void __launch_bounds__(kFitWarps * 32)
+    support_certificate_kernel(const T* __restrict__ feat, long long rows, long long fs,
+                               const int64_t* __restrict__ src_rows, const int64_t* __restrict__ parent_rows,
+                               const float* __restrict__ alpha, long long S, int D, float* __restrict__ cosine,
+                               float* __restrict__ residual, float* __restrict__ recon_norm) {
+  const long long s = static_cast<long long>(blockIdx.x) * kFitWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (s >= S) return;
+  long long r[5];
+  r[0] = src_rows ? src_rows[s] : s;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) r[c + 1] = parent_rows[s * 4 + c];
+  bool bad = false;
+#pragma unroll
+  for (int c = 0; c < 5; ++c) {
+    if (r[c] < 0 || r[c] >= rows) { bad = true; r[c] = 0; }
+  }
+  if (bad && lane == 0) atomicOr(&g_plan_err, kErrBadArgument);
+  float a[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) a[c] = alpha[s * 4 + c];
+  float xr = 0.f, xx = 0.f, rr = 0.f, dd = 0.f;
+  for (int d0 = lane * 16; d0 < D; d0 += 32 * 16) {
+    float x[16], rc[16], t[16];
+    load16<T>(feat + r[0] * fs + d0, x);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) rc[q] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      load16<T>(feat + r[c + 1] * fs + d0, t);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) rc[q] = __fadd_rn(rc[q], __fmul_rn(a[c], t[q]));
+    }
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      xr = fmaf(x[q], rc[q], xr);
+      xx = fmaf(x[q], x[q], xx);
+      rr = fmaf(rc[q], rc[q], rr);
+      const float e = x[q] - rc[q];
+      dd = fmaf(e, e, dd);
+    }
+  }
+  xr = warp_sum(xr);
+  xx = warp_sum(xx);
+  rr = warp_sum(rr);
+  dd = warp_sum(dd);
+  if (lane == 0) {
+    const float nx = sqrtf(xx), nr = sqrtf(rr);
+    cosine[s] = xr / (fmaxf(nx, 1e-8f) * fmaxf(nr, 1e-8f));
+    residual[s] = sqrtf(dd);
+    recon_norm[s] = nr;
+  }
+}
+
+// For each query row, the largest fp32 dot product with its targets (targets [Q, T], -1 =
+// none; a query with no target gets -inf): the top-1 cosine that prunes redundant uniform
+// anchors in the protected skeleton (sparse_convex.py:1404-1418).  One warp per query.
+template <typename T>
+__global__ void __launch_bounds__(kFitWarps * 32)
+    row_max_dot_kernel(const T* __restrict__ feat, long long rows, long long fs, const int64_t* __restrict__ query,
+                       const int64_t* __restrict__ targets, int n_targets, long long Q, int D,
+                       float* __restrict__ out) {
+  const long long q = static_cast<long long>(blockIdx.x) * kFitWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (q >= Q) return;
+  long long qr = query[q];
+  if (qr < 0 || qr >= rows) {
+    if (lane == 0) atomicOr(&g_plan_err, kErrBadArgument);
+    qr = 0;
+  }
+  float best = -INFINITY;
+  for (int t = 0; t < n_targets; ++t) {
+    const long long tr = targets[q * n_targets + t];
+    if (tr < 0) continue;  // uniform across the warp
+    if (tr >= rows) {
+      if (lane == 0) atomicOr(&g_plan_err, kErrBadArgument);
+      continue;
+    }
+    float acc = 0.f;
+    for (int d0 = lane * 16; d0 < D; d0 += 32 * 16) {
+      float x[16], y[16];
+      load16<T>(feat + qr * fs + d0, x);
+      load16<T>(feat + tr * fs + d0, y);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc = fmaf(x[i], y[i], acc);
+    }
+    best = fmaxf(best, warp_sum(acc));
+  }
+  if (lane == 0) out[q] = best;
+}
+
 inline unsigned blocks(long long n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
 
 }  // namespace
@@ -380,5 +503,52 @@ extern "C" int vb200_support_fit(int dtype, const void* feat, int64_t rows, int6
   else VB200_FIT(__half);
 #undef VB200_FIT
   VB200_CHECK_LAUNCH("support_fit_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_support_certificate(int dtype, const void* feat, int64_t rows, int64_t row_stride,
+                                         const int64_t* src_rows, const int64_t* parent_rows, const float* alpha,
+                                         int64_t S, int64_t D, float* cosine, float* residual, float* recon_norm,
+                                         void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16,
+                "support_certificate: bad dtype %d", dtype);
+  VB200_REQUIRE(S >= 0 && D > 0 && rows > 0, "support_certificate: bad sizes");
+  if (S == 0) return VB200_OK;
+  VB200_REQUIRE(feat && parent_rows && alpha && cosine && residual && recon_norm, "support_certificate: null pointer");
+  const int es = dtype == VB200_F32 ? 4 : 2;
+  VB200_REQUIRE(D % 16 == 0 && (row_stride * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(feat) & 15u) == 0,
+                "support_certificate: rows must be 16-byte aligned and D a multiple of 16");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_CERT(T)                                                                                   \
+  support_certificate_kernel<T><<<blocks(S, kFitWarps), kFitWarps * 32, 0, st>>>(                        \
+      static_cast<const T*>(feat), rows, row_stride, src_rows, parent_rows, alpha, S, static_cast<int>(D), \
+      cosine, residual, recon_norm)
+  if (dtype == VB200_F32) VB200_CERT(float);
+  else if (dtype == VB200_BF16) VB200_CERT(__nv_bfloat16);
+  else VB200_CERT(__half);
+#undef VB200_CERT
+  VB200_CHECK_LAUNCH("support_certificate_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_row_max_dot(int dtype, const void* feat, int64_t rows, int64_t row_stride, const int64_t* query,
+                                 const int64_t* targets, int n_targets, int64_t Q, int64_t D, float* out,
+                                 void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "row_max_dot: bad dtype %d", dtype);
+  VB200_REQUIRE(Q >= 0 && D > 0 && rows > 0 && n_targets >= 0, "row_max_dot: bad sizes");
+  if (Q == 0) return VB200_OK;
+  VB200_REQUIRE(feat && query && out && (n_targets == 0 || targets), "row_max_dot: null pointer");
+  const int es = dtype == VB200_F32 ? 4 : 2;
+  VB200_REQUIRE(D % 16 == 0 && (row_stride * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(feat) & 15u) == 0,
+                "row_max_dot: rows must be 16-byte aligned and D a multiple of 16");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_RMD(T)                                                                                      \
+  row_max_dot_kernel<T><<<blocks(Q, kFitWarps), kFitWarps * 32, 0, st>>>(                                  \
+      static_cast<const T*>(feat), rows, row_stride, query, targets, n_targets, Q, static_cast<int>(D), out)
+  if (dtype == VB200_F32) VB200_RMD(float);
+  else if (dtype == VB200_BF16) VB200_RMD(__nv_bfloat16);
+  else VB200_RMD(__half);
+#undef VB200_RMD
+  VB200_CHECK_LAUNCH("row_max_dot_kernel");
   return VB200_OK;
 }

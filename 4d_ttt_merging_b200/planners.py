@@ -25,7 +25,8 @@ from . import _clib as C
 from .ops import build_plan_csr, row_normalize_bf16, similarity_topk
 from .token_plan import TokenPlan, WeightedBilinearTokenPlan
 
-__all__ = ["build_fastvggt_plan", "build_uniform_convex_plan", "fastvggt_tables", "uniform_keep_layout"]
+__all__ = ["build_fastvggt_plan", "build_uniform_convex_plan", "build_ttt_protected_uniform_convex_plan",
+           "fastvggt_tables", "ttt_skeleton_tables", "uniform_keep_layout"]
 
 FAST_MATCH_SOURCE_CHUNK = 5000
 
@@ -199,3 +200,324 @@ def _device_layout(lay: dict, dev: torch.device) -> dict:
         hit["source_keep"] = torch.cat([hit["source"], hit["keep"]])  # feature-row order of the planner
         _DEVICE_LAYOUTS[key] = hit
     return hit
+
+
+# ------------------------------------------------------------------------------------------
+# The released planner: build_ttt_protected_uniform_convex_plan
+# ------------------------------------------------------------------------------------------
+LOCAL_FRAME_GROUP = 8  # frames per temporal-local support search (sparse_convex.py:31)
+
+
+@functools.lru_cache(maxsize=32)
+def ttt_skeleton_tables(frames: int, patch_hw: tuple[int, int]):
+    """Static tables of the protected uniform skeleton (host, cached), following
+    sparse_convex.py:1327-1368: one patch per 2x2 cell of every later frame drawn from a fresh
+    CPU generator seeded 0 (the same draw as the uniform planners), grouped by 4x4 macro cell in
+    position order (slot 0 is the protected anchor), and for every (frame, cell, slot) the
+    candidate targets that can make a non-protected anchor redundant: the reference frame's
+    patches of the cell, the cell's slot-0 anchor and the previous frame's slot-0 anchor.
+    -> dict(first [P], anchors [F-1, cells, 4] (-1 = empty slot), targets [F-1, cells, 4, T])."""
+    height, width = patch_hw
+    patches = height * width
+    first = torch.arange(patches)
+    if frames <= 1:
+        empty = torch.empty((0, 0, 4), dtype=torch.long)
+        return dict(first=first, anchors=empty, targets=torch.empty((0, 0, 4, 18), dtype=torch.long))
+    generator = torch.Generator(device="cpu").manual_seed(0)
+    rows, cols = torch.arange(0, height, 2), torch.arange(0, width, 2)
+    draw = torch.rand(frames - 1, len(rows), len(cols), 2, generator=generator)
+    r = rows[None, :, None] + (draw[..., 0] * (height - rows).clamp(max=2)[None, :, None]).long()
+    c = cols[None, None, :] + (draw[..., 1] * (width - cols).clamp(max=2)[None, None, :]).long()
+    position = (r * width + c).reshape(frames - 1, -1)
+    cells_x, cells_y = (width + 3) // 4, (height + 3) // 4
+    cell = (position // width // 4) * cells_x + (position % width) // 4
+    anchors = torch.full((frames - 1, cells_x * cells_y, 4), -1, dtype=torch.long)
+    for f in range(frames - 1):
+        filled = [0] * (cells_x * cells_y)
+        for p, g in zip(position[f].tolist(), cell[f].tolist()):
+            anchors[f, g, filled[g]] = (f + 1) * patches + p
+            filled[g] += 1
+    reference = torch.full((cells_x * cells_y, 16), -1, dtype=torch.long)
+    for g in range(cells_x * cells_y):
+        top, left = (g // cells_x) * 4, (g % cells_x) * 4
+        ids = [y * width + x for y in range(top, min(top + 4, height)) for x in range(left, min(left + 4, width))]
+        reference[g, :len(ids)] = torch.tensor(ids)
+    protected = anchors[..., 0]
+    previous = torch.cat([torch.full_like(protected[:1], -1), protected[:-1]])
+    per_cell = torch.cat([reference[None].expand(frames - 1, -1, -1), protected[..., None], previous[..., None]], -1)
+    targets = per_cell[:, :, None, :].expand(-1, -1, 4, -1).contiguous()
+    return dict(first=first, anchors=anchors, targets=targets)
+
+
+def _feature_fit(features: torch.Tensor, source_ids: torch.Tensor, support_ids: torch.Tensor, steps: int = 32):
+    """The reference's solve for given supports (sparse_convex.py:558-583): fp32 Gram and rhs of
+    the four supports, 32 projected-gradient steps (vb200_support_fit), then the certificate
+    (vb200_support_certificate).  -> (weights [S,4], cosine, residual, reconstruction norm)."""
+    S = source_ids.numel()
+    dev = features.device
+    alpha = torch.empty((S, 4), device=dev, dtype=torch.float32)
+    cos, res, nrm = (torch.empty(S, device=dev, dtype=torch.float32) for _ in range(3))
+    if S == 0:
+        return alpha, cos, res, nrm
+    src = source_ids.to(torch.int64).contiguous()
+    sup = support_ids.to(torch.int64).contiguous()
+    lib, stream = C.lib(), C.stream_of(dev)
+    dt, rows, stride, D = C.dtype_code(features.dtype), features.shape[0], features.stride(0), features.shape[1]
+    C.check(lib.vb200_support_fit(dt, features.data_ptr(), rows, stride, src.data_ptr(), sup.data_ptr(), S, D,
+                                  None, None, alpha.data_ptr(), int(steps), stream), "support_fit")
+    C.check(lib.vb200_support_certificate(dt, features.data_ptr(), rows, stride, src.data_ptr(), sup.data_ptr(),
+                                          alpha.data_ptr(), S, D, cos.data_ptr(), res.data_ptr(), nrm.data_ptr(),
+                                          stream), "support_certificate")
+    return alpha, cos, res, nrm
+
+
+def _certified(cos, res, nrm, threshold: float) -> torch.Tensor:
+    """cosine >= tau, residual <= sqrt(2 (1 - tau)), reconstruction norm >= 0.8
+    (sparse_convex.py:648-653, 1870-1874, 1898-1902)."""
+    return (cos >= threshold) & (res <= (2.0 * (1.0 - threshold)) ** 0.5) & (nrm >= 0.80)
+
+
+def _fit_global(features, basis_ids, source_ids):
+    """The exact global route (_adaptive_fit_fused, sparse_convex.py:168-330, feature route with the
+    one-hot shortcut off): top-4 of every source over the whole basis, then the solve."""
+    from .ops import row_gather
+    q = row_gather(features, source_ids)
+    b = row_gather(features, basis_ids)
+    _, idx = similarity_topk(q, b, 4)
+    support = basis_ids[idx]
+    return (support,) + _feature_fit(features, source_ids, support)
+
+
+def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, threshold: float, source_ids):
+    """_adaptive_fit_temporal_local (sparse_convex.py:440-684), feature route: sources of frames
+    [b, b + 8) (b = 1, 9, ...) take their top-4 among the basis of frame 0 and frames
+    [max(1, b - 1), min(F - 1, b + 8)] (one grouped tcgen05 search for all groups), one fused
+    solve, the certificate; uncertified rows (and reference-frame sources, which no group covers)
+    take the global route.  basis_ids / source_ids sorted ascending.
+    -> (support ids [S,4], weights, cosine, residual, reconstruction norm)."""
+    from .ops import row_gather
+    dev = features.device
+    n = source_ids.numel()
+    if n == 0 or basis_ids.numel() == 0:
+        empty = torch.zeros((n, 4), device=dev, dtype=torch.long)
+        return (empty,) + _feature_fit(features, source_ids, empty)
+    starts = list(range(1, frames, LOCAL_FRAME_GROUP))
+    ends = [min(b + LOCAL_FRAME_GROUP, frames) for b in starts]
+    lo = [max(1, b - 1) for b in starts]
+    hi = [min(frames - 1, e) for e in ends]
+    cut = torch.tensor([1] + starts + ends + lo + [h + 1 for h in hi], device=dev) * patches
+    s_pos = torch.searchsorted(source_ids, cut[1:1 + 2 * len(starts)]).tolist()
+    b_pos = torch.searchsorted(basis_ids, torch.cat([cut[:1], cut[1 + 2 * len(starts):]])).tolist()
+    g = len(starts)
+    s_begin, s_end = s_pos[:g], s_pos[g:]
+    b0, b_lo, b_hi = b_pos[0], b_pos[1:1 + g], b_pos[1 + g:]
+    # one query row per grouped source, one concatenated basis list per group
+    q_rows, b_lists, qb, bb = [], [], [0], [0]
+    for k in range(g):
+        q_rows.append(torch.arange(s_begin[k], s_end[k], device=dev))
+        b_lists.append(torch.cat([basis_ids[:b0], basis_ids[b_lo[k]:b_hi[k]]]))
+        qb.append(qb[-1] + s_end[k] - s_begin[k])
+        bb.append(bb[-1] + b_lists[-1].numel())
+    rows = torch.cat(q_rows)
+    local_basis = torch.cat(b_lists)
+    support = basis_ids[:1].expand(n, 4).clone()
+    weights = torch.zeros((n, 4), device=dev, dtype=torch.float32)
+    cos, res, nrm = (torch.zeros(n, device=dev, dtype=torch.float32) for _ in range(3))
+    assigned = torch.zeros(n, device=dev, dtype=torch.bool)
+    if rows.numel():
+        _, idx = similarity_topk(row_gather(features, source_ids[rows]), row_gather(features, local_basis), 4,
+                                 query_begin=torch.tensor(qb), basis_begin=torch.tensor(bb))
+        chosen = local_basis[idx]
+        fit = _feature_fit(features, source_ids[rows], chosen)
+        support[rows], weights[rows] = chosen, fit[0]
+        cos[rows], res[rows], nrm[rows] = fit[1], fit[2], fit[3]
+        assigned[rows] = True
+    fallback = torch.nonzero(~(assigned & _certified(cos, res, nrm, threshold))).flatten()
+    if fallback.numel():
+        gfit = _fit_global(features, basis_ids, source_ids[fallback])
+        support[fallback], weights[fallback] = gfit[0], gfit[1]
+        cos[fallback], res[fallback], nrm[fallback] = gfit[2], gfit[3], gfit[4]
+    return support, weights, cos, res, nrm
+
+
+def _ttt_event_bases(features, geometry, labels, sensitivity, excluded, *, patches: int, amount: int,
+                     geometry_weight: float) -> torch.Tensor:
+    """TTT-proposed event bases (sparse_convex.py:1268-1324) on the device: sensitive patches
+    (label 1, not excluded) binned by 4-frame time bin and 0.5-wide xyz bins; per bin the patch
+    whose feature is closest to the bin's normalised mean feature, with a geometry penalty and a
+    0.005 sensitivity bonus (lowest id on ties); with more bins than ``amount`` the bins with the
+    largest mean sensitivity x sqrt(size) win; with fewer, the most sensitive remaining patches
+    fill up.  Sorted unique patch ids."""
+    ids = torch.nonzero((labels == 1) & ~excluded).flatten()
+    if amount <= 0 or ids.numel() == 0:
+        return ids[:0]
+    geo = geometry.index_select(0, ids)
+    xyz = torch.floor((geo[:, :3] + 4.0) / 0.5).long().clamp(0, 31)
+    time_bin = (ids // patches) // 4
+    code = ((time_bin * 37 + xyz[:, 0]) * 37 + xyz[:, 1]) * 37 + xyz[:, 2]
+    _, inverse = torch.unique(code, return_inverse=True)
+    groups = int(inverse.max()) + 1
+    counts = torch.bincount(inverse, minlength=groups)
+    order = inverse.argsort(stable=True)
+    feat = features.index_select(0, ids).float()
+    mean_f = torch.segment_reduce(feat.index_select(0, order), "mean", lengths=counts)
+    center_f = torch.nn.functional.normalize(mean_f, dim=-1, eps=1e-8)
+    center_g = torch.segment_reduce(geo.index_select(0, order), "mean", lengths=counts)
+    sens = sensitivity.index_select(0, ids)
+    score = ((feat * center_f.index_select(0, inverse)).sum(-1)
+             - geometry_weight * (geo - center_g.index_select(0, inverse)).square().sum(-1) + 0.005 * sens)
+    best = torch.full((groups,), -torch.inf, device=ids.device)
+    best.scatter_reduce_(0, inverse, score, reduce="amax", include_self=True)
+    sentinel = labels.numel()
+    candidate = torch.where(score == best.index_select(0, inverse), ids, torch.full_like(ids, sentinel))
+    rep = torch.full((groups,), sentinel, device=ids.device, dtype=torch.long)
+    rep.scatter_reduce_(0, inverse, candidate, reduce="amin", include_self=True)
+    rep = rep[rep < sentinel]
+    if rep.numel() > amount:
+        group_score = torch.segment_reduce(sens.index_select(0, order), "mean", lengths=counts) * counts.float().sqrt()
+        rep = rep.index_select(0, group_score.topk(amount).indices)
+    if rep.numel() < amount:
+        chosen = torch.zeros(labels.numel(), device=ids.device, dtype=torch.bool)
+        chosen[rep] = True
+        remaining = ids[~chosen.index_select(0, ids)]
+        fill = min(amount - rep.numel(), remaining.numel())
+        if fill:
+            rep = torch.cat([rep, remaining.index_select(0, sensitivity.index_select(0, remaining).topk(fill).indices)])
+    return torch.unique(rep)
+
+
+@torch.no_grad()
+def build_ttt_protected_uniform_convex_plan(
+        tokens: torch.Tensor, *, frames: int, tokens_per_frame: int, patch_token_start: int,
+        patch_hw: tuple[int, int], threshold: float, labels: torch.Tensor, sensitivity: torch.Tensor,
+        geometry: torch.Tensor, max_support: int = 4, preserve_queries: bool = False,
+        preserve_destination_keys: bool | None = None, top1_prune_threshold: float = .95,
+        sensitive_event_ratio: float = .02, selection_geometry_weight: float = .01,
+        support_geometry_weight: float = 0.0, support_geometry_guard_tolerance: float | None = None,
+        fixed_dynamic_mask: torch.Tensor | None = None) -> WeightedBilinearTokenPlan:
+    """Protected uniform skeleton plus TTT-proposed residual event bases, the reference's
+    released planner (vggt_omega/models/sparse_convex.py:1738-2016), on B200.
+
+    Steps: bf16 patch features (row normalisation kernel, eps 1e-8); the protected uniform
+    skeleton with 4x4 top-1 pruning (vb200_row_max_dot); TTT event proposals (at most twice the
+    freed budget) kept only where the skeleton cannot certify them; the temporal-local support
+    search (grouped tcgen05 top-4 per 8-frame group), the fused Gram + 32-step projected-gradient
+    fit and its certificate, with the global route for uncertified sources; sources that still
+    fail stay physical; the plan's CSR and masses on the device.  Supports come from the feature
+    route (support_geometry_weight = 0, the default); the geometry-aware support search and the
+    fixed-topology / fixed-dynamic-basis variants behind environment switches are not built."""
+    import os
+    if tokens.shape[0] != 1 or max_support != 4:
+        raise ValueError("protected TTT planner requires batch one and four supports")
+    if support_geometry_weight:
+        raise ValueError("this planner builds the feature-only support route (support_geometry_weight=0)")
+    if os.environ.get("VGGT_TTT_FIXED_TOPOLOGY", "0") == "1" or os.environ.get("VGGT_TTT_FIXED_DYNAMIC_BASIS_PATH"):
+        raise ValueError("the fixed-topology and fixed-dynamic-basis planner variants are not built")
+    C.require_cuda(tokens, "build_ttt_protected_uniform_convex_plan")
+    height, width = patch_hw
+    patches = height * width
+    patch_count = frames * patches
+    total, dev = tokens.shape[1], tokens.device
+    if total != frames * tokens_per_frame or patch_token_start + patches != tokens_per_frame:
+        raise ValueError("invalid protected TTT token layout")
+    if labels.numel() != patch_count or sensitivity.numel() != patch_count:
+        raise ValueError("TTT labels/sensitivity must contain one value per patch token")
+    if geometry.shape != (patch_count, 4):
+        raise ValueError("TTT geometry must be [frames*patches,4]")
+    if selection_geometry_weight < 0 or support_geometry_weight < 0:
+        raise ValueError("TTT geometry weights must be nonnegative")
+    labels = labels.to(device=dev, dtype=torch.long).reshape(-1)
+    sensitivity = sensitivity.to(device=dev, dtype=torch.float32).reshape(-1)
+    geometry = geometry.to(device=dev, dtype=torch.float32)
+    patch_ids = (torch.arange(frames, device=dev)[:, None] * tokens_per_frame + patch_token_start
+                 + torch.arange(patches, device=dev)[None]).flatten()
+    features = row_normalize_bf16(tokens[0], patch_ids, eps=1e-8)
+
+    # protected uniform skeleton (sparse_convex.py:1371-1434)
+    tab = ttt_skeleton_tables(frames, tuple(patch_hw))
+    first = tab["first"].to(dev)
+    pruned = torch.zeros(0, device=dev, dtype=torch.bool)
+    if frames > 1:
+        anchors = tab["anchors"].to(dev)
+        valid = anchors >= 0
+        query = anchors.clamp_min(0).reshape(-1)
+        targets = tab["targets"].to(dev).reshape(query.numel(), -1)
+        top1 = torch.empty(query.numel(), device=dev, dtype=torch.float32)
+        C.check(C.lib().vb200_row_max_dot(C.dtype_code(features.dtype), features.data_ptr(), features.shape[0],
+                                          features.stride(0), query.data_ptr(), targets.data_ptr(), targets.shape[1],
+                                          query.numel(), features.shape[1], top1.data_ptr(), C.stream_of(dev)),
+                "row_max_dot")
+        removable = valid & (torch.arange(4, device=dev) > 0)
+        pruned = removable & (top1.view_as(valid) >= top1_prune_threshold)
+        stable = torch.unique(torch.cat([first, anchors[valid & ~pruned]]))
+    else:
+        stable = first
+    freed = int(pruned.sum())
+    pruning = top1_prune_threshold <= 1.0
+    budget = freed if pruning else int(round(sensitive_event_ratio * patch_count))
+    stable_mask = torch.zeros(patch_count, device=dev, dtype=torch.bool)
+    stable_mask[stable] = True
+
+    # TTT event proposals, kept where the skeleton cannot certify them (:1815-1880)
+    if fixed_dynamic_mask is not None:
+        if fixed_dynamic_mask.numel() != patch_count:
+            raise ValueError("predicted fixed dynamic basis mask has the wrong token count")
+        event = torch.nonzero(fixed_dynamic_mask.to(device=dev, dtype=torch.bool).reshape(-1)).flatten()
+        event = event[~stable_mask.index_select(0, event)]
+        proposal = event
+    else:
+        proposal = _ttt_event_bases(features, geometry, labels, sensitivity, stable_mask, patches=patches,
+                                    amount=2 * budget, geometry_weight=selection_geometry_weight)
+        event = proposal[:0]
+        if budget and proposal.numel():
+            efit = _fit_temporal_local(features, stable, frames=frames, patches=patches, threshold=threshold,
+                                       source_ids=proposal)
+            cand = torch.nonzero(~_certified(efit[2], efit[3], efit[4], threshold)).flatten()
+            if cand.numel() > budget:
+                priority = sensitivity.index_select(0, proposal.index_select(0, cand)) * efit[3].index_select(0, cand)
+                cand = cand.index_select(0, priority.topk(budget).indices)
+            event = proposal.index_select(0, cand)
+
+    # every remaining patch: temporal-local fit, certificate, global fallback (:1882-1902)
+    basis = torch.unique(torch.cat([stable, event]))
+    basis_mask = torch.zeros(patch_count, device=dev, dtype=torch.bool)
+    basis_mask[basis] = True
+    source = torch.nonzero(~basis_mask).flatten()
+    support, weights, cos, res, nrm = _fit_temporal_local(features, basis, frames=frames, patches=patches,
+                                                          threshold=threshold, source_ids=source)
+    accepted = _certified(cos, res, nrm, threshold)
+    rows = torch.nonzero(accepted).flatten()
+    source_local = source.index_select(0, rows)
+    support_local = support.index_select(0, rows)
+    weights = weights.index_select(0, rows).float().contiguous()
+
+    # the plan (:1932-1976)
+    kept_mask = torch.ones(patch_count, device=dev, dtype=torch.bool)
+    kept_mask[source_local] = False
+    keep_local = torch.nonzero(kept_mask).flatten()
+    special = (torch.arange(frames, device=dev)[:, None] * tokens_per_frame
+               + torch.arange(patch_token_start, device=dev)[None]).flatten()
+    keep = torch.sort(torch.cat([special, patch_ids.index_select(0, keep_local)])).values
+    original_to_compact = torch.full((total,), -1, device=dev, dtype=torch.long)
+    original_to_compact[keep] = torch.arange(keep.numel(), device=dev)
+    parent = original_to_compact.index_select(0, patch_ids.index_select(0, support_local.reshape(-1)))
+    parent = parent.view(-1, 4)
+    if bool((parent < 0).any()):
+        raise RuntimeError("protected TTT convex support must remain physical")
+    source_original = patch_ids.index_select(0, source_local)
+    csr = build_plan_csr(parent, weights, keep.numel(), src_rows=source_original)
+    mass = csr.mass.view(1, -1, 1)
+    return WeightedBilinearTokenPlan(
+        csr=csr, keep=keep[None], source_original=source_original[None], source_parent_compact=parent[None],
+        source_pool_weights=weights[None], source_restore_weights=weights[None], original_tokens=total,
+        normalizer=mass, preserve_queries=preserve_queries,
+        preserve_destination_keys=preserve_queries if preserve_destination_keys is None else preserve_destination_keys,
+        dense_special_queries=True, special_query_original=special,
+        special_query_compact=original_to_compact.index_select(0, special), key_log_mass=csr.log_mass[None],
+        metadata={"planner": "ttt_protected_uniform_residual_convex_v1", "threshold": float(threshold),
+                  "max_support": 4, "top1_prune_threshold": float(top1_prune_threshold),
+                  "top1_pruning_enabled": bool(pruning), "protected_uniform_bases": int(stable.numel()),
+                  "top1_pruned_uniform_bases": freed, "sensitive_event_budget": budget,
+                  "sensitive_event_proposals": int(proposal.numel()), "sensitive_event_bases": int(event.numel()),
+                  "fit_failure_promotions": int((~accepted).sum()), "physical_patch_tokens": int(keep_local.numel())},
+    )

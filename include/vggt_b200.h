@@ -322,6 +322,22 @@ VB200_API int vb200_support_fit(int dtype, const void* feat, int64_t rows, int64
                                 const int64_t* src_rows, const int64_t* parent_rows, int64_t S,
                                 int64_t D, float* gram, float* rhs, float* alpha, int steps,
                                 void* stream);
+/* Certificate of the fits above (the reference's solve epilogue, models/sparse_convex.py:575-583,
+ * :316-319 and the acceptance test :648-653 that reads it): per source the reconstruction
+ * r = sum_c alpha[s,c] * feat[parent_rows[s,c]], cosine = <x, r> / (max(|x|,1e-8) max(|r|,1e-8)),
+ * residual = |x - r|, recon_norm = |r|, with x = feat[src_rows[s]] (src_rows NULL: row s).
+ * alpha [S,4] fp32; outputs [S] fp32.  D % 16 == 0. */
+VB200_API int vb200_support_certificate(int dtype, const void* feat, int64_t rows, int64_t row_stride,
+                                        const int64_t* src_rows, const int64_t* parent_rows, const float* alpha,
+                                        int64_t S, int64_t D, float* cosine, float* residual, float* recon_norm,
+                                        void* stream);
+/* out[q] = max over t of the fp32 dot product <feat[query[q]], feat[targets[q, t]]> (targets
+ * [Q, n_targets] int64, -1 = no target; -inf when a query has none): the top-1 cosine that
+ * prunes redundant uniform anchors in the released planner's protected skeleton
+ * (models/sparse_convex.py:1404-1418).  D % 16 == 0. */
+VB200_API int vb200_row_max_dot(int dtype, const void* feat, int64_t rows, int64_t row_stride, const int64_t* query,
+                                const int64_t* targets, int n_targets, int64_t Q, int64_t D, float* out,
+                                void* stream);
 
 /* ---- next tier: 4-support simplex solvers ------------------------------------------------
  * Replaces four_support_projected_gradient (models/sparse_convex_kernels.py:283-296) and

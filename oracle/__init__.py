@@ -12,3 +12,4 @@ the script that made them live in ``tests/golden/``.
 from .ref import *  # noqa: F401,F403
 from .synth import *  # noqa: F401,F403
 from . import pipeline  # noqa: F401
+from . import ttt_planner  # noqa: F401

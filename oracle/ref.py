@@ -281,13 +281,14 @@ def torch_cpu_rand(seed: int, count: int) -> np.ndarray:
     return ((raw & ((1 << 24) - 1)).astype(np.float64) * 2.0 ** -24).astype(np.float32)
 
 
-def normalize_bf16(x) -> np.ndarray:
-    """``F.normalize(x.float(), dim=-1).to(bfloat16)`` (token_merging.py:1102-1103): the row
-    norm in float64 rounded to fp32, clamped at 1e-12, the fp32 quotient rounded to bf16."""
+def normalize_bf16(x, eps: float = 1e-12) -> np.ndarray:
+    """``F.normalize(x.float(), dim=-1, eps=eps).to(bfloat16)`` (token_merging.py:1102-1103;
+    eps 1e-8 in sparse_convex.py:1791-1793): the row norm in float64 rounded to fp32, clamped at
+    eps, the fp32 quotient rounded to bf16."""
     x = np.asarray(x, dtype=np.float32)
     x64 = x.astype(np.float64)
     n = np.sqrt((x64 * x64).sum(axis=1, keepdims=True)).astype(np.float32)
-    return round_bf16((x / np.maximum(n, np.float32(1e-12))).astype(np.float32))
+    return round_bf16((x / np.maximum(n, np.float32(eps))).astype(np.float32))
 
 
 def _patch_ids(frames, tokens_per_frame, patch_token_start):

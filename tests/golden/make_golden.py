@@ -179,6 +179,52 @@ def main() -> None:
     out["as_alpha"] = _np(alpha)
     out["as_cosine"] = _np(cos)
 
+    # ---------------- released planner: build_ttt_protected_uniform_convex_plan ----------------
+    # The Triton projected-gradient kernel cannot run on a CPU; its PyTorch restatement
+    # (oracle/torch_path.py, itself checked against _adaptive_fit above) stands in for it.
+    import vggt_omega.models.sparse_convex as sc
+    sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
+    from oracle.torch_path import projected_gradient as torch_pg
+    sc.four_support_projected_gradient = lambda gram, rhs, *, steps=32: torch_pg(gram.float(), rhs.float(), steps)
+    for tag, prune, ratio, noise in (("ttt_prune", 0.95, 0.02, 0.15), ("ttt_noprune", 2.0, 0.05, 0.35)):
+        gen = torch.Generator().manual_seed(70 if prune <= 1 else 71)
+        frames, hw, pts, dim = 10, (8, 8), 5, 64
+        patches = hw[0] * hw[1]
+        tpf = pts + patches
+        base = torch.randn(patches, dim, generator=gen)
+        tok = torch.randn(frames, tpf, dim, generator=gen)
+        tok[:, pts:] = base[None] + noise * torch.randn(frames, patches, dim, generator=gen)
+        moving = torch.zeros(frames, patches, dtype=torch.bool)
+        moving[5:, 10:30] = True  # a region whose content changes in later frames
+        tok[:, pts:][moving] = torch.randn(int(moving.sum()), dim, generator=gen)
+        labels = (moving | (torch.rand(frames, patches, generator=gen) < 0.05)).long().flatten()
+        labels[:patches] = 0
+        sensitivity = torch.rand(frames * patches, generator=gen)
+        geometry = torch.randn(frames * patches, 4, generator=gen)
+        tokens = tok.reshape(1, frames * tpf, dim)
+        plan = sc.build_ttt_protected_uniform_convex_plan(
+            tokens, frames=frames, tokens_per_frame=tpf, patch_token_start=pts, patch_hw=hw, threshold=0.9,
+            labels=labels, sensitivity=sensitivity, geometry=geometry, top1_prune_threshold=prune,
+            sensitive_event_ratio=ratio)
+        out[f"{tag}_tokens"] = _np(tokens[0])
+        out[f"{tag}_labels"] = _np(labels)
+        out[f"{tag}_sensitivity"] = _np(sensitivity)
+        out[f"{tag}_geometry"] = _np(geometry)
+        out[f"{tag}_keep"] = _np(plan.keep[0])
+        out[f"{tag}_source"] = _np(plan.source_original[0])
+        out[f"{tag}_parent"] = _np(plan.source_parent_compact[0])
+        out[f"{tag}_weights"] = _np(plan.source_pool_weights[0])
+        out[f"{tag}_normalizer"] = _np(plan.normalizer[0, :, 0])
+        out[f"{tag}_special_compact"] = _np(plan.special_query_compact)
+        md = plan.metadata
+        out[f"{tag}_counts"] = np.array([md["protected_uniform_bases"], md["top1_pruned_uniform_bases"],
+                                         md["sensitive_event_budget"], md["sensitive_event_proposals"],
+                                         md["sensitive_event_bases"], md["fit_failure_promotions"],
+                                         md["global_fallback_candidates"]], np.int64)
+        print(tag, {k: md[k] for k in ("protected_uniform_bases", "top1_pruned_uniform_bases",
+                                       "sensitive_event_budget", "sensitive_event_proposals", "sensitive_event_bases",
+                                       "fit_failure_promotions", "global_fallback_candidates", "physical_patch_tokens")})
+
     # ---------------- CPU generator stream ----------------
     out["rand_seed3"] = _np(torch.rand(2, 4, 4, 2, generator=torch.Generator(device="cpu").manual_seed(3)))
 

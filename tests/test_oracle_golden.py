@@ -136,3 +136,44 @@ def test_mass_bias_attention_known_answers(oracle):
     # zero log-mass is plain softmax attention
     np.testing.assert_allclose(oracle.mass_bias_attention(q, k, v, np.zeros(7, np.float32)),
                                oracle.mass_bias_attention(q, k, v), rtol=1e-12)
+
+
+@pytest.mark.parametrize("tag,prune,ratio", [("ttt_prune", 0.95, 0.02), ("ttt_noprune", 2.0, 0.05)])
+def test_ttt_planner_matches_reference(oracle, golden, tag, prune, ratio):
+    """The released planner (build_ttt_protected_uniform_convex_plan) restated in numpy against
+    the reference's own output: same keep set, sources, parents and masses; weights to fp32
+    solver precision."""
+    g = lambda k: golden[f"{tag}_{k}"]
+    plan = oracle.ttt_planner.build_plan(
+        g("tokens"), frames=10, tokens_per_frame=69, patch_token_start=5, patch_hw=(8, 8), threshold=0.9,
+        labels=g("labels"), sensitivity=g("sensitivity"), geometry=g("geometry"), top1_prune_threshold=prune,
+        sensitive_event_ratio=ratio)
+    counts = g("counts")  # stable bases, pruned, event budget, proposals, events, promotions, fallbacks
+    assert len(plan["stable_basis"]) == counts[0]
+    assert len(plan["event_proposal"]) == counts[3] and len(plan["event"]) == counts[4]
+    assert int((~plan["accepted"]).sum()) == counts[5]
+    np.testing.assert_array_equal(plan["keep"], g("keep"))
+    np.testing.assert_array_equal(plan["source"], g("source"))
+    np.testing.assert_array_equal(plan["special_compact"], g("special_compact"))
+    # parents: bit-exact up to exact bf16 ties (torch.topk orders equal scores its own way): every
+    # row's four picks have the same bf16 score sequence as the reference's
+    tpf, keep, feats = 69, plan["keep"], plan["features"]
+    patch = lambda tok: (tok // tpf) * 64 + tok % tpf - 5
+    src = patch(plan["source"])
+    ours, theirs = plan["parent"], g("parent")
+    score = lambda par: oracle.round_bf16(np.einsum("sd,scd->sc", feats[src].astype(np.float64),
+                                                    feats[patch(keep[par])].astype(np.float64)).astype(np.float32))
+    np.testing.assert_array_equal(score(ours), score(theirs))
+    same = np.all(ours == theirs, axis=1)
+    assert same.mean() > 0.8
+    # weights: identical supports give the reference's weights; where a tie moved which support
+    # comes first (the solver starts from support 0), the same support set still matches per id
+    np.testing.assert_allclose(plan["weights"][same], g("weights")[same], rtol=1e-4, atol=2e-5)
+    first = ~same & (ours[:, 0] == theirs[:, 0]) & np.array([set(a) == set(b) for a, b in zip(ours, theirs)])
+    for r in np.nonzero(first)[0]:
+        wa = dict(zip(ours[r], plan["weights"][r]))
+        np.testing.assert_allclose([wa[c] for c in theirs[r]], g("weights")[r], rtol=1e-4, atol=2e-5)
+    # masses: deterministic_weighted_normalizer of the reference's own parents and weights equals
+    # its normaliser; ours is the same function of our parents and weights
+    np.testing.assert_allclose(oracle.normalizer(theirs, g("weights"), len(keep)), g("normalizer"), rtol=1e-6)
+    np.testing.assert_allclose(plan["normalizer"], oracle.normalizer(ours, plan["weights"], len(keep)), rtol=1e-6)
