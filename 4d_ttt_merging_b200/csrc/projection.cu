@@ -99,27 +99,27 @@ __device__ __forceinline__ void gather_keep_row(const T* __restrict__ y, long lo
   for (int i = lane; i < nvec; i += 32) d[i] = __ldg(s + i);
 }
 
-// Source rows [base, base + 32) of the gather, one warp.  Lane l first loads the indices of
-// source base + l (destination, parents, weights, staging slots: coalesced, one round trip for
-// 32 sources), then the warp walks the 32 sources with the indices broadcast by shuffles, so
+// Source rows [base, base + per_warp) of the gather (per_warp <= 32), one warp.  Lane l first
+// loads the indices of source base + l (destination, parents, weights, staging slots: coalesced,
+// one round trip for the batch), then the warp walks the batch with the indices broadcast by
+// shuffles, so
 // each source costs one round trip for its parent rows alone.  All four parents' vectors of a
-// 32 x kGatherQ column block (a whole 1024-channel bf16 row, 8 KB per warp) are loaded before
-// any is used.  (Half rows at 64 registers, 32 warps per SM, measured slower: 1.11 vs 0.89 ms on
-// config 5.)  With
+// 32 x kGatherQ column block are loaded before any is used: kGatherQ = 4 (a whole 1024-channel
+// bf16 row, 8 KB per warp, ~125 registers) for large plans, kGatherQ = 1 (one vector per lane,
+// ~60 registers, twice the resident warps) with one source per warp for small ones.  (Half rows
+// at 64 registers with 32-source batches measured slower on config 5: 1.11 vs 0.89 ms.)  With
 // `hot` the parents that have a staging slot are read from that shared-memory copy.
-constexpr int kGatherQ = 4;
-
-template <typename T, bool kHot>
+template <typename T, bool kHot, int kGatherQ>
 __device__ __forceinline__ void gather_sources(const T* __restrict__ y, long long ys, long long K,
                                                const int64_t* __restrict__ src, const int64_t* __restrict__ parent,
                                                const float* __restrict__ w, long long S, int corners,
                                                T* __restrict__ out, long long os, long long N_out, int C,
-                                               long long base, int lane, const int32_t* __restrict__ hot_slot,
-                                               const T* hot) {
+                                               long long base, int per_warp, int lane,
+                                               const int32_t* __restrict__ hot_slot, const T* hot) {
   constexpr int V = Vec<T>::N;
   const int nvec = C / V;
-  // ---- per-lane indices of source base + lane ----
-  const long long sl = base + lane;
+  // ---- per-lane indices of source base + lane (lanes < per_warp) ----
+  const long long sl = lane < per_warp ? base + lane : S;
   long long dst = -1;
   int prow[4] = {0, 0, 0, 0};  // parent row of y, or ~slot when the row is staged
   float wl[4] = {0.f, 0.f, 0.f, 0.f};
@@ -144,7 +144,7 @@ __device__ __forceinline__ void gather_sources(const T* __restrict__ y, long lon
       }
     }
   }
-  const int n = static_cast<int>(min(32ll, S - base));
+  const int n = static_cast<int>(min(static_cast<long long>(per_warp), S - base));
   for (int t = 0; t < n; ++t) {
     const long long d = __shfl_sync(0xffffffffu, dst, t);
     int pr[4];
@@ -217,16 +217,16 @@ __device__ __forceinline__ void gather_sources(const T* __restrict__ y, long lon
   }
 }
 
-// Plain form: warps [0, keep_warps) copy one keep row each; every further warp gathers 32
-// sources, every parent read from global memory (the merged table fits in L2, or the plan is
+// Plain form: warps [0, K) copy one keep row each; every further warp gathers per_warp sources
+// (fewer on small plans, so the batches still fill the GPU), every parent read from global memory (the merged table fits in L2, or the plan is
 // too small for the staging below to pay).
-template <typename T, int kMaxCorners>
+template <typename T, int kMaxCorners, int kGatherQ>
 __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     proj_gather_kernel(const T* __restrict__ y, long long ys, const int64_t* __restrict__ keep,
                        long long K, const int64_t* __restrict__ src,
                        const int64_t* __restrict__ parent, const float* __restrict__ w,
                        long long S, int corners, T* __restrict__ out, long long os,
-                       long long N_out, int C) {
+                       long long N_out, int C, int per_warp) {
   static_assert(kMaxCorners == 4, "four corners at most");
   const long long wid = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -234,9 +234,10 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     gather_keep_row<T>(y, ys, keep, wid, out, os, N_out, C / Vec<T>::N, lane);
     return;
   }
-  const long long base = (wid - K) * 32;
+  const long long base = (wid - K) * per_warp;
   if (base >= S) return;
-  gather_sources<T, false>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, lane, nullptr, nullptr);
+  gather_sources<T, false, kGatherQ>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, per_warp, lane,
+                                     nullptr, nullptr);
 }
 
 // Skewed plans: the most-referenced merged rows (hot_rows, chosen once per plan by
@@ -245,6 +246,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
 // (the bound of the plain kernel on config 5: ~8 GB of L2 reads per restore).  One CTA of
 // kHotWarps warps per SM walks the keep rows, then the 32-source batches, in grid stride.
 constexpr int kHotWarps = 16;
+constexpr long long kGatherBatchMin = 1 << 17;  // sources from which the plain gather batches
 constexpr int kMaxHotRows = 128;
 constexpr long long kHotSmemBytes = 200 * 1024;  // shared memory for staged rows per CTA
 
@@ -274,7 +276,8 @@ __global__ void __launch_bounds__(kHotWarps * 32, 1)
   const long long nwarps = static_cast<long long>(gridDim.x) * kHotWarps;
   for (long long r = warp0; r < K; r += nwarps) gather_keep_row<T>(y, ys, keep, r, out, os, N_out, C / Vec<T>::N, lane);
   for (long long base = warp0 * 32; base < S; base += nwarps * 32)
-    gather_sources<T, true>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, lane, hot_slot, hot);
+    gather_sources<T, true, 4>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, 32, lane, hot_slot,
+                               hot);
 }
 
 // Hot-row selection (one block): row j's reference count is its CSR length; counts are bucketed
@@ -1384,10 +1387,27 @@ extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int
     VB200_CHECK_LAUNCH("zero_rows_kernel");
   }
   if (K + S == 0) return VB200_OK;
-#define VB200_GATHER(T)                                                                      \
-  proj_gather_kernel<T, 4><<<row_blocks(K + (S + 31) / 32), kWarpsPerBlock * 32, 0, st>>>(  \
-      static_cast<const T*>(y), ys, keep, K, src, parent, w, S, static_cast<int>(corners), \
-      static_cast<T*>(out), os, N_out, static_cast<int>(C))
+  // Large plans: batches of up to 32 sources per warp with whole rows in flight (one coalesced
+  // index load per batch; at least ~16 resident warps' worth of batches per SM).  Small plans:
+  // one source per warp, one vector per lane, twice the resident warps.
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool batched = S >= kGatherBatchMin;
+  const int per_warp =
+      batched ? static_cast<int>(std::max<long long>(1, std::min<long long>(32, S / (static_cast<long long>(sms) * 16))))
+              : 1;
+  const unsigned grid = row_blocks(K + (S + per_warp - 1) / per_warp);
+#define VB200_GATHER(T)                                                                                    \
+  do {                                                                                                     \
+    if (batched)                                                                                           \
+      proj_gather_kernel<T, 4, 4><<<grid, kWarpsPerBlock * 32, 0, st>>>(                                   \
+          static_cast<const T*>(y), ys, keep, K, src, parent, w, S, static_cast<int>(corners),             \
+          static_cast<T*>(out), os, N_out, static_cast<int>(C), per_warp);                                 \
+    else                                                                                                   \
+      proj_gather_kernel<T, 4, 1><<<grid, kWarpsPerBlock * 32, 0, st>>>(                                   \
+          static_cast<const T*>(y), ys, keep, K, src, parent, w, S, static_cast<int>(corners),             \
+          static_cast<T*>(out), os, N_out, static_cast<int>(C), per_warp);                                 \
+  } while (0)
   if (dtype == VB200_F32) VB200_GATHER(float);
   else if (dtype == VB200_BF16) VB200_GATHER(__nv_bfloat16);
   else VB200_GATHER(__half);
