@@ -52,6 +52,11 @@ _SIGNATURES = {
         [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
          _c_size, _c_vp],
     ),
+    "vb200_plan_csr_build_grouped": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp,
+         _c_vp, _c_vp],
+    ),
     "vb200_proj_scatter": (
         _c_int,
         [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,

@@ -1190,6 +1190,122 @@ __global__ void csr_mass_kernel(const int32_t* __restrict__ seg_offsets, const f
   }
 }
 
+// Grouped plans (every source's parents inside its own group of merged rows, as the
+// frame-group planners build them): one CTA per group builds the group's part of the CSR in
+// shared memory instead of the radix sort + scans of the general path.  Counts per segment
+// (shared-memory atomics, order-independent), a block-wide exclusive scan, placement of
+// (source, weight) pairs by per-segment cursors, then every segment's few entries are put in
+// ascending source order (insertion sort, one thread per segment) and the group's entries are
+// written out in order, so the result equals the general path's bit for bit.  Group g: sources
+// [q_begin[g], q_begin[g+1]), merged rows [b_begin[g], b_begin[g+1]); its entries fill
+// [q_begin[g], q_begin[g+1]) x corners of the entry arrays.  Masses follow in csr_mass_kernel.
+constexpr int kCsrGroupThreads = 512;
+constexpr int kCsrGroupMaxSegments = 16 * 1024;  // shared-memory counters per group
+constexpr int kCsrGroupMaxEntries = 20 * 1024;   // shared-memory (source, weight) pairs per group
+
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += n;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int t = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += n;
+    }
+    if (lane < nw) warp_tot[lane] = t;  // inclusive over warps
+  }
+  __syncthreads();
+  const int base = warp > 0 ? warp_tot[warp - 1] : 0;
+  return base + inc - v;
+}
+
+__global__ void __launch_bounds__(kCsrGroupThreads)
+    csr_grouped_kernel(const int64_t* __restrict__ parent, const float* __restrict__ weights,
+                       const int64_t* __restrict__ src_rows, int corners, long long M,
+                       const int64_t* __restrict__ q_begin, const int64_t* __restrict__ b_begin, int groups,
+                       int max_segments, int32_t* __restrict__ seg_offsets, int32_t* __restrict__ entry_src,
+                       float* __restrict__ entry_w) {
+  extern __shared__ __align__(16) int csr_smem[];
+  __shared__ int warp_tot[32];
+  int* cnt = csr_smem;                                     // [max_segments]: counts, then cursors
+  int* e_src = csr_smem + max_segments;                    // [entries]: source index in the group
+  float* e_w = reinterpret_cast<float*>(e_src + kCsrGroupMaxEntries);
+  const int g = blockIdx.x;
+  const long long q0 = q_begin[g], q1 = q_begin[g + 1], b0 = b_begin[g], b1 = b_begin[g + 1];
+  const int rows = static_cast<int>(b1 - b0);
+  const int nseg = rows * corners;
+  const int n = static_cast<int>((q1 - q0) * corners);
+  const long long e_base = q0 * corners;
+  if (nseg > max_segments || n > kCsrGroupMaxEntries || (nseg == 0 && n > 0)) {
+    if (threadIdx.x == 0) atomicOr(&g_proj_err, kErrBadArgument);  // host checks make this unreachable
+    return;
+  }
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    const long long p = parent[e_base + e] - b0;
+    if (p >= 0 && p < rows) atomicAdd(&cnt[p * corners + e % corners], 1);
+    else atomicOr(&g_proj_err, kErrBadArgument);
+  }
+  __syncthreads();
+  // exclusive scan: thread t scans a contiguous chunk of the counts
+  const int per = (nseg + blockDim.x - 1) / blockDim.x;
+  const int i0 = min(nseg, static_cast<int>(threadIdx.x) * per), i1 = min(nseg, i0 + per);
+  int local = 0;
+  for (int i = i0; i < i1; ++i) local += cnt[i];
+  int run = block_exclusive_scan(local, warp_tot);
+  for (int i = i0; i < i1; ++i) {
+    const int c = cnt[i];
+    cnt[i] = run;  // the segment's first entry (group-relative), the cursor below
+    seg_offsets[b0 * corners + i] = static_cast<int32_t>(e_base + run);
+    run += c;
+  }
+  __syncthreads();
+  // placement in shared memory (arbitrary order inside a segment for now)
+  for (int e = threadIdx.x; e < n; e += blockDim.x) {
+    const long long p = parent[e_base + e] - b0;
+    if (p < 0 || p >= rows) continue;
+    const int pos = atomicAdd(&cnt[static_cast<int>(p) * corners + e % corners], 1);
+    e_src[pos] = e / corners;
+    e_w[pos] = weights[e_base + e];
+  }
+  __syncthreads();
+  const int total = nseg > 0 ? cnt[nseg - 1] : 0;  // cursor of the last segment = entries placed
+  if (g == groups - 1 && threadIdx.x == 0)
+    for (long long j = b1 * corners; j <= M * corners; ++j) seg_offsets[j] = static_cast<int32_t>(e_base + total);
+  // ascending source order inside each segment (segments hold a few entries each)
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) {
+    const int a = i > 0 ? cnt[i - 1] : 0, b = cnt[i];
+    for (int x = a + 1; x < b; ++x) {
+      const int ks = e_src[x];
+      const float kw = e_w[x];
+      int y = x - 1;
+      while (y >= a && e_src[y] > ks) {
+        e_src[y + 1] = e_src[y];
+        e_w[y + 1] = e_w[y];
+        --y;
+      }
+      e_src[y + 1] = ks;
+      e_w[y + 1] = kw;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < total; e += blockDim.x) {
+    const long long s = q0 + e_src[e];
+    entry_src[e_base + e] = static_cast<int32_t>(src_rows ? src_rows[s] : s);
+    entry_w[e_base + e] = e_w[e];
+  }
+}
+
 // ------------------------------------------------------------------------------------------
 // row normalisation to bf16
 // ------------------------------------------------------------------------------------------
@@ -1634,6 +1750,39 @@ extern "C" int vb200_plan_csr_build(const int64_t* parent, const float* weights,
   if (M > 0 && (mass || log_mass)) {
     csr_mass_kernel<<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(
         seg_offsets, entry_w, M, static_cast<int>(corners), mass, log_mass);
+    VB200_CHECK_LAUNCH("csr_mass_kernel");
+  }
+  return VB200_OK;
+}
+
+extern "C" int vb200_plan_csr_build_grouped(const int64_t* parent, const float* weights, const int64_t* src_rows,
+                                            int64_t S, int64_t corners, int64_t M, const int64_t* q_begin,
+                                            const int64_t* b_begin, int groups, int max_group_rows,
+                                            int max_group_sources, int32_t* seg_offsets, int32_t* entry_src,
+                                            float* entry_w, float* mass, float* log_mass, void* stream) {
+  VB200_REQUIRE(S >= 0 && M >= 0 && corners >= 1 && corners <= 16 && groups >= 1, "plan_csr_build_grouped: bad sizes");
+  VB200_REQUIRE(S * corners < (1ll << 30) && M * corners < (1ll << 30),
+                "plan_csr_build_grouped: sizes exceed the int32 index range");
+  VB200_REQUIRE(max_group_rows >= 0 && static_cast<long long>(max_group_rows) * corners <= kCsrGroupMaxSegments &&
+                    max_group_sources >= 0 && static_cast<long long>(max_group_sources) * corners <= kCsrGroupMaxEntries,
+                "plan_csr_build_grouped: a group of %d rows / %d sources x %lld corners exceeds %d segments or %d "
+                "entries; use vb200_plan_csr_build",
+                max_group_rows, max_group_sources, (long long)corners, kCsrGroupMaxSegments, kCsrGroupMaxEntries);
+  VB200_REQUIRE(seg_offsets && q_begin && b_begin && (S == 0 || (parent && weights && entry_src && entry_w)),
+                "plan_csr_build_grouped: null pointer");
+  const int max_segments = static_cast<int>(std::max<long long>(1, static_cast<long long>(max_group_rows) * corners));
+  const size_t smem = static_cast<size_t>(max_segments) * 4 + static_cast<size_t>(kCsrGroupMaxEntries) * 8;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  VB200_CHECK_CUDA(cudaFuncSetAttribute(csr_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)),
+                   "cudaFuncSetAttribute");
+  csr_grouped_kernel<<<groups, kCsrGroupThreads, smem, st>>>(parent, weights, src_rows, static_cast<int>(corners), M,
+                                                               q_begin, b_begin, groups, max_segments, seg_offsets,
+                                                               entry_src, entry_w);
+  VB200_CHECK_LAUNCH("csr_grouped_kernel");
+  if (M > 0 && (mass || log_mass)) {
+    csr_mass_kernel<<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(seg_offsets, entry_w, M, static_cast<int>(corners),
+                                                                   mass, log_mass);
     VB200_CHECK_LAUNCH("csr_mass_kernel");
   }
   return VB200_OK;

@@ -225,9 +225,12 @@ class PlanCSR:
 
 
 def build_plan_csr(parent: torch.Tensor, weights: torch.Tensor, kept: int,
-                   src_rows: torch.Tensor | None = None) -> PlanCSR:
+                   src_rows: torch.Tensor | None = None, groups=None) -> PlanCSR:
     """Group (source, corner) pairs by compact parent; parent/weights are [S, corners]
-    (a leading batch dim of 1 is accepted)."""
+    (a leading batch dim of 1 is accepted).  ``groups`` = (q_begin, b_begin, max_rows): device
+    int64 group tables of a plan whose sources [q_begin[g], q_begin[g+1]) only take parents in
+    merged rows [b_begin[g], b_begin[g+1]); the CSR is then built in one launch
+    (``vb200_plan_csr_build_grouped``), with the same result."""
     C.require_cuda(parent, "build_plan_csr")
     if parent.ndim == 3:
         parent, weights = parent[0], weights[0]
@@ -245,14 +248,22 @@ def build_plan_csr(parent: torch.Tensor, weights: torch.Tensor, kept: int,
     mass = torch.empty(max(kept, 1), device=dev, dtype=torch.float32)
     log_mass = torch.empty(max(kept, 1), device=dev, dtype=torch.float32)
     lib = C.lib()
-    ws_bytes = lib.vb200_plan_csr_workspace_size(S, corners, kept)
-    ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
-    rc = lib.vb200_plan_csr_build(
-        parent.data_ptr(), weights.data_ptr(), C.ptr(src_rows), S, corners, kept, seg.data_ptr(),
-        esrc.data_ptr(), ew.data_ptr(), mass.data_ptr(), log_mass.data_ptr(), ws.data_ptr(), ws_bytes,
-        C.stream_of(dev),
-    )
-    C.check(rc, "build_plan_csr")
+    if groups is not None:
+        q_begin, b_begin, max_rows, max_sources = groups
+        rc = lib.vb200_plan_csr_build_grouped(
+            parent.data_ptr(), weights.data_ptr(), C.ptr(src_rows), S, corners, kept, q_begin.data_ptr(),
+            b_begin.data_ptr(), q_begin.numel() - 1, int(max_rows), int(max_sources), seg.data_ptr(),
+            esrc.data_ptr(), ew.data_ptr(), mass.data_ptr(), log_mass.data_ptr(), C.stream_of(dev))
+        C.check(rc, "build_plan_csr (grouped)")
+    else:
+        ws_bytes = lib.vb200_plan_csr_workspace_size(S, corners, kept)
+        ws = torch.empty(max(ws_bytes, 1), device=dev, dtype=torch.uint8)
+        rc = lib.vb200_plan_csr_build(
+            parent.data_ptr(), weights.data_ptr(), C.ptr(src_rows), S, corners, kept, seg.data_ptr(),
+            esrc.data_ptr(), ew.data_ptr(), mass.data_ptr(), log_mass.data_ptr(), ws.data_ptr(), ws_bytes,
+            C.stream_of(dev),
+        )
+        C.check(rc, "build_plan_csr")
     return PlanCSR(seg, esrc[: S * corners], ew[: S * corners], mass[:kept], log_mass[:kept], corners, kept)
 
 

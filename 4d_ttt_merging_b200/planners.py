@@ -176,7 +176,10 @@ def build_uniform_convex_plan(tokens: torch.Tensor, *, frames: int, tokens_per_f
                                    None, parent_rows.data_ptr(), S,
                                    feat.shape[1], None, None, alpha.data_ptr(), int(steps), C.stream_of(dev))
     C.check(rc, "support_fit")
-    csr = build_plan_csr(parent, alpha, K, src_rows=dl["source"])
+    grouped = dl["max_group_rows"] * 4 <= 16 * 1024 and dl["max_group_sources"] * 4 <= 20 * 1024
+    csr = build_plan_csr(parent, alpha, K, src_rows=dl["source"],
+                         groups=(dl["q_begin"], dl["b_begin"], dl["max_group_rows"], dl["max_group_sources"])
+                         if grouped else None)
     normalizer = csr.mass.view(1, K, 1)
     return WeightedBilinearTokenPlan(
         csr=csr,
@@ -196,8 +199,10 @@ def _device_layout(lay: dict, dev: torch.device) -> dict:
     key = (id(lay), str(dev))
     hit = _DEVICE_LAYOUTS.get(key)
     if hit is None:
-        hit = {k: lay[k].to(dev) for k in ("keep", "source", "special", "special_compact")}
+        hit = {k: lay[k].to(dev) for k in ("keep", "source", "special", "special_compact", "q_begin", "b_begin")}
         hit["source_keep"] = torch.cat([hit["source"], hit["keep"]])  # feature-row order of the planner
+        hit["max_group_rows"] = int((lay["b_begin"][1:] - lay["b_begin"][:-1]).max())
+        hit["max_group_sources"] = int((lay["q_begin"][1:] - lay["q_begin"][:-1]).max())
         _DEVICE_LAYOUTS[key] = hit
     return hit
 

@@ -134,6 +134,18 @@ VB200_API int vb200_plan_csr_build(const int64_t* parent, const float* weights, 
                          int64_t S, int64_t corners, int64_t M, int32_t* seg_offsets,
                          int32_t* entry_src, float* entry_w, float* mass, float* log_mass,
                          void* workspace, size_t workspace_bytes, void* stream);
+/* The same CSR, masses and log-masses for grouped plans, in one launch: group g's sources
+ * [q_begin[g], q_begin[g+1]) all have their parents among merged rows [b_begin[g], b_begin[g+1])
+ * (the frame-group planners; DEVICE int64 arrays of groups+1 entries, non-decreasing, ending at S
+ * and M).  One CTA per group builds its part in shared memory; max_group_rows / max_group_sources
+ * bound every group (rows x corners <= 16,384, sources x corners <= 20,480; larger groups:
+ * vb200_plan_csr_build).  A parent outside its group sets device error bit 1 and its entry is
+ * dropped.  Output identical to vb200_plan_csr_build.  Needs no workspace. */
+VB200_API int vb200_plan_csr_build_grouped(const int64_t* parent, const float* weights, const int64_t* src_rows,
+                                           int64_t S, int64_t corners, int64_t M, const int64_t* q_begin,
+                                           const int64_t* b_begin, int groups, int max_group_rows,
+                                           int max_group_sources, int32_t* seg_offsets, int32_t* entry_src,
+                                           float* entry_w, float* mass, float* log_mass, void* stream);
 
 /* ---- a4: top-4 scatter-accumulate (tokens -> merged) ----------------------------------------
  * out[j] = (x[keep[j]] + sum_c sum_{e in seg(j,c)} w_e * x[entry_src[e]]) / normalizer[j]

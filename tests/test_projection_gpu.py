@@ -197,3 +197,34 @@ def test_hot_row_gather_matches_plain(pkg, oracle, cuda_device, dtype, C, monkey
     assert torch.equal(plan.restore(yt[None])[0], plain)
     assert plan._hot is not None
     assert pkg.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("sizes", [[(3087, 1029)] * 3, [(500, 40), (0, 7), (1200, 300), (37, 5)]],
+                         ids=["frame_groups", "ragged"])
+def test_grouped_csr_equals_general(pkg, cuda_device, sizes):
+    """vb200_plan_csr_build_grouped (one CTA per group) against the general radix-sort build:
+    identical segment offsets, entries, masses and log-masses, for frame-group shapes and for
+    ragged groups (one without sources, skewed parents giving long segments)."""
+    rng = np.random.default_rng(len(sizes))
+    parents, weights, qb, bb = [], [], [0], [0]
+    for S_g, K_g in sizes:
+        if S_g:
+            pr = np.stack([rng.choice(K_g, 4, replace=False) for _ in range(S_g)])
+            if K_g > 100:  # skew: a third of the sources share two popular parents
+                pr[: S_g // 3, :2] = [0, 1]
+            parents.append(pr + bb[-1])
+            weights.append(rng.dirichlet(np.ones(4), size=S_g).astype(np.float32))
+        qb.append(qb[-1] + S_g)
+        bb.append(bb[-1] + K_g)
+    parent = torch.as_tensor(np.concatenate(parents), device=cuda_device)
+    w = torch.as_tensor(np.concatenate(weights), device=cuda_device)
+    S, M = qb[-1], bb[-1]
+    src_rows = torch.as_tensor(np.sort(rng.choice(4 * S, S, replace=False)), device=cuda_device)
+    ref = pkg.build_plan_csr(parent, w, M, src_rows=src_rows)
+    groups = (torch.as_tensor(qb, device=cuda_device), torch.as_tensor(bb, device=cuda_device),
+              max(k for _, k in sizes), max(q for q, _ in sizes))
+    got = pkg.build_plan_csr(parent, w, M, src_rows=src_rows, groups=groups)
+    torch.cuda.synchronize()
+    for name in ("seg_offsets", "entry_src", "entry_w", "mass", "log_mass"):
+        assert torch.equal(getattr(got, name), getattr(ref, name)), name
+    assert pkg.device_error_flags() == 0
