@@ -158,9 +158,22 @@ class GlobalAttention(nn.Module):
         own = {k: v for k, v in state.items() if k != "qkv.bias_mask"}
         self.load_state_dict({**own, "bias_mask": state.get("qkv.bias_mask", self.bias_mask)}, strict=True)
 
+    def _masked_qkv_bias(self):
+        """qkv bias with the key part zeroed (the reference's LinearKMaskedBias,
+        layers/attention.py:195-207), cached until either tensor is modified in place (torch's
+        version counters), so a step does not recompute it."""
+        b = self.qkv.bias
+        if b is None:
+            return None
+        key = (b.data_ptr(), b._version, self.bias_mask.data_ptr(), self.bias_mask._version, b.dtype)
+        cached = getattr(self, "_bias_cache", None)
+        if cached is None or cached[0] != key:
+            cached = (key, b * self.bias_mask.to(b.dtype))
+            self._bias_cache = cached
+        return cached[1]
+
     def qkv_projection(self, x: torch.Tensor) -> torch.Tensor:
-        bias = None if self.qkv.bias is None else self.qkv.bias * self.bias_mask.to(self.qkv.bias.dtype)
-        return F.linear(x, self.qkv.weight, bias)
+        return F.linear(x, self.qkv.weight, self._masked_qkv_bias())
 
     def forward(self, x: torch.Tensor, token_plan=None) -> torch.Tensor:
         qkv = (token_plan.precomputed_qkv

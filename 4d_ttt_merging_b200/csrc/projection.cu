@@ -1199,9 +1199,9 @@ __global__ void csr_mass_kernel(const int32_t* __restrict__ seg_offsets, const f
 // written out in order, so the result equals the general path's bit for bit.  Group g: sources
 // [q_begin[g], q_begin[g+1]), merged rows [b_begin[g], b_begin[g+1]); its entries fill
 // [q_begin[g], q_begin[g+1]) x corners of the entry arrays.  Masses follow in csr_mass_kernel.
-constexpr int kCsrGroupThreads = 512;
-constexpr int kCsrGroupMaxSegments = 16 * 1024;  // shared-memory counters per group
-constexpr int kCsrGroupMaxEntries = 20 * 1024;   // shared-memory (source, weight) pairs per group
+constexpr int kCsrGroupThreads = 1024;
+constexpr int kCsrGroupMaxSegments = 8 * 1024;    // shared-memory counters per group
+constexpr int kCsrGroupMaxEntries = 16 * 1024;    // shared-memory entries per group (12 bytes each)
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1232,30 +1232,41 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
     csr_grouped_kernel(const int64_t* __restrict__ parent, const float* __restrict__ weights,
                        const int64_t* __restrict__ src_rows, int corners, long long M,
                        const int64_t* __restrict__ q_begin, const int64_t* __restrict__ b_begin, int groups,
-                       int max_segments, int32_t* __restrict__ seg_offsets, int32_t* __restrict__ entry_src,
-                       float* __restrict__ entry_w) {
+                       int max_segments, int max_entries, int32_t* __restrict__ seg_offsets,
+                       int32_t* __restrict__ entry_src, float* __restrict__ entry_w) {
   extern __shared__ __align__(16) int csr_smem[];
   __shared__ int warp_tot[32];
-  int* cnt = csr_smem;                                     // [max_segments]: counts, then cursors
-  int* e_src = csr_smem + max_segments;                    // [entries]: source index in the group
-  float* e_w = reinterpret_cast<float*>(e_src + kCsrGroupMaxEntries);
+  // shared memory: counters [max_segments] | staged weights [max_entries] | placed weights
+  // [max_entries] | staged segment of each pair (int16 pairs) | placed source index (int16)
+  int* cnt = csr_smem;
+  float* w_in = reinterpret_cast<float*>(cnt + max_segments);
+  float* e_w = w_in + max_entries;
+  uint16_t* seg_in = reinterpret_cast<uint16_t*>(e_w + max_entries);
+  uint16_t* e_src = seg_in + max_entries;
   const int g = blockIdx.x;
   const long long q0 = q_begin[g], q1 = q_begin[g + 1], b0 = b_begin[g], b1 = b_begin[g + 1];
   const int rows = static_cast<int>(b1 - b0);
   const int nseg = rows * corners;
   const int n = static_cast<int>((q1 - q0) * corners);
   const long long e_base = q0 * corners;
-  if (nseg > max_segments || n > kCsrGroupMaxEntries || (nseg == 0 && n > 0)) {
-    if (threadIdx.x == 0) atomicOr(&g_proj_err, kErrBadArgument);  // host checks make this unreachable
+  if (nseg > max_segments || n > max_entries || (nseg == 0 && n > 0)) {
+    if (threadIdx.x == 0) atomicOr(&g_proj_err, kErrBadArgument);  // the host checks make this unreachable
     return;
   }
+  constexpr uint16_t kDropped = 0xffff;
   for (int i = threadIdx.x; i < nseg; i += blockDim.x) cnt[i] = 0;
-  __syncthreads();
+  // stage every pair's segment and weight: independent coalesced loads, several per thread in flight
+#pragma unroll 4
   for (int e = threadIdx.x; e < n; e += blockDim.x) {
     const long long p = parent[e_base + e] - b0;
-    if (p >= 0 && p < rows) atomicAdd(&cnt[p * corners + e % corners], 1);
-    else atomicOr(&g_proj_err, kErrBadArgument);
+    const bool ok = p >= 0 && p < rows;
+    if (!ok) atomicOr(&g_proj_err, kErrBadArgument);
+    seg_in[e] = ok ? static_cast<uint16_t>(p * corners + e % corners) : kDropped;
+    w_in[e] = weights[e_base + e];
   }
+  __syncthreads();
+  for (int e = threadIdx.x; e < n; e += blockDim.x)
+    if (seg_in[e] != kDropped) atomicAdd(&cnt[seg_in[e]], 1);
   __syncthreads();
   // exclusive scan: thread t scans a contiguous chunk of the counts
   const int per = (nseg + blockDim.x - 1) / blockDim.x;
@@ -1270,23 +1281,23 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
     run += c;
   }
   __syncthreads();
-  // placement in shared memory (arbitrary order inside a segment for now)
+  // placement (arbitrary order inside a segment for now)
   for (int e = threadIdx.x; e < n; e += blockDim.x) {
-    const long long p = parent[e_base + e] - b0;
-    if (p < 0 || p >= rows) continue;
-    const int pos = atomicAdd(&cnt[static_cast<int>(p) * corners + e % corners], 1);
-    e_src[pos] = e / corners;
-    e_w[pos] = weights[e_base + e];
+    const int sg = seg_in[e];
+    if (sg == kDropped) continue;
+    const int pos = atomicAdd(&cnt[sg], 1);
+    e_src[pos] = static_cast<uint16_t>(e / corners);
+    e_w[pos] = w_in[e];
   }
   __syncthreads();
-  const int total = nseg > 0 ? cnt[nseg - 1] : 0;  // cursor of the last segment = entries placed
+  const int total = cnt[nseg - 1];  // cursor of the last segment = pairs placed
   if (g == groups - 1 && threadIdx.x == 0)
     for (long long j = b1 * corners; j <= M * corners; ++j) seg_offsets[j] = static_cast<int32_t>(e_base + total);
   // ascending source order inside each segment (segments hold a few entries each)
   for (int i = threadIdx.x; i < nseg; i += blockDim.x) {
     const int a = i > 0 ? cnt[i - 1] : 0, b = cnt[i];
     for (int x = a + 1; x < b; ++x) {
-      const int ks = e_src[x];
+      const uint16_t ks = e_src[x];
       const float kw = e_w[x];
       int y = x - 1;
       while (y >= a && e_src[y] > ks) {
@@ -1299,6 +1310,7 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
     }
   }
   __syncthreads();
+#pragma unroll 4
   for (int e = threadIdx.x; e < total; e += blockDim.x) {
     const long long s = q0 + e_src[e];
     entry_src[e_base + e] = static_cast<int32_t>(src_rows ? src_rows[s] : s);
@@ -1771,14 +1783,15 @@ extern "C" int vb200_plan_csr_build_grouped(const int64_t* parent, const float* 
   VB200_REQUIRE(seg_offsets && q_begin && b_begin && (S == 0 || (parent && weights && entry_src && entry_w)),
                 "plan_csr_build_grouped: null pointer");
   const int max_segments = static_cast<int>(std::max<long long>(1, static_cast<long long>(max_group_rows) * corners));
-  const size_t smem = static_cast<size_t>(max_segments) * 4 + static_cast<size_t>(kCsrGroupMaxEntries) * 8;
+  const int max_entries = static_cast<int>(std::max<long long>(2, (static_cast<long long>(max_group_sources) * corners + 1) & ~1ll));
+  const size_t smem = static_cast<size_t>(max_segments) * 4 + static_cast<size_t>(max_entries) * 12;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   VB200_CHECK_CUDA(cudaFuncSetAttribute(csr_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)),
                    "cudaFuncSetAttribute");
   csr_grouped_kernel<<<groups, kCsrGroupThreads, smem, st>>>(parent, weights, src_rows, static_cast<int>(corners), M,
-                                                               q_begin, b_begin, groups, max_segments, seg_offsets,
-                                                               entry_src, entry_w);
+                                                               q_begin, b_begin, groups, max_segments, max_entries,
+                                                               seg_offsets, entry_src, entry_w);
   VB200_CHECK_LAUNCH("csr_grouped_kernel");
   if (M > 0 && (mass || log_mass)) {
     csr_mass_kernel<<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(seg_offsets, entry_w, M, static_cast<int>(corners),

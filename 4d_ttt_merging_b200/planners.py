@@ -176,7 +176,7 @@ def build_uniform_convex_plan(tokens: torch.Tensor, *, frames: int, tokens_per_f
                                    None, parent_rows.data_ptr(), S,
                                    feat.shape[1], None, None, alpha.data_ptr(), int(steps), C.stream_of(dev))
     C.check(rc, "support_fit")
-    grouped = dl["max_group_rows"] * 4 <= 16 * 1024 and dl["max_group_sources"] * 4 <= 20 * 1024
+    grouped = dl["max_group_rows"] * 4 <= 8 * 1024 and dl["max_group_sources"] * 4 <= 16 * 1024
     csr = build_plan_csr(parent, alpha, K, src_rows=dl["source"],
                          groups=(dl["q_begin"], dl["b_begin"], dl["max_group_rows"], dl["max_group_sources"])
                          if grouped else None)

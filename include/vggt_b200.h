@@ -138,7 +138,7 @@ VB200_API int vb200_plan_csr_build(const int64_t* parent, const float* weights, 
  * [q_begin[g], q_begin[g+1]) all have their parents among merged rows [b_begin[g], b_begin[g+1])
  * (the frame-group planners; DEVICE int64 arrays of groups+1 entries, non-decreasing, ending at S
  * and M).  One CTA per group builds its part in shared memory; max_group_rows / max_group_sources
- * bound every group (rows x corners <= 16,384, sources x corners <= 20,480; larger groups:
+ * bound every group (rows x corners <= 8,192, sources x corners <= 16,384; larger groups:
  * vb200_plan_csr_build).  A parent outside its group sets device error bit 1 and its entry is
  * dropped.  Output identical to vb200_plan_csr_build.  Needs no workspace. */
 VB200_API int vb200_plan_csr_build_grouped(const int64_t* parent, const float* weights, const int64_t* src_rows,
