@@ -1255,15 +1255,34 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
   }
   constexpr uint16_t kDropped = 0xffff;
   for (int i = threadIdx.x; i < nseg; i += blockDim.x) cnt[i] = 0;
-  // stage every pair's segment and weight: independent coalesced loads, several per thread in flight
-#pragma unroll 4
-  for (int e = threadIdx.x; e < n; e += blockDim.x) {
-    const long long p = parent[e_base + e] - b0;
-    const bool ok = p >= 0 && p < rows;
-    if (!ok) atomicOr(&g_proj_err, kErrBadArgument);
-    seg_in[e] = ok ? static_cast<uint16_t>(p * corners + e % corners) : kDropped;
-    w_in[e] = weights[e_base + e];
+  // stage every pair's segment and weight: four coalesced loads per thread in flight at a time,
+  // and one error report per thread (an atomic between the loads would serialise them)
+  bool bad = false;
+  const int stride = blockDim.x;
+  for (int e0 = threadIdx.x; e0 < n; e0 += 4 * stride) {
+    int64_t pv[4];
+    float wv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * stride;
+      if (e < n) {
+        pv[u] = parent[e_base + e];
+        wv[u] = weights[e_base + e];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * stride;
+      if (e < n) {
+        const long long p = pv[u] - b0;
+        const bool ok = p >= 0 && p < rows;
+        bad |= !ok;
+        seg_in[e] = ok ? static_cast<uint16_t>(p * corners + e % corners) : kDropped;
+        w_in[e] = wv[u];
+      }
+    }
   }
+  if (bad) atomicOr(&g_proj_err, kErrBadArgument);
   __syncthreads();
   for (int e = threadIdx.x; e < n; e += blockDim.x)
     if (seg_in[e] != kDropped) atomicAdd(&cnt[seg_in[e]], 1);
@@ -1310,11 +1329,24 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
     }
   }
   __syncthreads();
-#pragma unroll 4
-  for (int e = threadIdx.x; e < total; e += blockDim.x) {
-    const long long s = q0 + e_src[e];
-    entry_src[e_base + e] = static_cast<int32_t>(src_rows ? src_rows[s] : s);
-    entry_w[e_base + e] = e_w[e];
+  for (int e0 = threadIdx.x; e0 < total; e0 += 4 * stride) {
+    long long sv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * stride;
+      if (e < total) {
+        const long long s = q0 + e_src[e];
+        sv[u] = src_rows ? src_rows[s] : s;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * stride;
+      if (e < total) {
+        entry_src[e_base + e] = static_cast<int32_t>(sv[u]);
+        entry_w[e_base + e] = e_w[e];
+      }
+    }
   }
 }
 
