@@ -63,6 +63,14 @@ _SIGNATURES = {
          _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp],
     ),
     "vb200_proj_scatter_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
+    "vb200_proj_scatter_numerators": (
+        _c_int,
+        [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_size,
+         _c_vp],
+    ),
+    "vb200_rank_reduce_rows": (
+        _c_int, [_c_int, _c_vp, _c_int, _c_i64, _c_i64, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp],
+    ),
     "vb200_compact_qkv_workspace_size": (_c_size, [_c_i64, _c_i64]),
     "vb200_compact_qkv": (
         _c_int,

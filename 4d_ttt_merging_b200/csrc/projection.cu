@@ -230,11 +230,12 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
   static_assert(kMaxCorners == 4, "four corners at most");
   const long long wid = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (wid < K) {
+  const long long K_copy = keep != nullptr ? K : 0;  // no keep table: sources only (K bounds the parents)
+  if (wid < K_copy) {
     gather_keep_row<T>(y, ys, keep, wid, out, os, N_out, C / Vec<T>::N, lane);
     return;
   }
-  const long long base = (wid - K) * per_warp;
+  const long long base = (wid - K_copy) * per_warp;
   if (base >= S) return;
   gather_sources<T, false, kGatherQ>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, per_warp, lane,
                                      nullptr, nullptr);
@@ -274,7 +275,8 @@ __global__ void __launch_bounds__(kHotWarps * 32, 1)
   const int lane = threadIdx.x & 31;
   const long long warp0 = static_cast<long long>(blockIdx.x) * kHotWarps + (threadIdx.x >> 5);
   const long long nwarps = static_cast<long long>(gridDim.x) * kHotWarps;
-  for (long long r = warp0; r < K; r += nwarps) gather_keep_row<T>(y, ys, keep, r, out, os, N_out, C / Vec<T>::N, lane);
+  if (keep != nullptr)
+    for (long long r = warp0; r < K; r += nwarps) gather_keep_row<T>(y, ys, keep, r, out, os, N_out, C / Vec<T>::N, lane);
   for (long long base = warp0 * 32; base < S; base += nwarps * 32)
     gather_sources<T, true, 4>(y, ys, K, src, parent, w, S, corners, out, os, N_out, C, base, 32, lane, hot_slot,
                                hot);
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
                         const int32_t* __restrict__ entry_src, const float* __restrict__ entry_w,
                         const float* __restrict__ normalizer, T* __restrict__ out, long long os, int C,
                         const int32_t* __restrict__ chunk_base, float* __restrict__ partials,
-                        long long chunk_warps) {
+                        long long chunk_warps, float* __restrict__ numerators) {
   constexpr int V = Vec<T>::N;
   const long long w = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -552,7 +554,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
   const long long j = w - chunk_warps;
   if (j >= M) return;
   if (chunk_base != nullptr && chunk_base[j + 1] > chunk_base[j]) return;  // long row: finished later
-  const float norm = normalizer[j];
+  const float norm = numerators != nullptr ? 1.f : normalizer[j];
   const T* krow = nullptr;
   if (keep != nullptr) {
     const int64_t kr = keep[j];
@@ -563,7 +565,7 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
     }
   }
   const int32_t* seg = seg_offsets + j * corners;
-  T* drow = out + j * os;
+  T* drow = numerators != nullptr ? nullptr : out + j * os;
   // the row's accumulator lives in shared memory (each lane its own words), so the registers
   // hold only the in-flight source rows and the current corner's partial sums
   __shared__ uint64_t acc_s[kWarpsPerBlock][kScatterQ][V / 2][32];
@@ -600,6 +602,16 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32, 2)
     for (int q = 0; q < kScatterQ; ++q) {
       const int col = col0 + (lane + 32 * q) * V;
       if (col < C) {
+        if (numerators != nullptr) {  // partial numerator: the fp32 sum as it stands
+          float* nrow = numerators + j * C + col;
+#pragma unroll
+          for (int h = 0; h < V / 2; ++h) {
+            float a, b;
+            upk2(acc[q][h][lane], a, b);
+            *reinterpret_cast<float2*>(nrow + 2 * h) = make_float2(a, b);
+          }
+          continue;
+        }
         float o[V];
 #pragma unroll
         for (int h = 0; h < V / 2; ++h) {
@@ -621,12 +633,13 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     scatter_finish_kernel(const T* __restrict__ x, long long x_rows, long long xs, const int64_t* __restrict__ keep,
                           long long M, const float* __restrict__ normalizer, T* __restrict__ out, long long os,
                           int C, const int32_t* __restrict__ chunk_base, const float* __restrict__ partials,
-                          const int32_t* __restrict__ group_base, const float* __restrict__ partials1) {
+                          const int32_t* __restrict__ group_base, const float* __restrict__ partials1,
+                          float* __restrict__ numerators) {
   constexpr int V = Vec<T>::N;
   const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (j >= M || chunk_base[j + 1] == chunk_base[j]) return;
-  const float norm = normalizer[j];
+  const float norm = numerators != nullptr ? 1.f : normalizer[j];
   const T* krow = nullptr;
   if (keep != nullptr) {
     const int64_t kr = keep[j];
@@ -650,10 +663,60 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
       for (int e = 0; e < V; ++e) acc[e] = kv[e];
     }
     sum_partials<4>(src, k0, k1, C, col, acc, V);
+    if (numerators != nullptr) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) numerators[j * C + col + e] = acc[e];
+      continue;
+    }
     float o[V];
 #pragma unroll
     for (int e = 0; e < V; ++e) o[e] = __fdiv_rn(acc[e], norm);
     store_vec<T>(drow + col, o);
+  }
+}
+
+// Rank-ordered reduction of partial numerators (the sharded scatter): out[j] = (x[keep[j]] +
+// sum over r = 0..R-1, in rank order, of partials[r][j]) / normalizer[j], fp32 sums rounded to T
+// once.  partials [R, rows, C] fp32 (what an all-to-all delivered, rank r's slice at r);
+// keep[j] < 0: no keep row.  One warp per row, 16-byte vectors.
+template <typename T>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+    rank_reduce_rows_kernel(const float* __restrict__ partials, int R, long long rows, int C,
+                            const T* __restrict__ x, long long x_rows, long long xs, const int64_t* __restrict__ keep,
+                            const float* __restrict__ normalizer, T* __restrict__ out, long long os) {
+  constexpr int V = Vec<T>::N;
+  const long long j = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= rows) return;
+  const T* krow = nullptr;
+  if (keep != nullptr && keep[j] >= 0) {
+    if (keep[j] < x_rows) krow = x + keep[j] * xs;
+    else if (lane == 0) atomicOr(&g_proj_err, kErrBadArgument);
+  }
+  const float norm = normalizer[j];
+  for (int col = lane * V; col < C; col += 32 * V) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (krow != nullptr) {
+      float kv[V];
+      load_vec<T>(krow + col, kv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) acc[e] = kv[e];
+    }
+    for (int r = 0; r < R; ++r) {
+      const float* pr = partials + (static_cast<long long>(r) * rows + j) * C + col;
+      const float4 a = *reinterpret_cast<const float4*>(pr);
+      acc[0] = __fadd_rn(acc[0], a.x); acc[1] = __fadd_rn(acc[1], a.y);
+      acc[2] = __fadd_rn(acc[2], a.z); acc[3] = __fadd_rn(acc[3], a.w);
+      if (V == 8) {
+        const float4 b = *reinterpret_cast<const float4*>(pr + 4);
+        acc[4] = __fadd_rn(acc[4], b.x); acc[5] = __fadd_rn(acc[5], b.y);
+        acc[6] = __fadd_rn(acc[6], b.z); acc[7] = __fadd_rn(acc[7], b.w);
+      }
+    }
+    float o[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) o[e] = __fdiv_rn(acc[e], norm);
+    store_vec<T>(out + j * os + col, o);
   }
 }
 
@@ -1530,8 +1593,7 @@ extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int
   VB200_REQUIRE(corners >= 1 && corners <= 4, "proj_gather: corners must be in [1, 4] (got %lld)",
                 (long long)corners);
   if (C == 0 || N_out == 0) return VB200_OK;
-  VB200_REQUIRE(out != nullptr && (K == 0 || (y && keep)) && (S == 0 || (src && parent && w)),
-                "proj_gather: null pointer");
+  VB200_REQUIRE(out != nullptr && (K == 0 || y) && (S == 0 || (src && parent && w)), "proj_gather: null pointer");
   VB200_REQUIRE(S == 0 || K > 0, "proj_gather: sources need at least one compact row to read");
   int rc;
   if (K > 0 && (rc = check_rows(dtype, y, ys, C, "proj_gather input")) != VB200_OK) return rc;
@@ -1556,7 +1618,7 @@ extern "C" int vb200_proj_gather(int dtype, const void* y, int64_t ys, const int
   const int per_warp =
       batched ? static_cast<int>(std::max<long long>(1, std::min<long long>(32, S / (static_cast<long long>(sms) * 16))))
               : 1;
-  const unsigned grid = row_blocks(K + (S + per_warp - 1) / per_warp);
+  const unsigned grid = row_blocks((keep != nullptr ? K : 0) + (S + per_warp - 1) / per_warp);
 #define VB200_GATHER(T)                                                                                    \
   do {                                                                                                     \
     if (batched)                                                                                           \
@@ -1604,8 +1666,7 @@ extern "C" int vb200_proj_gather_hot(int dtype, const void* y, int64_t ys, const
   VB200_REQUIRE(corners >= 1 && corners <= 4, "proj_gather_hot: corners must be in [1, 4] (got %lld)",
                 (long long)corners);
   if (C == 0 || N_out == 0 || K + S == 0) return VB200_OK;
-  VB200_REQUIRE(out != nullptr && (K == 0 || (y && keep)) && (S == 0 || (src && parent && w)),
-                "proj_gather_hot: null pointer");
+  VB200_REQUIRE(out != nullptr && (K == 0 || y) && (S == 0 || (src && parent && w)), "proj_gather_hot: null pointer");
   VB200_REQUIRE(hot_slot && n_hot && hot_rows, "proj_gather_hot: null hot-row table");
   VB200_REQUIRE(S == 0 || K > 0, "proj_gather_hot: sources need at least one compact row to read");
   const int cap = vb200_proj_gather_hot_capacity(dtype, C);
@@ -1674,21 +1735,27 @@ extern "C" size_t vb200_proj_scatter_workspace_size(int64_t M, int64_t n_entries
   return scatter_layout(M, n_entries, C).total;
 }
 
-extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64_t xs, const int64_t* keep,
-                                  int64_t M, int64_t corners, const int32_t* seg_offsets,
-                                  const int32_t* entry_src, const float* entry_w,
-                                  const float* normalizer, void* out, int64_t os, int64_t C,
-                                  int64_t n_entries, void* workspace, size_t workspace_bytes, void* stream) {
+namespace vb200 {
+namespace {
+// Both scatter forms: out = (keep + sums) / normalizer, or (numerators != NULL, keep and
+// normalizer unused) the fp32 sums alone in numerators [M, C].
+int scatter_launch(int dtype, const void* x, int64_t x_rows, int64_t xs, const int64_t* keep, int64_t M,
+                   int64_t corners, const int32_t* seg_offsets, const int32_t* entry_src, const float* entry_w,
+                   const float* normalizer, void* out, int64_t os, int64_t C, int64_t n_entries, void* workspace,
+                   size_t workspace_bytes, float* numerators, void* stream) {
   VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "proj_scatter: bad dtype %d", dtype);
   VB200_REQUIRE(M >= 0 && C >= 0 && corners >= 1 && n_entries >= 0, "proj_scatter: bad sizes");
   if (M == 0 || C == 0) return VB200_OK;
-  VB200_REQUIRE(x && out && seg_offsets && normalizer && x_rows > 0, "proj_scatter: null pointer or empty input");
+  VB200_REQUIRE(x && seg_offsets && x_rows > 0 && (numerators != nullptr || (out && normalizer)),
+                "proj_scatter: null pointer or empty input");
   const ScatterWorkspace lay = scatter_layout(M, n_entries, C);
   VB200_REQUIRE(workspace != nullptr && workspace_bytes >= lay.total,
                 "proj_scatter: workspace of %zu bytes required (got %zu)", lay.total, workspace_bytes);
   int rc;
   if ((rc = check_rows(dtype, x, xs, C, "proj_scatter input")) != VB200_OK) return rc;
-  if ((rc = check_rows(dtype, out, os, C, "proj_scatter output")) != VB200_OK) return rc;
+  if (numerators == nullptr && (rc = check_rows(dtype, out, os, C, "proj_scatter output")) != VB200_OK) return rc;
+  VB200_REQUIRE(numerators == nullptr || (reinterpret_cast<uintptr_t>(numerators) & 15u) == 0,
+                "proj_scatter: numerators must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* nchunk = reinterpret_cast<int32_t*>(ws + lay.nchunk);
@@ -1713,7 +1780,7 @@ extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int6
 #define VB200_WORK(T)                                                                                    \
   scatter_work_kernel<T><<<row_blocks(chunk_warps + M), kWarpsPerBlock * 32, 0, st>>>(                    \
       static_cast<const T*>(x), x_rows, xs, keep, M, static_cast<int>(corners), seg_offsets, entry_src, entry_w, \
-      normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials, chunk_warps)
+      normalizer, static_cast<T*>(out), os, static_cast<int>(C), chunk_base, partials, chunk_warps, numerators)
   if (dtype == VB200_F32) VB200_WORK(float);
   else if (dtype == VB200_BF16) VB200_WORK(__nv_bfloat16);
   else VB200_WORK(__half);
@@ -1732,12 +1799,61 @@ extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int6
 #define VB200_FINISH(T)                                                                            \
   scatter_finish_kernel<T><<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(                          \
       static_cast<const T*>(x), x_rows, xs, keep, M, normalizer, static_cast<T*>(out), os, static_cast<int>(C), \
-      chunk_base, partials, group_base, partials1)
+      chunk_base, partials, group_base, partials1, numerators)
   if (dtype == VB200_F32) VB200_FINISH(float);
   else if (dtype == VB200_BF16) VB200_FINISH(__nv_bfloat16);
   else VB200_FINISH(__half);
 #undef VB200_FINISH
   VB200_CHECK_LAUNCH("scatter_finish_kernel");
+  return VB200_OK;
+}
+
+}  // namespace
+}  // namespace vb200
+
+extern "C" int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64_t xs, const int64_t* keep,
+                                  int64_t M, int64_t corners, const int32_t* seg_offsets,
+                                  const int32_t* entry_src, const float* entry_w,
+                                  const float* normalizer, void* out, int64_t os, int64_t C,
+                                  int64_t n_entries, void* workspace, size_t workspace_bytes, void* stream) {
+  VB200_REQUIRE(out && normalizer, "proj_scatter: null pointer");
+  return scatter_launch(dtype, x, x_rows, xs, keep, M, corners, seg_offsets, entry_src, entry_w, normalizer, out, os,
+                        C, n_entries, workspace, workspace_bytes, nullptr, stream);
+}
+
+extern "C" int vb200_proj_scatter_numerators(int dtype, const void* x, int64_t x_rows, int64_t xs, int64_t M,
+                                             int64_t corners, const int32_t* seg_offsets, const int32_t* entry_src,
+                                             const float* entry_w, float* numerators, int64_t C, int64_t n_entries,
+                                             void* workspace, size_t workspace_bytes, void* stream) {
+  VB200_REQUIRE(numerators != nullptr, "proj_scatter_numerators: null pointer");
+  return scatter_launch(dtype, x, x_rows, xs, nullptr, M, corners, seg_offsets, entry_src, entry_w, nullptr, nullptr,
+                        0, C, n_entries, workspace, workspace_bytes, numerators, stream);
+}
+
+extern "C" int vb200_rank_reduce_rows(int dtype, const float* partials, int R, int64_t rows, int64_t C, const void* x,
+                                      int64_t x_rows, int64_t xs, const int64_t* keep, const float* normalizer,
+                                      void* out, int64_t os, void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "rank_reduce_rows: bad dtype %d",
+                dtype);
+  VB200_REQUIRE(R >= 1 && rows >= 0 && C >= 0, "rank_reduce_rows: bad sizes");
+  if (rows == 0 || C == 0) return VB200_OK;
+  VB200_REQUIRE(partials && normalizer && out && (keep == nullptr || (x && x_rows > 0)),
+                "rank_reduce_rows: null pointer");
+  VB200_REQUIRE(C % 8 == 0 && (reinterpret_cast<uintptr_t>(partials) & 15u) == 0,
+                "rank_reduce_rows: C must be a multiple of 8 and partials 16-byte aligned");
+  int rc;
+  if (keep != nullptr && (rc = check_rows(dtype, x, xs, C, "rank_reduce_rows input")) != VB200_OK) return rc;
+  if ((rc = check_rows(dtype, out, os, C, "rank_reduce_rows output")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_RR(T)                                                                                         \
+  rank_reduce_rows_kernel<T><<<row_blocks(rows), kWarpsPerBlock * 32, 0, st>>>(                              \
+      partials, R, rows, static_cast<int>(C), static_cast<const T*>(x), x_rows, xs, keep, normalizer,        \
+      static_cast<T*>(out), os)
+  if (dtype == VB200_F32) VB200_RR(float);
+  else if (dtype == VB200_BF16) VB200_RR(__nv_bfloat16);
+  else VB200_RR(__half);
+#undef VB200_RR
+  VB200_CHECK_LAUNCH("rank_reduce_rows_kernel");
   return VB200_OK;
 }
 

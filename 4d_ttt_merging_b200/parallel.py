@@ -26,7 +26,8 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-__all__ = ["FrameShard", "frame_shard", "gather_merged", "agree_all", "PeerExchange", "ShardedGlobalBlock", "StepGraph"]
+__all__ = ["FrameShard", "frame_shard", "gather_merged", "agree_all", "PeerExchange", "ShardedGlobalBlock", "StepGraph",
+           "shard_projection_plan", "ShardedProjection"]
 
 
 @dataclass(frozen=True)
@@ -374,3 +375,130 @@ class StepGraph:
         """Drop the graph (do this before destroying the process group)."""
         self.graph = None
         self.out = None
+
+
+def shard_projection_plan(keep: torch.Tensor, source: torch.Tensor, parent: torch.Tensor, weights: torch.Tensor,
+                          N: int, world: int, rank: int) -> dict:
+    """This rank's share of a one-GPU projection plan over N tokens: tokens [t0, t1) with
+    t_r = r * N // world, the merged rows whose keep token lies there ([m0, m1)) and the sources
+    that lie there ([s0, s1)); keep and source must be ascending original token ids (as the
+    reference's plans are).  Returns the bounds, every rank's owned merged-row count, and the
+    local keep / source ids (relative to t0) with the sources' GLOBAL parents and weights."""
+    keep = keep.reshape(-1)
+    source = source.reshape(-1)
+    parent = parent.reshape(source.numel(), -1)
+    weights = weights.reshape(source.numel(), -1)
+    cuts = torch.tensor([r * N // world for r in range(world + 1)], dtype=keep.dtype, device=keep.device)
+    mcut = torch.searchsorted(keep, cuts).tolist()
+    scut = torch.searchsorted(source, cuts).tolist()
+    t0, t1 = rank * N // world, (rank + 1) * N // world
+    m0, m1, s0, s1 = mcut[rank], mcut[rank + 1], scut[rank], scut[rank + 1]
+    return dict(t0=t0, t1=t1, m0=m0, m1=m1, s0=s0, s1=s1,
+                owned_counts=[mcut[r + 1] - mcut[r] for r in range(world)],
+                keep_local=(keep[m0:m1] - t0).contiguous(), source_local=(source[s0:s1] - t0).contiguous(),
+                parent_local=parent[s0:s1].to(torch.int64).contiguous(),
+                weights_local=weights[s0:s1].to(torch.float32).contiguous())
+
+
+class ShardedProjection:
+    """The top-4 projection of one large plan (config 5: a million tokens whose sources take
+    parents anywhere among the merged rows) sharded by query rows over the ranks of `group`.
+
+    Rank r holds tokens [r N / R, (r + 1) N / R) and owns the merged rows whose keep token lies
+    there.  ``compact`` runs the deterministic scatter over the rank's own sources into fp32
+    partial numerators of ALL merged rows (vb200_proj_scatter_numerators), sends each owner its
+    rows with one NCCL all_to_all_single (data only; the partial sums are exact fp32 values of a
+    fixed order), and the owner adds its keep row and the ranks' partials in rank order and
+    divides by the global mass (vb200_rank_reduce_rows): the result does not depend on timing
+    and equals the one-GPU compact up to the fp32 summation order of each merged row (the
+    one-GPU kernel sums a row's entries in source order in one chain; here per rank, then
+    across ranks).  ``restore`` all-gathers the merged rows (rank order = compact order) and
+    runs the gather for the rank's own tokens.  ``normalizer`` is the global mass [M] (from the
+    whole plan).  Reference: the one-GPU compact / restore of token_merging.py:343-370,
+    :285-341; the reference has no multi-GPU form of them."""
+
+    def __init__(self, keep: torch.Tensor, source: torch.Tensor, parent: torch.Tensor, weights: torch.Tensor,
+                 normalizer: torch.Tensor, N: int, group=None):
+        from .ops import build_plan_csr
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        sh = shard_projection_plan(keep, source, parent, weights, N, self.world, self.rank)
+        self.__dict__.update(sh)
+        self.M = keep.numel()
+        self.tokens = self.t1 - self.t0
+        self.normalizer = normalizer.reshape(-1)[self.m0:self.m1].to(torch.float32).contiguous()
+        self.csr = build_plan_csr(self.parent_local, self.weights_local, self.M, src_rows=self.source_local)
+        self._hot = None
+
+    def compact(self, x_local: torch.Tensor) -> torch.Tensor:
+        """x_local [tokens, C] (this rank's token rows) -> the owned merged rows [m1 - m0, C]."""
+        from . import _clib as C
+        C.require_cuda(x_local, "ShardedProjection.compact")
+        if x_local.ndim != 2 or x_local.shape[0] != self.tokens or x_local.stride(-1) != 1:
+            raise ValueError(f"x_local must be [{self.tokens}, C] with unit channel stride")
+        Cd, dev = x_local.shape[1], x_local.device
+        lib, stream = C.lib(), C.stream_of(dev)
+        numer = torch.empty((self.M, Cd), device=dev, dtype=torch.float32)
+        n_entries = self.csr.entry_src.numel()
+        ws_bytes = lib.vb200_proj_scatter_workspace_size(self.M, n_entries, Cd)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+        rc = lib.vb200_proj_scatter_numerators(
+            C.dtype_code(x_local.dtype), x_local.data_ptr(), x_local.shape[0], x_local.stride(0), self.M,
+            self.csr.corners, self.csr.seg_offsets.data_ptr(), self.csr.entry_src.data_ptr(),
+            self.csr.entry_w.data_ptr(), numer.data_ptr(), Cd, n_entries, ws.data_ptr(), ws_bytes, stream)
+        C.check(rc, "proj_scatter_numerators")
+        owned = self.m1 - self.m0
+        if self.world > 1:
+            recv = torch.empty((self.world * owned, Cd), device=dev, dtype=torch.float32)
+            dist.all_to_all_single(recv, numer, output_split_sizes=[owned] * self.world,
+                                   input_split_sizes=self.owned_counts, group=self.group)
+        else:
+            recv = numer
+        out = torch.empty((owned, Cd), device=dev, dtype=x_local.dtype)
+        rc = lib.vb200_rank_reduce_rows(
+            C.dtype_code(x_local.dtype), recv.data_ptr(), self.world, owned, Cd, x_local.data_ptr(),
+            x_local.shape[0], x_local.stride(0), self.keep_local.data_ptr(), self.normalizer.data_ptr(),
+            out.data_ptr(), out.stride(0), stream)
+        C.check(rc, "rank_reduce_rows")
+        return out
+
+    def restore(self, y_owned: torch.Tensor) -> torch.Tensor:
+        """y_owned [m1 - m0, C] (this rank's merged rows) -> this rank's token rows [tokens, C]."""
+        from . import _clib as C
+        from .token_plan import HOT_GATHER_MIN_REFERENCES
+        C.require_cuda(y_owned, "ShardedProjection.restore")
+        if len(set(self.owned_counts)) != 1:
+            raise ValueError("restore needs the same number of merged rows on every rank")
+        y_owned = y_owned.contiguous()
+        (full,) = gather_merged([y_owned], self.group) if self.world > 1 else (y_owned,)
+        Cd, dev = y_owned.shape[1], y_owned.device
+        lib, stream = C.lib(), C.stream_of(dev)
+        code = C.dtype_code(y_owned.dtype)
+        out = torch.empty((self.tokens, Cd), device=dev, dtype=y_owned.dtype)
+        S, corners = self.parent_local.shape
+        if self.keep_local.numel() + S != self.tokens:
+            out.zero_()
+        # the rank's own kept tokens: straight copies of its merged rows
+        rc = lib.vb200_proj_gather(code, full[self.m0:self.m1].data_ptr(), Cd, self.keep_local.data_ptr(),
+                                   self.keep_local.numel(), None, None, None, 0, corners, out.data_ptr(), Cd,
+                                   self.tokens, Cd, 0, stream)
+        C.check(rc, "proj_gather (keep rows)")
+        if S == 0:
+            return out
+        # its sources: weighted sums of merged rows of every rank
+        args = (code, full.data_ptr(), Cd, None, self.M, self.source_local.data_ptr(), self.parent_local.data_ptr(),
+                self.weights_local.data_ptr(), S, corners, out.data_ptr(), Cd, self.tokens, Cd)
+        if self.parent_local.numel() >= HOT_GATHER_MIN_REFERENCES:
+            if self._hot is None or self._hot[0] != (Cd, y_owned.dtype):
+                from .ops import plan_hot_rows
+                cap = lib.vb200_proj_gather_hot_capacity(code, Cd)
+                self._hot = ((Cd, y_owned.dtype), plan_hot_rows(self.csr, cap))
+            hot_rows, hot_slot, n_hot, max_hot = self._hot[1]
+            rc = lib.vb200_proj_gather_hot(*args, hot_rows.data_ptr(), hot_slot.data_ptr(), n_hot.data_ptr(), max_hot,
+                                           stream)
+            C.check(rc, "proj_gather_hot (sources)")
+        else:
+            rc = lib.vb200_proj_gather(*args, 0, stream)
+            C.check(rc, "proj_gather (sources)")
+        return out

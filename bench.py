@@ -214,16 +214,13 @@ def cpu_baseline(repeats: int = 2) -> dict:
             "sample": _reference_sample(repeats, 1, threads, t) + " (median)"}
 
 
-def projection_stress(pkg, dev, hbm_peak: float, N: int = 1 << 20, reps: int = 5) -> dict:
-    """Config 5 (top-4 projection bandwidth stress) on one GPU: N = 1,048,576 tokens,
-    M = 65,536 evenly spaced merged tokens, D = 1024 bf16.  Each source draws four distinct
-    parents Zipf(1.1) over the merged tokens (ranks mapped to ids by a seeded permutation), with
-    Dirichlet(1,1,1,1) weights; sampled on the GPU.  Times the scatter (tokens -> merged,
-    `plan.compact`) and the gather (merged -> tokens, `plan.restore`) with CUDA events; GB/s
-    counts compulsory HBM bytes (every token row and merged row once, plus the plan arrays).
-    ``N`` scales the case down for profiling (M = N / 16, same distributions)."""
+def _config5_plan(pkg, dev, N: int):
+    """Config 5's plan on the device (same seed on every rank, so every rank holds the same
+    plan): keep = M = N / 16 evenly spaced tokens, sources = the rest, four distinct parents per
+    source drawn Zipf(1.1) over the merged tokens (ranks mapped to ids by a seeded permutation),
+    Dirichlet(1,1,1,1) weights, and the masses of that plan -> (keep, src, parent, w, norm, gen)."""
     import torch
-    M, D, corners = N // 16, 1024, 4
+    M, corners = N // 16, 4
     g = torch.Generator(device=dev).manual_seed(5)
     keep = torch.arange(M, device=dev, dtype=torch.long) * (N // M)
     mask = torch.ones(N, dtype=torch.bool, device=dev)
@@ -247,31 +244,52 @@ def projection_stress(pkg, dev, hbm_peak: float, N: int = 1 << 20, reps: int = 5
     e = -torch.rand(S, corners, device=dev, generator=g).clamp_min(1e-12).log()
     w = (e / e.sum(1, keepdim=True)).float()
     norm = pkg.deterministic_weighted_normalizer(parent[None], w[None], M)
+    return keep, src, parent, w, norm, g
+
+
+def _compulsory_bytes(N: int, M: int, S: int, D: int, corners: int = 4) -> tuple[int, int]:
+    """Compulsory HBM bytes of config 5's (scatter, gather): every token row and merged row once
+    (bf16), plus the plan arrays each kernel reads (scatter: CSR int32 source + fp32 weight per
+    entry, mass and offsets per merged row; gather: int64 source and parents + fp32 weights per
+    source, the keep table)."""
+    meta = S * corners * (4 + 4) + M * 4 * 2
+    return N * D * 2 + M * D * 2 + meta, M * D * 2 + N * D * 2 + S * corners * (8 + 8 + 4) + M * 8
+
+
+def _median_ms(fn, reps: int) -> float:
+    import torch
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    return statistics.median(ms)
+
+
+def projection_stress(pkg, dev, hbm_peak: float, N: int = 1 << 20, reps: int = 5) -> dict:
+    """Config 5 (top-4 projection bandwidth stress) on one GPU: N = 1,048,576 tokens,
+    M = 65,536 merged tokens, D = 1024 bf16 (plan: _config5_plan, sampled on the GPU).  Times
+    the scatter (tokens -> merged, `plan.compact`) and the gather (merged -> tokens,
+    `plan.restore`) with CUDA events; GB/s counts compulsory HBM bytes (_compulsory_bytes).
+    ``N`` scales the case down for profiling (M = N / 16, same distributions)."""
+    import torch
+    M, D = N // 16, 1024
+    keep, src, parent, w, norm, g = _config5_plan(pkg, dev, N)
+    S = src.numel()
     plan = pkg.WeightedBilinearTokenPlan(
         keep=keep[None], source_original=src[None], source_parent_compact=parent[None], source_pool_weights=w[None],
         source_restore_weights=w[None], original_tokens=N, normalizer=norm, key_log_mass=norm[..., 0].log())
     x = torch.randn(1, N, D, device=dev, generator=g).to(torch.bfloat16)
     y = torch.randn(1, M, D, device=dev, generator=g).to(torch.bfloat16)
-
-    def timed(fn, reps=5):
-        for _ in range(2):
-            fn()
-        torch.cuda.synchronize()
-        ms = []
-        for _ in range(reps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            torch.cuda.synchronize()
-            ms.append(e0.elapsed_time(e1))
-        return statistics.median(ms)
-
-    scatter_ms = timed(lambda: plan.compact(x), reps)
-    gather_ms = timed(lambda: plan.restore(y), reps)
-    meta = S * corners * (4 + 4) + M * 4 * 2
-    scatter_bytes = N * D * 2 + M * D * 2 + meta
-    gather_bytes = M * D * 2 + N * D * 2 + S * corners * (8 + 8 + 4) + M * 8
+    scatter_ms = _median_ms(lambda: plan.compact(x), reps)
+    gather_ms = _median_ms(lambda: plan.restore(y), reps)
+    scatter_bytes, gather_bytes = _compulsory_bytes(N, M, S, D)
     sgbs = scatter_bytes / (scatter_ms / 1e3) / 1e9
     ggbs = gather_bytes / (gather_ms / 1e3) / 1e9
     del x, y, plan
@@ -280,6 +298,53 @@ def projection_stress(pkg, dev, hbm_peak: float, N: int = 1 << 20, reps: int = 5
             "scatter_ms": scatter_ms, "scatter_gbs": sgbs, "scatter_frac": sgbs / hbm_peak,
             "gather_ms": gather_ms, "gather_gbs": ggbs, "gather_frac": ggbs / hbm_peak,
             "peak_gbs": hbm_peak}
+
+
+def projection_sharded(pkg, dev, world: int, rank: int, local_rank: int, hbm_peak: float, N: int = 1 << 20,
+                       reps: int = 5) -> dict:
+    """Config 5 query-sharded over the ranks (parallel.ShardedProjection): each rank holds
+    N / world tokens and the merged rows whose keep token is among them; compact = scatter of
+    its sources into fp32 partial numerators of all merged rows + NCCL all-to-all + rank-ordered
+    reduction by the owners; restore = NCCL all-gather of the merged rows + gather of the
+    rank's tokens.  Each phase timed with CUDA events after a barrier, median of ``reps``,
+    max over ranks.  GB/s: the one-GPU compulsory bytes of the whole job / that time."""
+    import torch
+    import torch.distributed as dist
+    M, D = N // 16, 1024
+    keep, src, parent, w, norm, _ = _config5_plan(pkg, dev, N)
+    S = src.numel()
+    proj = pkg.parallel.ShardedProjection(keep, src, parent, w, norm[0, :, 0], N)
+    del keep, src, parent, w
+    gen = torch.Generator(device=dev).manual_seed(50 + rank)
+    x = torch.randn(proj.tokens, D, device=dev, generator=gen).to(torch.bfloat16)
+    y = torch.randn(proj.m1 - proj.m0, D, device=dev, generator=gen).to(torch.bfloat16)
+
+    def phase(fn):
+        times = []
+        for i in range(reps + 2):
+            dist.barrier(device_ids=[local_rank])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= 2:
+                times.append(e0.elapsed_time(e1))
+        t = torch.tensor([statistics.median(times)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    scatter_ms = phase(lambda: proj.compact(x))
+    gather_ms = phase(lambda: proj.restore(y))
+    scatter_bytes, gather_bytes = _compulsory_bytes(N, M, S, D)
+    del x, y, proj
+    return {"workload": f"config 5: N={N:,} tokens, M={M:,} merged, D=1024 bf16, query rows sharded x{world} "
+                        "(scatter to fp32 partial numerators + all-to-all + rank-ordered reduction; "
+                        "all-gather + gather)",
+            "scatter_ms": scatter_ms, "scatter_gbs_job": scatter_bytes / (scatter_ms / 1e3) / 1e9,
+            "gather_ms": gather_ms, "gather_gbs_job": gather_bytes / (gather_ms / 1e3) / 1e9,
+            "peak_gbs_per_gpu": hbm_peak, "timing": "max over ranks of the median of the per-rank CUDA-event times"}
 
 
 def long_sequence(pkg, attn, dev, world: int, rank: int, steps: int, flush) -> dict:
@@ -553,6 +618,9 @@ def run_ours(args) -> None:
                                                                 max(3, min(args.steps, 10)), flush)
     if world == 1:
         line["components"]["projection_config5"] = projection_stress(pkg, dev, hbm_peak)
+    else:
+        line["components"]["projection_config5_sharded"] = projection_sharded(pkg, dev, world, rank, local_rank,
+                                                                              hbm_peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:

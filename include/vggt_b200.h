@@ -164,6 +164,23 @@ VB200_API int vb200_proj_scatter(int dtype, const void* x, int64_t x_rows, int64
                        const float* entry_w, const float* normalizer, void* out,
                        int64_t out_row_stride, int64_t C, int64_t n_entries, void* workspace,
                        size_t workspace_bytes, void* stream);
+/* The scatter's partial numerators for the query-sharded projection: numerators[j] = the fp32
+ * sums of the plan's corner segments of row j (same order and tree as vb200_proj_scatter),
+ * without the keep row and without dividing by the normaliser; numerators [M, C] fp32,
+ * 16-byte aligned.  Each rank passes the CSR of its own sources; the owners then combine the
+ * ranks' numerators with vb200_rank_reduce_rows.  No reference counterpart (the reference's
+ * compact runs on one GPU, token_merging.py:343-370). */
+VB200_API int vb200_proj_scatter_numerators(int dtype, const void* x, int64_t x_rows, int64_t x_row_stride, int64_t M,
+                                            int64_t corners, const int32_t* seg_offsets, const int32_t* entry_src,
+                                            const float* entry_w, float* numerators, int64_t C, int64_t n_entries,
+                                            void* workspace, size_t workspace_bytes, void* stream);
+/* out[j] = (x[keep[j]] + partials[0][j] + partials[1][j] + ... + partials[R-1][j]) / normalizer[j],
+ * summed in fp32 in rank order and rounded to dtype once: the deterministic cross-rank reduction
+ * of the query-sharded compact.  partials [R, rows, C] fp32 (rank r's numerators of these rows
+ * at r, as an all-to-all delivers them); keep[j] < 0 or keep NULL: no keep row.  C % 8 == 0. */
+VB200_API int vb200_rank_reduce_rows(int dtype, const float* partials, int R, int64_t rows, int64_t C, const void* x,
+                                     int64_t x_rows, int64_t x_row_stride, const int64_t* keep, const float* normalizer,
+                                     void* out, int64_t out_row_stride, void* stream);
 /* Scratch of vb200_proj_scatter for M merged rows, n_entries CSR entries (the length of
  * entry_src) and C channels.  Merged rows with more than 256 entries (skewed plans) are split
  * into 256-entry chunks and groups of 64 chunks; the scratch holds the fp32 chunk and group
@@ -220,6 +237,7 @@ VB200_API int vb200_head_layernorm(int dtype, const void* x, int64_t rows, int64
  * `dtype` before the (fp32) 4-term sum, which is rounded once — the reference's
  * value-dtype arithmetic.  Rows of `out` covered by neither keep nor src are left as they
  * are unless zero_fill != 0 (then they are zeroed), as new_zeros does in the reference.
+ * keep may be NULL: only the source rows are written (K still bounds the parent ids).
  * Replaces WeightedBilinearTokenPlan.restore / restore_query (token_merging.py:387-426). */
 VB200_API int vb200_proj_gather(int dtype, const void* y, int64_t y_row_stride, const int64_t* keep,
                       int64_t K, const int64_t* src, const int64_t* parent, const float* w,
