@@ -32,7 +32,7 @@ from .token_plan import TokenPlan, WeightedBilinearTokenPlan
 from .planners import build_fastvggt_plan, build_ttt_protected_uniform_convex_plan, build_uniform_convex_plan
 from .attention_block import GlobalAttention, compute_attention
 from .install import install, uninstall
-from . import parallel
+from . import parallel, ttt_kernels
 
 __all__ = [
     "GlobalAttention",

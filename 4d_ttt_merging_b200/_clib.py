@@ -63,6 +63,20 @@ _SIGNATURES = {
          _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp],
     ),
     "vb200_proj_scatter_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
+    "vb200_row_l2_normalize": (_c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_float, _c_vp, _c_vp]),
+    "vb200_local_top2_match": (
+        _c_int,
+        [_c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp,
+         _c_vp],
+    ),
+    "vb200_integer_warp": (_c_int, [_c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp]),
+    "vb200_motion_cues": (
+        _c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp],
+    ),
+    "vb200_sensitivity_labels": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_float, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp],
+    ),
     "vb200_proj_scatter_numerators": (
         _c_int,
         [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_vp, _c_size,

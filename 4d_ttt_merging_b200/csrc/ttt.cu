@@ -1,0 +1,293 @@
+// The flow-free TTT pre-pass (vggt_omega/utils/ttt_kernels.py): the per-clip work that turns
+// patch descriptors into the labels, sensitivity and geometry the released planner consumes.
+//
+//   row_l2_normalize   descriptor rows / max(||row||, eps), fp32 out (normalize_rows,
+//                      ttt_kernels.py:233-249; the reference's default is F.normalize(eps=1e-6)).
+//   local_top2_match   exact-window cosine top-2 between the patch grids of two frames
+//                      (_local_top2_match_kernel, ttt_kernels.py:45-101, wrapper :252-277): for
+//                      every source patch the best and second-best dot over the targets within
+//                      (2 ry + 1) x (2 rx + 1), in the reference's candidate order (row-major
+//                      offsets, or reversed for the backward direction); a candidate replaces
+//                      the best only when strictly greater, so the first of equal maxima wins.
+//   integer_warp       border-clamped integer gather of a [B,H,W,C] field by a truncated
+//                      integer flow (ttt_kernels.py:104-127, :280-297).
+//   motion_cues        per patch: mean |flow - predicted| over the available directions, the
+//                      smaller confidence, and |flow - 3x3 zero-padded box mean| (:130-196, :300-318).
+//   sensitivity_labels 0.45 novelty + 0.35 residual + 0.20 boundary (clamped units) and the
+//                      low-confidence / raw-event predicates (:199-230, :321-341).
+//
+// All arithmetic is fp32 with IEEE division and square root.  The descriptors are small
+// (a few hundred thousand patches of 32-256 channels); one warp per patch row keeps a source
+// row in registers and reads the candidate rows through L1, where neighbouring patches'
+// windows overlap.
+#include "common.cuh"
+#include "host_common.h"
+
+namespace vb200 {
+namespace {
+
+constexpr int kTttWarps = 8;
+
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+inline unsigned blocks_of(long long n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
+
+template <typename T>
+__global__ void __launch_bounds__(kTttWarps * 32)
+    row_l2_normalize_kernel(const T* __restrict__ x, long long rows, int C, float eps, float* __restrict__ out) {
+  const long long r = static_cast<long long>(blockIdx.x) * kTttWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const T* xr = x + r * C;
+  float ss = 0.f;
+  for (int c = lane; c < C; c += 32) {
+    const float v = to_f32<T>(xr[c]);
+    ss = fmaf(v, v, ss);
+  }
+  const float norm = fmaxf(sqrtf(warp_allsum(ss)), eps);
+  for (int c = lane; c < C; c += 32) out[r * C + c] = __fdiv_rn(to_f32<T>(xr[c]), norm);
+}
+
+// One warp per source patch; channel c = lane + 32 i lives in register i (C <= 256).
+template <typename T>
+__global__ void __launch_bounds__(kTttWarps * 32)
+    local_top2_match_kernel(const T* __restrict__ source, const T* __restrict__ target, long long rows, int H, int W,
+                            int C, int ry, int rx, int reverse, float* __restrict__ best_out,
+                            float* __restrict__ second_out, int32_t* __restrict__ dy_out,
+                            int32_t* __restrict__ dx_out) {
+  const long long row = static_cast<long long>(blockIdx.x) * kTttWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const long long pc = static_cast<long long>(H) * W;
+  const long long pair = row / pc;
+  const int patch = static_cast<int>(row - pair * pc);
+  const int y = patch / W, x = patch - (patch / W) * W;
+  float s[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = lane + 32 * i;
+    s[i] = c < C ? to_f32<T>(source[row * C + c]) : 0.f;
+  }
+  float best = -INFINITY, second = -INFINITY;
+  int by = 0, bx = 0;
+  const int span_x = 2 * rx + 1;
+  const int candidates = (2 * ry + 1) * span_x;
+  for (int k = 0; k < candidates; ++k) {
+    const int cy = k / span_x, cx = k - (k / span_x) * span_x;
+    const int oy = reverse ? ry - cy : cy - ry;
+    const int ox = reverse ? rx - cx : cx - rx;
+    const int ty = y + oy, tx = x + ox;
+    float sim = -INFINITY;
+    if (ty >= 0 && ty < H && tx >= 0 && tx < W) {  // uniform across the warp
+      const T* t = target + (pair * pc + static_cast<long long>(ty) * W + tx) * C;
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = lane + 32 * i;
+        if (c < C) acc = fmaf(s[i], to_f32<T>(__ldg(t + c)), acc);
+      }
+      sim = warp_allsum(acc);
+    }
+    const bool better = sim > best;
+    second = better ? best : fmaxf(second, sim);
+    if (better) {
+      best = sim;
+      by = oy;
+      bx = ox;
+    }
+  }
+  if (lane == 0) {
+    best_out[row] = best;
+    second_out[row] = second;
+    dy_out[row] = by;
+    dx_out[row] = bx;
+  }
+}
+
+// One thread per element; flow (x, y) is truncated toward zero like a float -> int cast.
+template <typename T>
+__global__ void integer_warp_kernel(const T* __restrict__ field, const float* __restrict__ flow, long long elements,
+                                    int H, int W, int C, T* __restrict__ out) {
+  const long long e = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (e >= elements) return;
+  const long long row = e / C;
+  const int ch = static_cast<int>(e - row * C);
+  const long long pc = static_cast<long long>(H) * W;
+  const long long b = row / pc;
+  const int patch = static_cast<int>(row - b * pc);
+  const int y = patch / W, x = patch - (patch / W) * W;
+  const int fx = static_cast<int>(flow[row * 2]);
+  const int fy = static_cast<int>(flow[row * 2 + 1]);
+  const int sx = min(max(x + fx, 0), W - 1);
+  const int sy = min(max(y + fy, 0), H - 1);
+  out[e] = field[(b * pc + static_cast<long long>(sy) * W + sx) * C + ch];
+}
+
+__device__ __forceinline__ float hyp(float a, float b) { return sqrtf(a * a + b * b); }
+
+// One thread per patch of frame f: forward flow of pair f (f + 1 < F), backward flow of pair
+// f - 1 (f > 0); absent directions contribute nothing and count nothing.
+__global__ void motion_cues_kernel(const float* __restrict__ fwd, const float* __restrict__ bwd,
+                                   const float* __restrict__ pred, const float* __restrict__ fconf,
+                                   const float* __restrict__ bconf, int F, int H, int W, float* __restrict__ residual,
+                                   float* __restrict__ confidence, float* __restrict__ boundary) {
+  const long long pc = static_cast<long long>(H) * W;
+  const long long row = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= F * pc) return;
+  const int f = static_cast<int>(row / pc);
+  const int patch = static_cast<int>(row - f * pc);
+  const int y = patch / W, x = patch - (patch / W) * W;
+  const bool has_f = f + 1 < F, has_b = f > 0;
+  const long long frow = f * pc + patch, brow = (f - 1) * pc + patch;
+  const float fdx = has_f ? fwd[frow * 2] : 0.f, fdy = has_f ? fwd[frow * 2 + 1] : 0.f;
+  const float bdx = has_b ? bwd[brow * 2] : 0.f, bdy = has_b ? bwd[brow * 2 + 1] : 0.f;
+  const float pfx = has_f ? pred[row * 4] : 0.f, pfy = has_f ? pred[row * 4 + 1] : 0.f;
+  const float pbx = has_b ? pred[row * 4 + 2] : 0.f, pby = has_b ? pred[row * 4 + 3] : 0.f;
+  const float f_res = hyp(fdx - pfx, fdy - pfy);
+  const float b_res = hyp(bdx - pbx, bdy - pby);
+  const float count = static_cast<float>(has_f) + static_cast<float>(has_b);
+  float fmx = 0.f, fmy = 0.f, bmx = 0.f, bmy = 0.f;
+  for (int oy = -1; oy <= 1; ++oy) {
+    for (int ox = -1; ox <= 1; ++ox) {
+      const int ny = y + oy, nx = x + ox;
+      const bool inside = ny >= 0 && ny < H && nx >= 0 && nx < W;
+      const long long np = static_cast<long long>(ny) * W + nx;
+      const bool fi = has_f && inside, bi = has_b && inside;
+      fmx += __fdiv_rn(fi ? fwd[(f * pc + np) * 2] : 0.f, 9.f);
+      fmy += __fdiv_rn(fi ? fwd[(f * pc + np) * 2 + 1] : 0.f, 9.f);
+      bmx += __fdiv_rn(bi ? bwd[((f - 1) * pc + np) * 2] : 0.f, 9.f);
+      bmy += __fdiv_rn(bi ? bwd[((f - 1) * pc + np) * 2 + 1] : 0.f, 9.f);
+    }
+  }
+  const float f_bnd = hyp(fdx - fmx, fdy - fmy);
+  const float b_bnd = hyp(bdx - bmx, bdy - bmy);
+  const float fc = has_f ? fconf[frow] : 1.f, bc = has_b ? bconf[brow] : 1.f;
+  const float denom = fmaxf(count, 1.f);
+  residual[row] = __fdiv_rn(f_res + b_res, denom);
+  confidence[row] = fminf(fc, bc);
+  boundary[row] = __fdiv_rn(f_bnd + b_bnd, denom);
+}
+
+__device__ __forceinline__ float clamp01(float v) { return fminf(fmaxf(v, 0.f), 1.f); }
+
+__global__ void sensitivity_kernel(const float* __restrict__ residual, const float* __restrict__ confidence,
+                                   const float* __restrict__ boundary, long long rows, long long pc, float uc,
+                                   const float* __restrict__ rs, const float* __restrict__ bs,
+                                   const float* __restrict__ rt, const float* __restrict__ bt,
+                                   float* __restrict__ sens, int8_t* __restrict__ low, int8_t* __restrict__ event) {
+  const long long row = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const bool later = row / pc > 0;
+  const float res = residual[row], conf = confidence[row], bnd = boundary[row];
+  const float novelty = 1.f - conf;
+  const float ru = clamp01(__fdiv_rn(res, fmaxf(*rs, 1e-6f)));
+  const float bu = clamp01(__fdiv_rn(bnd, fmaxf(*bs, 1e-6f)));
+  sens[row] = clamp01(0.45f * novelty + 0.35f * ru + 0.20f * bu);
+  low[row] = later && conf < uc;
+  event[row] = later && ((res >= *rt && conf >= uc) || bnd >= *bt || novelty >= 0.55f);
+}
+
+}  // namespace
+}  // namespace vb200
+
+using namespace vb200;
+
+extern "C" int vb200_row_l2_normalize(int dtype, const void* x, int64_t rows, int64_t C, float eps, float* out,
+                                      void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "row_l2_normalize: bad dtype %d",
+                dtype);
+  VB200_REQUIRE(rows >= 0 && C > 0 && eps >= 0.f, "row_l2_normalize: bad sizes");
+  if (rows == 0) return VB200_OK;
+  VB200_REQUIRE(x && out, "row_l2_normalize: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_NRM(T)                                                                                        \
+  row_l2_normalize_kernel<T><<<blocks_of(rows, kTttWarps), kTttWarps * 32, 0, st>>>(static_cast<const T*>(x), \
+                                                                                      rows, static_cast<int>(C), eps, out)
+  if (dtype == VB200_F32) VB200_NRM(float);
+  else if (dtype == VB200_BF16) VB200_NRM(__nv_bfloat16);
+  else VB200_NRM(__half);
+#undef VB200_NRM
+  VB200_CHECK_LAUNCH("row_l2_normalize_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_local_top2_match(int dtype, const void* source, const void* target, int64_t pairs, int64_t H,
+                                      int64_t W, int64_t C, int radius_y, int radius_x, int reverse, float* best,
+                                      float* second, int32_t* dy, int32_t* dx, void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "local_top2_match: bad dtype %d",
+                dtype);
+  VB200_REQUIRE(pairs >= 0 && H > 0 && W > 0 && C >= 1 && C <= 256, "local_top2_match: need 1 <= C <= 256");
+  VB200_REQUIRE(radius_y >= 0 && radius_x >= 0 && radius_y < H && radius_x < W,
+                "local_top2_match: radii must lie in [0, H) x [0, W)");
+  const long long rows = pairs * H * W;
+  if (rows == 0) return VB200_OK;
+  VB200_REQUIRE(source && target && best && second && dy && dx, "local_top2_match: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_LTM(T)                                                                                     \
+  local_top2_match_kernel<T><<<blocks_of(rows, kTttWarps), kTttWarps * 32, 0, st>>>(                     \
+      static_cast<const T*>(source), static_cast<const T*>(target), rows, static_cast<int>(H),            \
+      static_cast<int>(W), static_cast<int>(C), radius_y, radius_x, reverse ? 1 : 0, best, second, dy, dx)
+  if (dtype == VB200_F32) VB200_LTM(float);
+  else if (dtype == VB200_BF16) VB200_LTM(__nv_bfloat16);
+  else VB200_LTM(__half);
+#undef VB200_LTM
+  VB200_CHECK_LAUNCH("local_top2_match_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_integer_warp(int dtype, const void* field, const float* flow, int64_t B, int64_t H, int64_t W,
+                                  int64_t C, void* out, void* stream) {
+  VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "integer_warp: bad dtype %d", dtype);
+  VB200_REQUIRE(B >= 0 && H > 0 && W > 0 && C > 0, "integer_warp: bad sizes");
+  const long long elements = B * H * W * C;
+  if (elements == 0) return VB200_OK;
+  VB200_REQUIRE(field && flow && out, "integer_warp: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+#define VB200_IW(T)                                                                                           \
+  integer_warp_kernel<T><<<blocks_of(elements, 256), 256, 0, st>>>(static_cast<const T*>(field), flow, elements, \
+                                                                   static_cast<int>(H), static_cast<int>(W),      \
+                                                                   static_cast<int>(C), static_cast<T*>(out))
+  if (dtype == VB200_F32) VB200_IW(float);
+  else if (dtype == VB200_BF16) VB200_IW(__nv_bfloat16);
+  else VB200_IW(__half);
+#undef VB200_IW
+  VB200_CHECK_LAUNCH("integer_warp_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_motion_cues(const float* forward_flow, const float* backward_flow, const float* predicted,
+                                 const float* forward_conf, const float* backward_conf, int64_t F, int64_t H,
+                                 int64_t W, float* residual, float* confidence, float* boundary, void* stream) {
+  VB200_REQUIRE(F >= 1 && H > 0 && W > 0, "motion_cues: bad sizes");
+  VB200_REQUIRE(predicted && residual && confidence && boundary &&
+                    (F == 1 || (forward_flow && backward_flow && forward_conf && backward_conf)),
+                "motion_cues: null pointer");
+  const long long rows = F * H * W;
+  motion_cues_kernel<<<blocks_of(rows, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      forward_flow, backward_flow, predicted, forward_conf, backward_conf, static_cast<int>(F), static_cast<int>(H),
+      static_cast<int>(W), residual, confidence, boundary);
+  VB200_CHECK_LAUNCH("motion_cues_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_sensitivity_labels(const float* residual, const float* confidence, const float* boundary,
+                                        int64_t rows, int64_t patch_count, float uncertain_confidence,
+                                        const float* residual_scale, const float* boundary_scale,
+                                        const float* residual_threshold, const float* boundary_threshold,
+                                        float* sensitivity, int8_t* low_confidence, int8_t* raw_event,
+                                        void* stream) {
+  VB200_REQUIRE(rows >= 0 && patch_count > 0, "sensitivity_labels: bad sizes");
+  if (rows == 0) return VB200_OK;
+  VB200_REQUIRE(residual && confidence && boundary && residual_scale && boundary_scale && residual_threshold &&
+                    boundary_threshold && sensitivity && low_confidence && raw_event,
+                "sensitivity_labels: null pointer");
+  sensitivity_kernel<<<blocks_of(rows, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      residual, confidence, boundary, rows, patch_count, uncertain_confidence, residual_scale, boundary_scale,
+      residual_threshold, boundary_threshold, sensitivity, low_confidence, raw_event);
+  VB200_CHECK_LAUNCH("sensitivity_kernel");
+  return VB200_OK;
+}

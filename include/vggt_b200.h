@@ -378,6 +378,49 @@ VB200_API int vb200_four_support_projected_gradient(const float* gram, const flo
 VB200_API int vb200_four_support_active_set(const float* gram, const float* rhs, float* out,
                                   int64_t rows, float ridge, void* stream);
 
+/* ---- (f) next, 4: TTT pre-pass kernels ------------------------------------------------------
+ * The flow-free token-matching TTT's per-clip kernels (vggt_omega/utils/ttt_kernels.py).  All
+ * arithmetic is fp32; descriptor / field inputs may be f32, bf16 or f16 (dtype), contiguous. */
+
+/* out[r] = x[r] / max(||x[r]||_2, eps), fp32 [rows, C].  Replaces normalize_rows
+ * (ttt_kernels.py:233-249), whose default is F.normalize(value.float(), eps=1e-6). */
+VB200_API int vb200_row_l2_normalize(int dtype, const void* x, int64_t rows, int64_t C, float eps, float* out,
+                                     void* stream);
+/* Exact-window cosine top-2 of [pairs, H, W, C] descriptors (1 <= C <= 256): for every source
+ * patch (p, y, x) the best and second-best dot product with target[p, y + oy, x + ox] over
+ * |oy| <= radius_y, |ox| <= radius_x inside the grid, and the (dy, dx) of the best.  Candidates
+ * run in row-major offset order (reverse != 0: the reversed order the backward match uses); a
+ * later candidate replaces the best only when strictly greater.  best/second fp32, dy/dx int32,
+ * each [pairs * H * W].  Replaces local_top2_match / _local_top2_match_kernel
+ * (ttt_kernels.py:252-277, :45-101). */
+VB200_API int vb200_local_top2_match(int dtype, const void* source, const void* target, int64_t pairs, int64_t H,
+                                     int64_t W, int64_t C, int radius_y, int radius_x, int reverse, float* best,
+                                     float* second, int32_t* dy, int32_t* dx, void* stream);
+/* out[b, y, x] = field[b, clamp(y + int(flow_y)), clamp(x + int(flow_x))] with the flow
+ * [B, H, W, 2] (x, y) truncated toward zero; field / out [B, H, W, C] of dtype.  Replaces
+ * integer_gather_warp (ttt_kernels.py:280-297, :104-127). */
+VB200_API int vb200_integer_warp(int dtype, const void* field, const float* flow, int64_t B, int64_t H, int64_t W,
+                                 int64_t C, void* out, void* stream);
+/* Per patch of F frames: residual = mean over the available directions (forward flow of pair f
+ * when f + 1 < F, backward flow of pair f - 1 when f > 0) of |flow - predicted|; confidence =
+ * the smaller of those directions' confidences (1 where absent); boundary = mean of |flow - its
+ * 3 x 3 zero-padded box mean|.  forward/backward flow [F-1, H, W, 2], predicted [F, H, W, 4]
+ * (forward dx, dy, backward dx, dy), confidences [F-1, H, W]; outputs fp32 [F, H, W].  Replaces
+ * fused_motion_cues (ttt_kernels.py:300-318, :130-196). */
+VB200_API int vb200_motion_cues(const float* forward_flow, const float* backward_flow, const float* predicted,
+                                const float* forward_conf, const float* backward_conf, int64_t F, int64_t H,
+                                int64_t W, float* residual, float* confidence, float* boundary, void* stream);
+/* sensitivity = clamp(0.45 (1 - conf) + 0.35 clamp(residual / max(rs, 1e-6)) + 0.20
+ * clamp(boundary / max(bs, 1e-6)), 0, 1); for patches after the first frame (row >= patch_count)
+ * low = conf < uncertain_confidence and event = (residual >= rt and conf >= uncertain) or
+ * boundary >= bt or 1 - conf >= 0.55 (int8 0/1).  rs, bs, rt, bt are device fp32 scalars.
+ * Replaces fused_sensitivity_labels (ttt_kernels.py:321-341, :199-230). */
+VB200_API int vb200_sensitivity_labels(const float* residual, const float* confidence, const float* boundary,
+                                       int64_t rows, int64_t patch_count, float uncertain_confidence,
+                                       const float* residual_scale, const float* boundary_scale,
+                                       const float* residual_threshold, const float* boundary_threshold,
+                                       float* sensitivity, int8_t* low_confidence, int8_t* raw_event, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,3 +13,4 @@ from .ref import *  # noqa: F401,F403
 from .synth import *  # noqa: F401,F403
 from . import pipeline  # noqa: F401
 from . import ttt_planner  # noqa: F401
+from . import ttt_prepass  # noqa: F401

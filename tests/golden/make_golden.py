@@ -225,6 +225,57 @@ def main() -> None:
                                        "sensitive_event_budget", "sensitive_event_proposals", "sensitive_event_bases",
                                        "fit_failure_promotions", "global_fallback_candidates", "physical_patch_tokens")})
 
+    # ---------------- TTT pre-pass: correspondences, warp, motion cues, sensitivity ----------------
+    import vggt_omega.utils.token_matching as tm
+    from vggt_omega.utils.ttt_4d import _flow_grid, _warp
+    from vggt_omega.utils.ttt_kernels import normalize_rows as ref_normalize_rows
+    gen = torch.Generator().manual_seed(80)
+    T, H, W, Cd = 4, 6, 7, 32
+    base = torch.randn(H + 6, W + 6, Cd, generator=gen)
+    shifts = [(0, 0), (1, 0), (1, -1), (2, 1)]  # per-frame content shift (dy, dx)
+    raw = torch.stack([base[3 + dy:3 + dy + H, 3 + dx:3 + dx + W] for dy, dx in shifts])
+    raw = raw + 0.3 * torch.randn(T, H, W, Cd, generator=gen)
+    desc = ref_normalize_rows(raw)
+    fflow, bflow, fconf, bconf, _ = tm.adjacent_token_correspondences(desc, search_radius=2)
+    out["ttt_raw"], out["ttt_desc"] = _np(raw), _np(desc)
+    out["ttt_forward_flow"], out["ttt_backward_flow"] = _np(fflow), _np(bflow)
+    out["ttt_forward_conf"], out["ttt_backward_conf"] = _np(fconf), _np(bconf)
+    field = torch.randn(2, 5, 6, 3, generator=gen)
+    flow = torch.randint(-3, 4, (2, 5, 6, 2), generator=gen).float()
+    grid, _ = _flow_grid(flow)
+    out["ttt_field"], out["ttt_flow"], out["ttt_warped"] = _np(field), _np(flow), _np(_warp(field, grid))
+    # motion cues and sensitivity through the CPU path of adapt_token_motion_ttt: the adapter's
+    # predicted motion is recorded from its eval-mode forward, the residual and boundary maps
+    # from the two _robust_unit calls of the sensitivity formula
+    seen = {"pred": [], "unit": []}
+    fwd = tm.SequenceTokenMotionAdapter.forward
+
+    def record_forward(self, inputs, motion_scale):
+        f, b = fwd(self, inputs, motion_scale)
+        if not self.training:
+            seen["pred"].append(torch.cat((f, b), -1).detach().clone())
+        return f, b
+
+    unit = tm._robust_unit
+
+    def record_unit(value, mask):
+        seen["unit"].append(value.detach().clone())
+        return unit(value, mask)
+
+    tm.SequenceTokenMotionAdapter.forward, tm._robust_unit = record_forward, record_unit
+    try:
+        anchors = torch.randn(2, H, W, 3, generator=gen)
+        _, labels, sens, md = tm.adapt_token_motion_ttt(anchors, (0, T - 1), desc, fflow, bflow, fconf, bconf,
+                                                        steps=4, uncertain_confidence=0.10)
+    finally:
+        tm.SequenceTokenMotionAdapter.forward, tm._robust_unit = fwd, unit
+    out["ttt_predicted"] = _np(torch.cat(seen["pred"]).reshape(T, H, W, 4))
+    out["ttt_residual"], out["ttt_boundary"] = _np(seen["unit"][0]), _np(seen["unit"][1])
+    out["ttt_sensitivity"], out["ttt_labels"] = _np(sens), _np(labels)
+    out["ttt_cue_stats"] = np.array([md["motion_residual_threshold"], md["motion_boundary_threshold"],
+                                     md["confidence_mean"], md["motion_residual_mean"], md["motion_boundary_mean"]],
+                                    np.float64)
+
     # ---------------- CPU generator stream ----------------
     out["rand_seed3"] = _np(torch.rand(2, 4, 4, 2, generator=torch.Generator(device="cpu").manual_seed(3)))
 

@@ -177,3 +177,52 @@ def test_ttt_planner_matches_reference(oracle, golden, tag, prune, ratio):
     # its normaliser; ours is the same function of our parents and weights
     np.testing.assert_allclose(oracle.normalizer(theirs, g("weights"), len(keep)), g("normalizer"), rtol=1e-6)
     np.testing.assert_allclose(plan["normalizer"], oracle.normalizer(ours, plan["weights"], len(keep)), rtol=1e-6)
+
+
+def _robust_threshold(value, reliable, floor):
+    """The reference's robust_threshold (token_matching.py:767-776): max(floor, median + 3 x
+    1.4826 x MAD) over the reliable entries, torch's lower median."""
+    sel = np.sort(value[reliable].astype(np.float32))
+    if sel.size == 0:
+        return np.float32(floor)
+    med = sel[(sel.size - 1) // 2]
+    dev = np.sort(np.abs(sel - med))
+    mad = dev[(dev.size - 1) // 2]
+    return max(np.float32(floor), np.float32(med + np.float32(3.0 * 1.4826) * mad))
+
+
+def test_ttt_prepass_matches_reference(oracle, golden):
+    """The TTT pre-pass oracle against the reference's own CPU code: descriptor normalisation,
+    adjacent_token_correspondences (flows exact, confidences to fp32 rounding), the border warp
+    (grid_sample at integer flow), and the motion cues / sensitivity of adapt_token_motion_ttt's
+    CPU path (recorded residual and boundary maps, thresholds and sensitivity)."""
+    tp = oracle.ttt_prepass
+    g = lambda k: golden[f"ttt_{k}"]
+    desc = tp.normalize_rows(g("raw"))
+    np.testing.assert_allclose(desc, g("desc"), rtol=1e-6, atol=1e-7)
+    ff, bf, fc, bc = tp.correspondences(g("desc"), search_radius=2)
+    np.testing.assert_array_equal(ff, g("forward_flow"))
+    np.testing.assert_array_equal(bf, g("backward_flow"))
+    assert np.abs(ff).max() >= 1  # the clip's content shifts are found
+    np.testing.assert_allclose(fc, g("forward_conf"), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(bc, g("backward_conf"), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(tp.integer_warp(g("field"), g("flow")), g("warped"), rtol=1e-6, atol=1e-6)
+    # motion cues on the reference's recorded adapter prediction
+    res, conf, bnd = tp.motion_cues(g("forward_flow"), g("backward_flow"), g("predicted"), g("forward_conf"),
+                                    g("backward_conf"))
+    np.testing.assert_allclose(res, g("residual"), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(bnd, g("boundary"), rtol=1e-5, atol=1e-6)
+    rt_ref, bt_ref, conf_mean, res_mean, bnd_mean = g("cue_stats")
+    np.testing.assert_allclose([conf.mean(), res.mean(), bnd.mean()], [conf_mean, res_mean, bnd_mean], rtol=1e-5)
+    later = (np.arange(res.shape[0]) > 0)[:, None, None] & np.ones(res.shape, bool)
+    reliable = later & (conf >= np.float32(0.10))
+    rt, bt = _robust_threshold(res, reliable, .5), _robust_threshold(bnd, reliable, .5)
+    np.testing.assert_allclose([rt, bt], [rt_ref, bt_ref], rtol=1e-5)
+    rs = max(np.float32(np.quantile(res[later], .9)), np.float32(1e-6))
+    bs = max(np.float32(np.quantile(bnd[later], .9)), np.float32(1e-6))
+    sens, low, event = tp.sensitivity_labels(res, conf, bnd, uncertain_confidence=0.10, residual_scale=rs,
+                                             boundary_scale=bs, residual_threshold=rt, boundary_threshold=bt)
+    np.testing.assert_allclose(sens.ravel(), g("sensitivity"), rtol=1e-5, atol=1e-6)
+    labels = g("labels").reshape(res.shape)
+    assert np.all(labels[0] == 0)
+    assert np.all(event[labels == 1]) and np.all(low[labels == 2])  # labels come from the raw predicates
