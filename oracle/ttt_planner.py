@@ -1,6 +1,8 @@
 """numpy restatement of the reference's released merge planner (TEST ORACLE):
 ``build_ttt_protected_uniform_convex_plan`` (vggt_omega/models/sparse_convex.py:1738-2016) on
-its feature-only support route (support_geometry_weight = 0, the function's default).
+its feature-only support route (support_geometry_weight = 0, the function's default) and its
+Pareto-guarded geometry route (support_geometry_weight > 0 with a guard tolerance; the released
+configuration uses 0.01 and 0).
 
 Pieces, each citing the reference lines it restates:
   * uniform_2x2_tables / cell_table      sparse_convex.py:1327-1368, :1194-1203
@@ -25,7 +27,7 @@ import numpy as np
 from . import ref
 
 __all__ = ["cell_table", "uniform_2x2_tables", "protected_skeleton", "ttt_event_bases", "certificate",
-           "fit_supports", "fit_temporal_local", "fit_global", "build_plan", "LOCAL_FRAME_GROUP"]
+           "fit_supports", "geometry_shortlist", "geometry_residual", "guard_choose", "fit_temporal_local", "fit_global", "build_plan", "LOCAL_FRAME_GROUP"]
 
 LOCAL_FRAME_GROUP = 8  # sparse_convex.py:31
 
@@ -194,20 +196,80 @@ def _certified(fit, threshold):
     return (fit[2] >= threshold) & (fit[3] <= limit) & (fit[4] >= 0.80)
 
 
-def fit_global(features, basis_ids, threshold: float, source_ids):
-    """_adaptive_fit_fused on its feature route with the one-hot shortcut off (the default):
-    top-4 over the whole basis, then the solve and certificate of every row."""
+def geometry_shortlist(features, geometry, query_ids, basis_ids, weight: float):
+    """The Pareto-guard selection (sparse_convex.py:502-531 local, :263-306 global): bf16 feature
+    scores; a top-16 shortlist (top-min(16, basis)); joint = score - w * sum_d (g_s - g_c)^2 in
+    float32 (squares summed in order d = 0..3); the joint top-4 positions, reordered by feature
+    score (stable descending, so equal scores keep the joint order).  Every ranking here is a
+    stable descending sort (ties to the lower position; the reference's torch.topk leaves tie
+    order open).  -> (feature top-4 basis ids, joint basis ids), each [S, 4]."""
+    f = np.asarray(features, np.float32)
+    query_ids = np.asarray(query_ids, np.int64)
+    basis_ids = np.asarray(basis_ids, np.int64)
+    vals, idx = ref.similarity_topk(f[query_ids], f[basis_ids], min(16, len(basis_ids)))
+    g = np.asarray(geometry, np.float32)
+    diff = (g[query_ids][:, None, :] - g[basis_ids[idx]]).astype(np.float32)
+    sq = (diff * diff).astype(np.float32)
+    dist = (((sq[..., 0] + sq[..., 1]).astype(np.float32) + sq[..., 2]).astype(np.float32) + sq[..., 3])
+    joint = (vals.astype(np.float32) - (np.float32(weight) * dist.astype(np.float32)).astype(np.float32))
+    jpos = np.argsort(-joint.astype(np.float32), axis=1, kind="stable")[:, :4]
+    canon = np.argsort(-np.take_along_axis(vals, jpos, 1), axis=1, kind="stable")
+    jpos = np.take_along_axis(jpos, canon, 1)
+    return basis_ids[idx[:, :4]], basis_ids[np.take_along_axis(idx, jpos, 1)]
+
+
+def geometry_residual(geometry, source_ids, support_ids, weights):
+    """|| g_s - sum_c w_c g_{support_c} || (sparse_convex.py:577-582, :325-330)."""
+    g = np.asarray(geometry, np.float64)
+    recon = np.einsum("sc,scd->sd", np.asarray(weights, np.float64), g[np.asarray(support_ids, np.int64)])
+    return np.linalg.norm(g[np.asarray(source_ids, np.int64)] - recon, axis=1)
+
+
+def guard_choose(features, geometry, source_ids, feature_ids, joint_ids, tolerance: float):
+    """Both solves and the Pareto guard (sparse_convex.py:586-639, :335-367): the joint set wins
+    only where it differs from the feature top-4, its cosine and residual are no worse (up to
+    the tolerance) and its 4-D residual is strictly smaller.  -> (support, weights, cosine,
+    residual, norm, chosen mask)."""
+    feat = fit_supports(features, source_ids, feature_ids)
+    joint = fit_supports(features, source_ids, joint_ids)
+    changed = np.any(joint_ids != feature_ids, axis=1)
+    gf = geometry_residual(geometry, source_ids, feature_ids, feat[0])
+    gj = geometry_residual(geometry, source_ids, joint_ids, joint[0])
+    choose = (joint[1] + tolerance >= feat[1]) & (joint[2] <= feat[2] + tolerance) & (gj < gf) & changed
+    pick = lambda a, b: np.where(choose.reshape((-1,) + (1,) * (np.ndim(a) - 1)), a, b)
+    return (pick(joint_ids, feature_ids),) + tuple(pick(j, f) for j, f in zip(joint, feat)) + (choose,)
+
+
+def fit_global(features, basis_ids, threshold: float, source_ids, geometry=None, geometry_weight: float = 0.0,
+               guard_tolerance=None, stats=None):
+    """_adaptive_fit_fused with the one-hot shortcut off (the default): top-4 over the whole
+    basis, then the solve and certificate of every row; with geometry_weight > 0 and a guard
+    tolerance, the top-16 shortlist, joint re-rank and Pareto guard (:263-367)."""
+    if geometry_weight > 0 and guard_tolerance is not None:
+        fids, jids = geometry_shortlist(features, geometry, source_ids, basis_ids, geometry_weight)
+        out = guard_choose(features, geometry, source_ids, fids, jids, guard_tolerance)
+        if stats is not None:
+            stats["guard_selected"] = stats.get("guard_selected", 0) + int(out[5].sum())
+        return out[:5]
+    if geometry_weight > 0:
+        raise ValueError("the joint-metric route (geometry weight without a guard tolerance) is not restated")
     support = _top4(features, source_ids, basis_ids)
     return (support,) + fit_supports(features, source_ids, support)
 
 
 def fit_temporal_local(features, basis_ids, *, frames: int, patches: int, threshold: float, source_ids,
-                       frame_group: int = LOCAL_FRAME_GROUP):
+                       frame_group: int = LOCAL_FRAME_GROUP, geometry=None, geometry_weight: float = 0.0,
+                       guard_tolerance=None, stats=None):
     """_adaptive_fit_temporal_local (sparse_convex.py:440-684) on its feature route: sources of
     frames [b, b + 8) (b = 1, 9, ...) search the basis of frame 0 and frames [max(1, b - 1),
     min(F - 1, b + 8)]; rows that fail the certificate (and reference-frame sources, which no
-    group covers) take the global route.  -> (support ids [S, 4], weights, cosine, residual,
-    reconstruction norm)."""
+    group covers) take the global route.  With geometry_weight > 0 and a guard tolerance, each
+    group's selection is the guarded shortlist (geometry_shortlist / guard_choose;
+    sparse_convex.py:502-531, :586-639) and the fallback is the guarded global route.
+    -> (support ids [S, 4], weights, cosine, residual, reconstruction norm)."""
+    guard = geometry_weight > 0 and guard_tolerance is not None
+    if geometry_weight > 0 and not guard:
+        raise ValueError("the joint-metric route (geometry weight without a guard tolerance) is not restated")
     source_ids = np.asarray(source_ids, np.int64)
     basis_ids = np.asarray(basis_ids, np.int64)
     n = len(source_ids)
@@ -225,14 +287,21 @@ def fit_temporal_local(features, basis_ids, *, frames: int, patches: int, thresh
             continue
         lo, hi = max(1, begin - 1), min(frames - 1, end)
         local = basis_ids[(bf == 0) | ((bf >= lo) & (bf <= hi))]
-        sup = _top4(features, source_ids[rows], local)
-        w, c, r, nr = fit_supports(features, source_ids[rows], sup)
+        if guard:
+            fids, jids = geometry_shortlist(features, geometry, source_ids[rows], local, geometry_weight)
+            sup, w, c, r, nr, chosen = guard_choose(features, geometry, source_ids[rows], fids, jids, guard_tolerance)
+            if stats is not None:  # counted before the fallback, as the reference counts
+                stats["guard_selected"] = stats.get("guard_selected", 0) + int(chosen.sum())
+        else:
+            sup = _top4(features, source_ids[rows], local)
+            w, c, r, nr = fit_supports(features, source_ids[rows], sup)
         support[rows], weights[rows], cos[rows], res[rows], norm[rows] = sup, w, c, r, nr
         assigned[rows] = True
     fit = (support, weights, cos, res, norm)
     fallback = np.nonzero(~(assigned & _certified(fit, threshold)))[0]
     if len(fallback):
-        g = fit_global(features, basis_ids, threshold, source_ids[fallback])
+        g = fit_global(features, basis_ids, threshold, source_ids[fallback], geometry, geometry_weight,
+                       guard_tolerance, stats)
         for dst, val in zip(fit, g):
             dst[fallback] = val
     return fit
@@ -240,8 +309,11 @@ def fit_temporal_local(features, basis_ids, *, frames: int, patches: int, thresh
 
 def build_plan(tokens, *, frames: int, tokens_per_frame: int, patch_token_start: int, patch_hw, threshold: float,
                labels, sensitivity, geometry, top1_prune_threshold: float = 0.95,
-               sensitive_event_ratio: float = 0.02, selection_geometry_weight: float = 0.01):
-    """build_ttt_protected_uniform_convex_plan (sparse_convex.py:1738-2016), feature route.
+               sensitive_event_ratio: float = 0.02, selection_geometry_weight: float = 0.01,
+               support_geometry_weight: float = 0.0, support_geometry_guard_tolerance=None):
+    """build_ttt_protected_uniform_convex_plan (sparse_convex.py:1738-2016): the feature route,
+    or with support_geometry_weight > 0 and a guard tolerance the Pareto-guarded geometry route
+    (both fits of :1845-1891 take geometry, weight and tolerance).
     tokens [N, D] float32.  Returns dict(keep, source, parent (compact ids), weights, normalizer,
     special, special_compact, stable_basis, event_proposal, event, accepted)."""
     height, width = patch_hw
@@ -252,6 +324,8 @@ def build_plan(tokens, *, frames: int, tokens_per_frame: int, patch_token_start:
         raise ValueError("invalid protected TTT token layout")
     patch_ids = (np.arange(frames)[:, None] * tokens_per_frame + patch_token_start + np.arange(patches)[None]).ravel()
     features = ref.normalize_bf16(np.asarray(tokens, np.float32)[patch_ids], 1e-8)
+    gkw = dict(geometry=np.asarray(geometry, np.float32) if support_geometry_weight else None,
+               geometry_weight=support_geometry_weight, guard_tolerance=support_geometry_guard_tolerance)
     stable, stats = protected_skeleton(features, frames, patch_hw, top1_prune_threshold)
     stable_mask = np.zeros(patch_count, bool)
     stable_mask[stable] = True
@@ -263,7 +337,7 @@ def build_plan(tokens, *, frames: int, tokens_per_frame: int, patch_token_start:
     event = proposal[:0]
     if budget and len(proposal):
         efit = fit_temporal_local(features, stable, frames=frames, patches=patches, threshold=threshold,
-                                  source_ids=proposal)
+                                  source_ids=proposal, **gkw)
         cand = np.nonzero(~_certified(efit, threshold))[0]
         if len(cand) > budget:
             priority = (np.asarray(sensitivity, np.float32)[proposal[cand]].astype(np.float64) * efit[3][cand])
@@ -273,7 +347,9 @@ def build_plan(tokens, *, frames: int, tokens_per_frame: int, patch_token_start:
     basis_mask = np.zeros(patch_count, bool)
     basis_mask[basis] = True
     source = np.nonzero(~basis_mask)[0]
-    fit = fit_temporal_local(features, basis, frames=frames, patches=patches, threshold=threshold, source_ids=source)
+    fit_stats = {"guard_selected": 0}
+    fit = fit_temporal_local(features, basis, frames=frames, patches=patches, threshold=threshold, source_ids=source,
+                             stats=fit_stats, **gkw)
     accepted = _certified(fit, threshold)
     rows = np.nonzero(accepted)[0]
     source_local, support_local, weights = source[rows], fit[0][rows], fit[1][rows].astype(np.float32)
@@ -290,4 +366,5 @@ def build_plan(tokens, *, frames: int, tokens_per_frame: int, patch_token_start:
     norm = ref.normalizer(parent, weights, len(keep))
     return dict(keep=keep, source=patch_ids[source_local], parent=parent, weights=weights, normalizer=norm,
                 special=special, special_compact=o2c[special], stable_basis=stable, event_proposal=proposal,
-                event=event, accepted=accepted, fit_source=source, fit=fit, features=features)
+                event=event, accepted=accepted, fit_source=source, fit=fit, features=features,
+                guard_selected=fit_stats["guard_selected"])

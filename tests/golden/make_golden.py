@@ -186,8 +186,12 @@ def main() -> None:
     sys.path.insert(0, str(Path(__file__).resolve().parents[2]))
     from oracle.torch_path import projected_gradient as torch_pg
     sc.four_support_projected_gradient = lambda gram, rhs, *, steps=32: torch_pg(gram.float(), rhs.float(), steps)
-    for tag, prune, ratio, noise in (("ttt_prune", 0.95, 0.02, 0.15), ("ttt_noprune", 2.0, 0.05, 0.35)):
-        gen = torch.Generator().manual_seed(70 if prune <= 1 else 71)
+    # ttt_geo: the released configuration's support route (geometry weight 0.01, guard
+    # tolerance 0, top-1 pruning off, event ratio 0.01) on geometry that follows the content
+    cases = (("ttt_prune", 0.95, 0.02, 0.15, 0.0, 70), ("ttt_noprune", 2.0, 0.05, 0.35, 0.0, 71),
+             ("ttt_geo", 2.0, 0.01, 0.35, 0.01, 72))
+    for tag, prune, ratio, noise, support_w, seed in cases:
+        gen = torch.Generator().manual_seed(seed)
         frames, hw, pts, dim = 10, (8, 8), 5, 64
         patches = hw[0] * hw[1]
         tpf = pts + patches
@@ -201,11 +205,16 @@ def main() -> None:
         labels[:patches] = 0
         sensitivity = torch.rand(frames * patches, generator=gen)
         geometry = torch.randn(frames * patches, 4, generator=gen)
+        if support_w:  # per-patch xyz of the base content plus noise, time in the fourth channel
+            base_xyz = torch.randn(patches, 3, generator=gen)
+            geometry = torch.cat([base_xyz[None].expand(frames, -1, -1) + 0.3 * torch.randn(frames, patches, 3, generator=gen),
+                                  torch.linspace(-1, 1, frames)[:, None, None].expand(-1, patches, 1)], -1).reshape(-1, 4)
         tokens = tok.reshape(1, frames * tpf, dim)
+        extra = dict(support_geometry_weight=support_w, support_geometry_guard_tolerance=0.0) if support_w else {}
         plan = sc.build_ttt_protected_uniform_convex_plan(
             tokens, frames=frames, tokens_per_frame=tpf, patch_token_start=pts, patch_hw=hw, threshold=0.9,
             labels=labels, sensitivity=sensitivity, geometry=geometry, top1_prune_threshold=prune,
-            sensitive_event_ratio=ratio)
+            sensitive_event_ratio=ratio, **extra)
         out[f"{tag}_tokens"] = _np(tokens[0])
         out[f"{tag}_labels"] = _np(labels)
         out[f"{tag}_sensitivity"] = _np(sensitivity)
@@ -221,6 +230,8 @@ def main() -> None:
                                          md["sensitive_event_budget"], md["sensitive_event_proposals"],
                                          md["sensitive_event_bases"], md["fit_failure_promotions"],
                                          md["global_fallback_candidates"]], np.int64)
+        if support_w:
+            out[f"{tag}_guard_selected"] = np.array([md["geometry_guard_selected"]], np.int64)
         print(tag, {k: md[k] for k in ("protected_uniform_bases", "top1_pruned_uniform_bases",
                                        "sensitive_event_budget", "sensitive_event_proposals", "sensitive_event_bases",
                                        "fit_failure_promotions", "global_fallback_candidates", "physical_patch_tokens")})

@@ -138,16 +138,19 @@ def test_mass_bias_attention_known_answers(oracle):
                                oracle.mass_bias_attention(q, k, v), rtol=1e-12)
 
 
-@pytest.mark.parametrize("tag,prune,ratio", [("ttt_prune", 0.95, 0.02), ("ttt_noprune", 2.0, 0.05)])
-def test_ttt_planner_matches_reference(oracle, golden, tag, prune, ratio):
+@pytest.mark.parametrize("tag,prune,ratio,support_w", [("ttt_prune", 0.95, 0.02, 0.0), ("ttt_noprune", 2.0, 0.05, 0.0),
+                                                       ("ttt_geo", 2.0, 0.01, 0.01)])
+def test_ttt_planner_matches_reference(oracle, golden, tag, prune, ratio, support_w):
     """The released planner (build_ttt_protected_uniform_convex_plan) restated in numpy against
     the reference's own output: same keep set, sources, parents and masses; weights to fp32
-    solver precision."""
+    solver precision.  ttt_geo runs the released configuration's Pareto-guarded geometry route
+    (support weight 0.01, guard tolerance 0)."""
     g = lambda k: golden[f"{tag}_{k}"]
+    extra = dict(support_geometry_weight=support_w, support_geometry_guard_tolerance=0.0) if support_w else {}
     plan = oracle.ttt_planner.build_plan(
         g("tokens"), frames=10, tokens_per_frame=69, patch_token_start=5, patch_hw=(8, 8), threshold=0.9,
         labels=g("labels"), sensitivity=g("sensitivity"), geometry=g("geometry"), top1_prune_threshold=prune,
-        sensitive_event_ratio=ratio)
+        sensitive_event_ratio=ratio, **extra)
     counts = g("counts")  # stable bases, pruned, event budget, proposals, events, promotions, fallbacks
     assert len(plan["stable_basis"]) == counts[0]
     assert len(plan["event_proposal"]) == counts[3] and len(plan["event"]) == counts[4]
@@ -163,7 +166,24 @@ def test_ttt_planner_matches_reference(oracle, golden, tag, prune, ratio):
     ours, theirs = plan["parent"], g("parent")
     score = lambda par: oracle.round_bf16(np.einsum("sd,scd->sc", feats[src].astype(np.float64),
                                                     feats[patch(keep[par])].astype(np.float64)).astype(np.float32))
-    np.testing.assert_array_equal(score(ours), score(theirs))
+    so, st = score(ours), score(theirs)
+    if not support_w:
+        np.testing.assert_array_equal(so, st)
+    else:
+        # the guarded route re-ranks a shortlist and solves twice; an exact bf16 tie among a row's
+        # candidates changes which support the solver starts from, hence its weights, hence the
+        # guard's decision.  Rows whose score sequences differ must hold such a tie, and be few.
+        differ = np.nonzero(np.any(so != st, axis=1))[0]
+        assert len(differ) <= 0.02 * len(so), len(differ)
+        for r in differ:
+            ids = np.concatenate([ours[r], theirs[r]])
+            vals = np.concatenate([so[r], st[r]])
+            uniq = {}
+            for i, v in zip(ids, vals):
+                uniq.setdefault(int(i), float(v))
+            assert len(set(uniq.values())) < len(uniq), (r, ours[r], theirs[r], so[r], st[r])
+        # and the guard took the joint set about as often as the reference's
+        assert abs(int(plan["guard_selected"]) - int(g("guard_selected")[0])) <= max(3, 0.05 * g("guard_selected")[0])
     same = np.all(ours == theirs, axis=1)
     assert same.mean() > 0.8
     # weights: identical supports give the reference's weights; where a tie moved which support
