@@ -1,12 +1,14 @@
 // Merge step for B200 (sm_100a): cosine-similarity GEMM with a fused running top-k epilogue.
 //
 //   score[r, n] = bf16_round( sum_d query[r, d] * basis[n, d] )     (fp32 accumulation)
-//   out[r]      = the k highest scores of row r (k = 1 or 4), best first, ties -> lower n
+//   out[r]      = the k highest scores of row r (k = 1, 4 or 16), best first, ties -> lower n
 //
 // This is the bf16 GEMM + max(-1) of build_fastvggt_plan (vggt_omega/models/token_merging.py:
 // 1100-1111) and the bf16 GEMM + topk(4) support retrieval (vggt_omega/models/sparse_convex.py:
 // 264, 294, 546-547) / streaming_top4 (vggt_omega/models/sparse_convex_kernels.py:20-93, which
 // rounds the accumulator to bf16 before ranking, :51-54), without writing the score matrix.
+// k = 16 is the semantic shortlist of the geometry-guarded support route (sparse_convex.py:
+// 263-266, 506-508: score.topk(16)).
 //
 // Kernel (one CTA per 128 query rows of one group, 6 warps):
 //   warp 0      TMA producer: for every basis tile of tile_n rows and every 64-channel
@@ -142,8 +144,20 @@ __device__ __forceinline__ void key_insert(uint32_t (&kk)[4], uint32_t key) {
   m = max(kk[2], key); key = min(kk[2], key); kk[2] = m;
   kk[3] = max(kk[3], key);
 }
+// Sixteen slots: the cascade runs only for a key above the current 16th (after the first few
+// tiles almost no score is), so the common case is one compare.
+__device__ __forceinline__ void key_insert(uint32_t (&kk)[16], uint32_t key) {
+  if (key <= kk[15]) return;
+#pragma unroll
+  for (int i = 0; i < 15; ++i) {
+    const uint32_t m = max(kk[i], key);
+    key = min(kk[i], key);
+    kk[i] = m;
+  }
+  kk[15] = max(kk[15], key);
+}
 
-// kKeys: top-4 through score_key (every basis group has at most 65536 rows).
+// kKeys: top-K (K = 4 or 16) through score_key (every basis group has at most 65536 rows).
 template <int K, bool kKeys>
 __global__ void __launch_bounds__(kThreads, 1)
     sim_topk_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_b,
@@ -243,9 +257,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    float tv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    int ti[4] = {-1, -1, -1, -1};
-    uint32_t kk[4] = {0u, 0u, 0u, 0u};
+    constexpr int KS = K < 4 ? 4 : K;  // slots (K = 1 uses the first of four)
+    float tv[KS];
+    int ti[KS];
+    uint32_t kk[KS];
+#pragma unroll
+    for (int i = 0; i < KS; ++i) {
+      tv[i] = -INFINITY;
+      ti[i] = -1;
+      kk[i] = 0u;
+    }
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
       const int ab = t & 1;
@@ -280,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) *abort_flag = 1;
     bool piece_written = false;
     if constexpr (kKeys) {
-      if (p.split > 1) {
+      if (K == 4 && p.split > 1) {
         // split search: this piece's four keys go to slot z of the row's 48 output bytes
         // (slot 0: the row of `values`, slots 1-2: the halves of the row of `indices`);
         // topk_merge_kernel combines the slots and writes the final row
@@ -288,12 +309,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (grow < q1) {
           uint4* slot = blockIdx.z == 0 ? reinterpret_cast<uint4*>(p.values) + grow
                                         : reinterpret_cast<uint4*>(p.indices) + 2 * grow + (blockIdx.z - 1);
-          *slot = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+          *slot = make_uint4(kk[0], kk[1], kk[2], kk[KS - 1]);
         }
         piece_written = true;
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < KS; ++i) {
         tv[i] = kk[i] ? key_score(kk[i]) : -INFINITY;
         ti[i] = kk[i] ? static_cast<int>(b0 + (0xFFFF - static_cast<int>(kk[i] & 0xFFFFu))) : -1;
       }
@@ -406,7 +427,7 @@ extern "C" int vb200_sim_topk(const void* query, int64_t q_row_stride, const voi
                               int64_t b_row_stride, int64_t R, int64_t Nb, int64_t D, int k,
                               const int64_t* q_begin, const int64_t* b_begin, int64_t groups,
                               float* values, int64_t* indices, void* stream) {
-  VB200_REQUIRE(k == 1 || k == 4, "sim_topk: k must be 1 or 4 (got %d)", k);
+  VB200_REQUIRE(k == 1 || k == 4 || k == 16, "sim_topk: k must be 1, 4 or 16 (got %d)", k);
   VB200_REQUIRE(R >= 0 && Nb >= 0 && D > 0 && D % kBK == 0,
                 "sim_topk: D must be a positive multiple of 64 (got %lld)", (long long)D);
   VB200_REQUIRE(groups >= 1, "sim_topk: groups must be >= 1");
@@ -441,9 +462,12 @@ extern "C" int vb200_sim_topk(const void* query, int64_t q_row_stride, const voi
   if ((rc = make_rows_map(&tq, query, R, D, q_row_stride, kBM)) != VB200_OK) return rc;
   if (Nb > 0 && (rc = make_rows_map(&tb, basis, Nb, D, b_row_stride, tile_n)) != VB200_OK) return rc;
   if (Nb == 0) tb = tq;  // never read: every group then has zero basis tiles
+  VB200_REQUIRE(k != 16 || max_nb <= 65536, "sim_topk: k = 16 needs basis groups of at most 65536 rows");
   const bool keys4 = k == 4 && max_nb <= 65536;
   TopkParams prm{values, indices, k, static_cast<int>(D / kBK), tile_n, 1};
-  auto kernel = k == 1 ? sim_topk_kernel<1, false> : (keys4 ? sim_topk_kernel<4, true> : sim_topk_kernel<4, false>);
+  auto kernel = k == 1 ? sim_topk_kernel<1, false>
+                       : k == 16 ? sim_topk_kernel<16, true>
+                                 : (keys4 ? sim_topk_kernel<4, true> : sim_topk_kernel<4, false>);
   VB200_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
                    "cudaFuncSetAttribute");
   for (int64_t g0 = 0; g0 < groups; g0 += kMaxGroups) {

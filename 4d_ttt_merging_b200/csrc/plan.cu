@@ -410,6 +410,123 @@ __global__ void __launch_bounds__(kFitWarps * 32)
   if (lane == 0) out[q] = best;
 }
 
+// The Pareto-guarded geometry route's selection (sparse_convex.py:502-531, :263-306), one
+// thread per source: from the row's top-k feature shortlist (bf16 scores, best first, -1 for
+// empty slots) the joint value score - w * sum_d (g_s - g_c)^2 (fp32, squares added in order
+// d = 0..3, no contraction), its top-4 positions (ties to the lower position), reordered by
+// feature score (insertion sort, equal scores keep the joint order).  feature_ids = the first
+// four shortlist ids; changed = the two id lists differ anywhere.
+__global__ void geometry_shortlist_kernel(const float* __restrict__ values, const int64_t* __restrict__ indices,
+                                          long long S, int k, const float* __restrict__ query_geo,
+                                          const float* __restrict__ basis_geo, long long Nb, float weight,
+                                          int64_t* __restrict__ feature_ids, int64_t* __restrict__ joint_ids,
+                                          int32_t* __restrict__ changed) {
+  const long long s = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (s >= S) return;
+  float v[16], joint[16];
+  int64_t id[16];
+  const float4 gs = *reinterpret_cast<const float4*>(query_geo + s * 4);
+  for (int c = 0; c < k; ++c) {
+    v[c] = values[s * k + c];
+    id[c] = indices[s * k + c];
+    joint[c] = -INFINITY;
+    if (id[c] < 0) continue;
+    if (id[c] >= Nb) {
+      atomicOr(&g_plan_err, kErrBadArgument);
+      id[c] = -1;
+      continue;
+    }
+    const float4 gc = *reinterpret_cast<const float4*>(basis_geo + id[c] * 4);
+    const float d0 = __fsub_rn(gs.x, gc.x), d1 = __fsub_rn(gs.y, gc.y);
+    const float d2 = __fsub_rn(gs.z, gc.z), d3 = __fsub_rn(gs.w, gc.w);
+    float dist = __fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1));
+    dist = __fadd_rn(dist, __fmul_rn(d2, d2));
+    dist = __fadd_rn(dist, __fmul_rn(d3, d3));
+    joint[c] = __fsub_rn(v[c], __fmul_rn(weight, dist));
+  }
+  int pos[4];
+  unsigned taken = 0u;
+  for (int j = 0; j < 4; ++j) {
+    int best = -1;
+    for (int c = 0; c < k; ++c) {
+      if (taken & (1u << c)) continue;
+      if (best < 0 || joint[c] > joint[best]) best = c;
+    }
+    pos[j] = best;
+    taken |= 1u << best;
+  }
+  for (int j = 1; j < 4; ++j) {  // stable descending by feature score
+    const int p = pos[j];
+    int i = j - 1;
+    while (i >= 0 && v[pos[i]] < v[p]) {
+      pos[i + 1] = pos[i];
+      --i;
+    }
+    pos[i + 1] = p;
+  }
+  int diff = 0;
+  for (int j = 0; j < 4; ++j) {
+    feature_ids[s * 4 + j] = id[j];
+    joint_ids[s * 4 + j] = id[pos[j]];
+    diff |= id[pos[j]] != id[j];
+  }
+  changed[s] = diff;
+}
+
+__device__ __forceinline__ float geometry_residual(const float* __restrict__ geo, long long rows, float4 gs,
+                                                   const int64_t* ids, const float* w) {
+  float r[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int c = 0; c < 4; ++c) {
+    long long id = ids[c];
+    if (id < 0 || id >= rows) {
+      atomicOr(&g_plan_err, kErrBadArgument);
+      id = 0;
+    }
+    const float4 g = *reinterpret_cast<const float4*>(geo + id * 4);
+    r[0] = __fadd_rn(r[0], __fmul_rn(w[c], g.x));
+    r[1] = __fadd_rn(r[1], __fmul_rn(w[c], g.y));
+    r[2] = __fadd_rn(r[2], __fmul_rn(w[c], g.z));
+    r[3] = __fadd_rn(r[3], __fmul_rn(w[c], g.w));
+  }
+  const float e0 = gs.x - r[0], e1 = gs.y - r[1], e2 = gs.z - r[2], e3 = gs.w - r[3];
+  return sqrtf(e0 * e0 + e1 * e1 + e2 * e2 + e3 * e3);
+}
+
+// The Pareto guard (sparse_convex.py:586-639, :335-367), one thread per source: the joint set
+// wins only where it differs from the feature top-4, its cosine and residual are no worse up
+// to the tolerance, and its 4-D residual || g_s - sum_c w_c g_c || is strictly smaller.
+__global__ void geometry_guard_kernel(long long S, const float* __restrict__ geo, long long rows,
+                                      const int64_t* __restrict__ source_ids, const int64_t* __restrict__ fid,
+                                      const float* __restrict__ fw, const float* __restrict__ fcos,
+                                      const float* __restrict__ fres, const float* __restrict__ fnrm,
+                                      const int64_t* __restrict__ jid, const float* __restrict__ jw,
+                                      const float* __restrict__ jcos, const float* __restrict__ jres,
+                                      const float* __restrict__ jnrm, const int32_t* __restrict__ changed, float tol,
+                                      int64_t* __restrict__ out_id, float* __restrict__ out_w,
+                                      float* __restrict__ out_cos, float* __restrict__ out_res,
+                                      float* __restrict__ out_nrm, int32_t* __restrict__ chosen) {
+  const long long s = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (s >= S) return;
+  long long src = source_ids[s];
+  if (src < 0 || src >= rows) {
+    atomicOr(&g_plan_err, kErrBadArgument);
+    src = 0;
+  }
+  const float4 gs = *reinterpret_cast<const float4*>(geo + src * 4);
+  const float gf = geometry_residual(geo, rows, gs, fid + s * 4, fw + s * 4);
+  const float gj = geometry_residual(geo, rows, gs, jid + s * 4, jw + s * 4);
+  const bool pick = changed[s] != 0 && __fadd_rn(jcos[s], tol) >= fcos[s] && jres[s] <= __fadd_rn(fres[s], tol) &&
+                    gj < gf;
+  for (int c = 0; c < 4; ++c) {
+    out_id[s * 4 + c] = pick ? jid[s * 4 + c] : fid[s * 4 + c];
+    out_w[s * 4 + c] = pick ? jw[s * 4 + c] : fw[s * 4 + c];
+  }
+  out_cos[s] = pick ? jcos[s] : fcos[s];
+  out_res[s] = pick ? jres[s] : fres[s];
+  out_nrm[s] = pick ? jnrm[s] : fnrm[s];
+  chosen[s] = pick;
+}
+
 inline unsigned blocks(long long n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
 
 }  // namespace
@@ -550,5 +667,42 @@ extern "C" int vb200_row_max_dot(int dtype, const void* feat, int64_t rows, int6
   else VB200_RMD(__half);
 #undef VB200_RMD
   VB200_CHECK_LAUNCH("row_max_dot_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_geometry_shortlist(const float* values, const int64_t* indices, int64_t S, int k,
+                                        const float* query_geo, const float* basis_geo, int64_t Nb, float weight,
+                                        int64_t* feature_ids, int64_t* joint_ids, int32_t* changed, void* stream) {
+  VB200_REQUIRE(S >= 0 && k >= 4 && k <= 16 && Nb >= 0, "geometry_shortlist: need 4 <= k <= 16");
+  if (S == 0) return VB200_OK;
+  VB200_REQUIRE(values && indices && query_geo && basis_geo && feature_ids && joint_ids && changed,
+                "geometry_shortlist: null pointer");
+  VB200_REQUIRE((reinterpret_cast<uintptr_t>(query_geo) & 15u) == 0 && (reinterpret_cast<uintptr_t>(basis_geo) & 15u) == 0,
+                "geometry_shortlist: geometry rows must be 16-byte aligned [rows, 4] fp32");
+  geometry_shortlist_kernel<<<blocks(S, 128), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      values, indices, S, k, query_geo, basis_geo, Nb, weight, feature_ids, joint_ids, changed);
+  VB200_CHECK_LAUNCH("geometry_shortlist_kernel");
+  return VB200_OK;
+}
+
+extern "C" int vb200_geometry_guard(int64_t S, const float* geometry, int64_t rows, const int64_t* source_ids,
+                                    const int64_t* feature_ids, const float* feature_w, const float* feature_cos,
+                                    const float* feature_res, const float* feature_nrm, const int64_t* joint_ids,
+                                    const float* joint_w, const float* joint_cos, const float* joint_res,
+                                    const float* joint_nrm, const int32_t* changed, float tolerance, int64_t* out_ids,
+                                    float* out_w, float* out_cos, float* out_res, float* out_nrm, int32_t* chosen,
+                                    void* stream) {
+  VB200_REQUIRE(S >= 0 && rows > 0 && tolerance >= 0.f, "geometry_guard: bad sizes or negative tolerance");
+  if (S == 0) return VB200_OK;
+  VB200_REQUIRE(geometry && source_ids && feature_ids && feature_w && feature_cos && feature_res && feature_nrm &&
+                    joint_ids && joint_w && joint_cos && joint_res && joint_nrm && changed && out_ids && out_w &&
+                    out_cos && out_res && out_nrm && chosen,
+                "geometry_guard: null pointer");
+  VB200_REQUIRE((reinterpret_cast<uintptr_t>(geometry) & 15u) == 0,
+                "geometry_guard: geometry must be 16-byte aligned [rows, 4] fp32");
+  geometry_guard_kernel<<<blocks(S, 128), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      S, geometry, rows, source_ids, feature_ids, feature_w, feature_cos, feature_res, feature_nrm, joint_ids, joint_w,
+      joint_cos, joint_res, joint_nrm, changed, tolerance, out_ids, out_w, out_cos, out_res, out_nrm, chosen);
+  VB200_CHECK_LAUNCH("geometry_guard_kernel");
   return VB200_OK;
 }

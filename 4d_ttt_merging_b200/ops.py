@@ -129,13 +129,13 @@ def mass_bias_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 def similarity_topk(query: torch.Tensor, basis: torch.Tensor, k: int, *,
                     query_begin: torch.Tensor | None = None,
                     basis_begin: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Row top-k (k = 1 or 4) of bf16_round(query @ basis.T) on tcgen05, ties to the lower
+    """Row top-k (k = 1, 4 or 16) of bf16_round(query @ basis.T) on tcgen05, ties to the lower
     index.  query [R, D] and basis [Nb, D] are bf16 with D % 64 == 0.  With group tables
     (host int64 [G+1] each) query rows [qb[g], qb[g+1]) are ranked only against basis rows
     [bb[g], bb[g+1]).  Returns (values fp32 [R, k], indices int64 [R, k])."""
     C.require_cuda(query, "similarity_topk")
-    if k not in (1, 4):
-        raise ValueError("k must be 1 or 4")
+    if k not in (1, 4, 16):
+        raise ValueError("k must be 1, 4 or 16")
     if query.ndim != 2 or basis.ndim != 2 or query.shape[1] != basis.shape[1]:
         raise ValueError("query [R,D] and basis [N,D] are required")
     query = query.to(torch.bfloat16)

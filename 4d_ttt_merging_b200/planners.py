@@ -282,10 +282,55 @@ def _certified(cos, res, nrm, threshold: float) -> torch.Tensor:
     return (cos >= threshold) & (res <= (2.0 * (1.0 - threshold)) ** 0.5) & (nrm >= 0.80)
 
 
-def _fit_global(features, basis_ids, source_ids):
-    """The exact global route (_adaptive_fit_fused, sparse_convex.py:168-330, feature route with the
-    one-hot shortcut off): top-4 of every source over the whole basis, then the solve."""
+def _guarded_fit(features, geometry, query_ids, basis_list, weight: float, tolerance: float,
+                 query_begin=None, basis_begin=None):
+    """The Pareto-guarded geometry route for the queries against their basis rows (grouped like
+    similarity_topk): the tcgen05 top-16 feature shortlist, the joint re-rank
+    (vb200_geometry_shortlist), both fits (feature top-4 and joint set, each vb200_support_fit +
+    vb200_support_certificate) and the guard (vb200_geometry_guard); sparse_convex.py:502-531,
+    586-639 and 263-367.  -> (support ids [S,4], weights, cosine, residual, norm, chosen int32 [S])."""
     from .ops import row_gather
+    dev = features.device
+    S = query_ids.numel()
+    vals16, idx16 = similarity_topk(row_gather(features, query_ids), row_gather(features, basis_list), 16,
+                                    query_begin=query_begin, basis_begin=basis_begin)
+    qgeo = geometry.index_select(0, query_ids).contiguous()
+    bgeo = geometry.index_select(0, basis_list).contiguous()
+    fidx = torch.empty((S, 4), device=dev, dtype=torch.long)
+    jidx = torch.empty((S, 4), device=dev, dtype=torch.long)
+    changed = torch.empty(S, device=dev, dtype=torch.int32)
+    lib, stream = C.lib(), C.stream_of(dev)
+    C.check(lib.vb200_geometry_shortlist(vals16.data_ptr(), idx16.data_ptr(), S, 16, qgeo.data_ptr(), bgeo.data_ptr(),
+                                         basis_list.numel(), float(weight), fidx.data_ptr(), jidx.data_ptr(),
+                                         changed.data_ptr(), stream), "geometry_shortlist")
+    fids = basis_list.index_select(0, fidx.reshape(-1)).view(S, 4).contiguous()
+    jids = basis_list.index_select(0, jidx.reshape(-1)).view(S, 4).contiguous()
+    ffit = _feature_fit(features, query_ids, fids)
+    jfit = _feature_fit(features, query_ids, jids)
+    out_ids = torch.empty((S, 4), device=dev, dtype=torch.long)
+    out_w = torch.empty((S, 4), device=dev, dtype=torch.float32)
+    out_c, out_r, out_n = (torch.empty(S, device=dev, dtype=torch.float32) for _ in range(3))
+    chosen = torch.empty(S, device=dev, dtype=torch.int32)
+    src = query_ids.to(torch.int64).contiguous()
+    C.check(lib.vb200_geometry_guard(
+        S, geometry.data_ptr(), geometry.shape[0], src.data_ptr(), fids.data_ptr(), ffit[0].data_ptr(),
+        ffit[1].data_ptr(), ffit[2].data_ptr(), ffit[3].data_ptr(), jids.data_ptr(), jfit[0].data_ptr(),
+        jfit[1].data_ptr(), jfit[2].data_ptr(), jfit[3].data_ptr(), changed.data_ptr(), float(tolerance),
+        out_ids.data_ptr(), out_w.data_ptr(), out_c.data_ptr(), out_r.data_ptr(), out_n.data_ptr(), chosen.data_ptr(),
+        stream), "geometry_guard")
+    return out_ids, out_w, out_c, out_r, out_n, chosen
+
+
+def _fit_global(features, basis_ids, source_ids, guard=None):
+    """The exact global route (_adaptive_fit_fused, sparse_convex.py:168-330, one-hot shortcut
+    off): top-4 of every source over the whole basis, then the solve; with ``guard`` =
+    (geometry, weight, tolerance, counter) the guarded geometry route (:263-367)."""
+    from .ops import row_gather
+    if guard is not None:
+        geometry, weight, tolerance, counter = guard
+        out = _guarded_fit(features, geometry, source_ids, basis_ids, weight, tolerance)
+        counter.append(out[5])
+        return out[:5]
     q = row_gather(features, source_ids)
     b = row_gather(features, basis_ids)
     _, idx = similarity_topk(q, b, 4)
@@ -293,12 +338,15 @@ def _fit_global(features, basis_ids, source_ids):
     return (support,) + _feature_fit(features, source_ids, support)
 
 
-def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, threshold: float, source_ids):
+def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, threshold: float, source_ids,
+                        guard=None):
     """_adaptive_fit_temporal_local (sparse_convex.py:440-684), feature route: sources of frames
     [b, b + 8) (b = 1, 9, ...) take their top-4 among the basis of frame 0 and frames
     [max(1, b - 1), min(F - 1, b + 8)] (one grouped tcgen05 search for all groups), one fused
     solve, the certificate; uncertified rows (and reference-frame sources, which no group covers)
-    take the global route.  basis_ids / source_ids sorted ascending.
+    take the global route.  With ``guard`` = (geometry, weight, tolerance, counter) every search
+    is the Pareto-guarded geometry route (_guarded_fit); each launch's chosen flags are appended
+    to ``counter``.  basis_ids / source_ids sorted ascending.
     -> (support ids [S,4], weights, cosine, residual, reconstruction norm)."""
     from .ops import row_gather
     dev = features.device
@@ -329,7 +377,13 @@ def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, thres
     weights = torch.zeros((n, 4), device=dev, dtype=torch.float32)
     cos, res, nrm = (torch.zeros(n, device=dev, dtype=torch.float32) for _ in range(3))
     assigned = torch.zeros(n, device=dev, dtype=torch.bool)
-    if rows.numel():
+    if rows.numel() and guard is not None:
+        geometry, weight, tolerance, counter = guard
+        fit = _guarded_fit(features, geometry, source_ids[rows], local_basis, weight, tolerance,
+                           query_begin=torch.tensor(qb), basis_begin=torch.tensor(bb))
+        counter.append(fit[5])
+        chosen, fit = fit[0], fit[1:5]
+    elif rows.numel():
         _, idx = similarity_topk(row_gather(features, source_ids[rows]), row_gather(features, local_basis), 4,
                                  query_begin=torch.tensor(qb), basis_begin=torch.tensor(bb))
         chosen = local_basis[idx]
@@ -339,7 +393,7 @@ def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, thres
         assigned[rows] = True
     fallback = torch.nonzero(~(assigned & _certified(cos, res, nrm, threshold))).flatten()
     if fallback.numel():
-        gfit = _fit_global(features, basis_ids, source_ids[fallback])
+        gfit = _fit_global(features, basis_ids, source_ids[fallback], guard)
         support[fallback], weights[fallback] = gfit[0], gfit[1]
         cos[fallback], res[fallback], nrm[fallback] = gfit[2], gfit[3], gfit[4]
     return support, weights, cos, res, nrm
@@ -409,13 +463,20 @@ def build_ttt_protected_uniform_convex_plan(
     search (grouped tcgen05 top-4 per 8-frame group), the fused Gram + 32-step projected-gradient
     fit and its certificate, with the global route for uncertified sources; sources that still
     fail stay physical; the plan's CSR and masses on the device.  Supports come from the feature
-    route (support_geometry_weight = 0, the default); the geometry-aware support search and the
-    fixed-topology / fixed-dynamic-basis variants behind environment switches are not built."""
+    route (support_geometry_weight = 0, the default) or, with support_geometry_weight > 0 and a
+    guard tolerance (the released configuration: 0.01 and 0), from the Pareto-guarded geometry
+    route: a top-16 feature shortlist re-ranked by 4-D distance, both sets fitted, the joint set
+    kept only where it is no worse in feature space and strictly better in 4-D.  The joint-metric
+    route (a geometry weight without a guard tolerance) and the fixed-topology /
+    fixed-dynamic-basis variants behind environment switches are not built."""
     import os
     if tokens.shape[0] != 1 or max_support != 4:
         raise ValueError("protected TTT planner requires batch one and four supports")
-    if support_geometry_weight:
-        raise ValueError("this planner builds the feature-only support route (support_geometry_weight=0)")
+    if support_geometry_weight and support_geometry_guard_tolerance is None:
+        raise ValueError("the joint-metric support route (support_geometry_weight without a guard tolerance) "
+                         "is not built; pass support_geometry_guard_tolerance")
+    if support_geometry_guard_tolerance is not None and support_geometry_guard_tolerance < 0:
+        raise ValueError("the 4-D feature guard tolerance must be nonnegative")
     if os.environ.get("VGGT_TTT_FIXED_TOPOLOGY", "0") == "1" or os.environ.get("VGGT_TTT_FIXED_DYNAMIC_BASIS_PATH"):
         raise ValueError("the fixed-topology and fixed-dynamic-basis planner variants are not built")
     C.require_cuda(tokens, "build_ttt_protected_uniform_convex_plan")
@@ -437,6 +498,9 @@ def build_ttt_protected_uniform_convex_plan(
     patch_ids = (torch.arange(frames, device=dev)[:, None] * tokens_per_frame + patch_token_start
                  + torch.arange(patches, device=dev)[None]).flatten()
     features = row_normalize_bf16(tokens[0], patch_ids, eps=1e-8)
+    guard_counter: list[torch.Tensor] = []
+    guard = ((geometry.contiguous(), float(support_geometry_weight), float(support_geometry_guard_tolerance), [])
+             if support_geometry_weight else None)
 
     # protected uniform skeleton (sparse_convex.py:1371-1434)
     tab = ttt_skeleton_tables(frames, tuple(patch_hw))
@@ -476,7 +540,7 @@ def build_ttt_protected_uniform_convex_plan(
         event = proposal[:0]
         if budget and proposal.numel():
             efit = _fit_temporal_local(features, stable, frames=frames, patches=patches, threshold=threshold,
-                                       source_ids=proposal)
+                                       source_ids=proposal, guard=guard)
             cand = torch.nonzero(~_certified(efit[2], efit[3], efit[4], threshold)).flatten()
             if cand.numel() > budget:
                 priority = sensitivity.index_select(0, proposal.index_select(0, cand)) * efit[3].index_select(0, cand)
@@ -488,8 +552,10 @@ def build_ttt_protected_uniform_convex_plan(
     basis_mask = torch.zeros(patch_count, device=dev, dtype=torch.bool)
     basis_mask[basis] = True
     source = torch.nonzero(~basis_mask).flatten()
+    if guard is not None:  # the reported count covers the final fit, as the reference's does
+        guard = guard[:3] + (guard_counter,)
     support, weights, cos, res, nrm = _fit_temporal_local(features, basis, frames=frames, patches=patches,
-                                                          threshold=threshold, source_ids=source)
+                                                          threshold=threshold, source_ids=source, guard=guard)
     accepted = _certified(cos, res, nrm, threshold)
     rows = torch.nonzero(accepted).flatten()
     source_local = source.index_select(0, rows)
@@ -524,5 +590,10 @@ def build_ttt_protected_uniform_convex_plan(
                   "top1_pruning_enabled": bool(pruning), "protected_uniform_bases": int(stable.numel()),
                   "top1_pruned_uniform_bases": freed, "sensitive_event_budget": budget,
                   "sensitive_event_proposals": int(proposal.numel()), "sensitive_event_bases": int(event.numel()),
-                  "fit_failure_promotions": int((~accepted).sum()), "physical_patch_tokens": int(keep_local.numel())},
+                  "fit_failure_promotions": int((~accepted).sum()), "physical_patch_tokens": int(keep_local.numel()),
+                  "selection_geometry_weight": float(selection_geometry_weight),
+                  "support_geometry_weight": float(support_geometry_weight),
+                  "support_geometry_guard_tolerance": support_geometry_guard_tolerance,
+                  "geometry_guard_enabled": guard is not None,
+                  "geometry_guard_selected": int(sum(int(c.sum()) for c in guard_counter))},
     )

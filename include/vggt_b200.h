@@ -311,7 +311,9 @@ VB200_API int vb200_row_normalize_bf16(int dtype, const void* x, int64_t x_rows,
  * stores per-piece keys in the output rows and merges them in a second small kernel). */
 VB200_API int vb200_sim_topk_split(int64_t ctas, int n_tiles, int sms);
 
-/* Cosine-similarity GEMM with a fused running top-k epilogue (k = 1 or 4).
+/* Cosine-similarity GEMM with a fused running top-k epilogue (k = 1, 4 or 16; 16 is the
+ * semantic shortlist of the geometry-guarded route, sparse_convex.py:263-266, 506-508, and needs
+ * basis groups of at most 65,536 rows).
  * score[r, n] = bf16_round( <query[r], basis[n]> ) over D channels (fp32 accumulation on
  * tcgen05), ranked per row; ties keep the lower basis index.  With groups: query rows
  * [q_begin[g], q_begin[g+1]) are matched only against basis rows [b_begin[g], b_begin[g+1]);
@@ -361,6 +363,31 @@ VB200_API int vb200_support_certificate(int dtype, const void* feat, int64_t row
                                         const int64_t* src_rows, const int64_t* parent_rows, const float* alpha,
                                         int64_t S, int64_t D, float* cosine, float* residual, float* recon_norm,
                                         void* stream);
+/* The geometry-guarded support route of the released planner (support_geometry_weight > 0 with
+ * a guard tolerance; sparse_convex.py:502-531, 586-639 (temporal-local) and 263-367 (global)).
+ *
+ * vb200_geometry_shortlist: per source row, from its top-k feature shortlist (values / indices
+ * of vb200_sim_topk with k = 16: bf16 scores best first, indices into the basis rows, -1 for
+ * empty slots) the joint value score - weight * |g_s - g_c|^2 (fp32), its top-4 shortlist
+ * positions (ties to the lower position) reordered by feature score (stable), written as basis
+ * indices to joint_ids [S, 4]; feature_ids [S, 4] = the first four shortlist indices; changed[s]
+ * = 1 where the two differ.  query_geo [S, 4] and basis_geo [Nb, 4] fp32, 16-byte aligned. */
+VB200_API int vb200_geometry_shortlist(const float* values, const int64_t* indices, int64_t S, int k,
+                                       const float* query_geo, const float* basis_geo, int64_t Nb, float weight,
+                                       int64_t* feature_ids, int64_t* joint_ids, int32_t* changed, void* stream);
+/* vb200_geometry_guard: given both fits (ids [S, 4] into the rows of geometry [rows, 4], weights
+ * [S, 4], cosine / residual / reconstruction norm [S] from vb200_support_fit and
+ * vb200_support_certificate), keep the joint fit where changed[s] and joint cosine + tolerance >=
+ * feature cosine and joint residual <= feature residual + tolerance and the joint 4-D residual
+ * |g_s - sum_c w_c g_c| is strictly smaller; else the feature fit.  Writes the chosen ids,
+ * weights and certificate, and chosen[s] (0 / 1). */
+VB200_API int vb200_geometry_guard(int64_t S, const float* geometry, int64_t rows, const int64_t* source_ids,
+                                   const int64_t* feature_ids, const float* feature_w, const float* feature_cos,
+                                   const float* feature_res, const float* feature_nrm, const int64_t* joint_ids,
+                                   const float* joint_w, const float* joint_cos, const float* joint_res,
+                                   const float* joint_nrm, const int32_t* changed, float tolerance, int64_t* out_ids,
+                                   float* out_w, float* out_cos, float* out_res, float* out_nrm, int32_t* chosen,
+                                   void* stream);
 /* out[q] = max over t of the fp32 dot product <feat[query[q]], feat[targets[q, t]]> (targets
  * [Q, n_targets] int64, -1 = no target; -inf when a query has none): the top-1 cosine that
  * prunes redundant uniform anchors in the released planner's protected skeleton

@@ -69,6 +69,44 @@ def test_against_oracle(pkg, oracle, cuda_device, k, shape):
     assert pkg.device_error_flags() == 0
 
 
+@pytest.mark.parametrize("shape", [(130, 300, 128), (1000, 2100, 1024), (257, 513, 192)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_shortlist16_against_oracle(pkg, oracle, cuda_device, shape):
+    """k = 16, the geometry-guarded route's shortlist (sparse_convex.py:263-266, 506-508)."""
+    R, Nb, D = shape
+    rng = np.random.default_rng(R * 3 + Nb + D)
+    q = rng.standard_normal((R, D)).astype(np.float32)
+    b = rng.standard_normal((Nb, D)).astype(np.float32)
+    q = oracle.round_bf16(q / np.linalg.norm(q, axis=1, keepdims=True))
+    b = oracle.round_bf16(b / np.linalg.norm(b, axis=1, keepdims=True))
+    v, i = pkg.similarity_topk(_bf16(q, cuda_device), _bf16(b, cuda_device), 16)
+    assert v.shape == (R, 16) and i.shape == (R, 16)
+    _check_topk(oracle, q, b, to_np(v), i.cpu().numpy(), 16)
+    # the first four are the top-4 search's picks
+    v4, i4 = pkg.similarity_topk(_bf16(q, cuda_device), _bf16(b, cuda_device), 4)
+    assert torch.equal(i[:, :4], i4) and torch.equal(v[:, :4], v4)
+    assert pkg.device_error_flags() == 0
+
+
+def test_shortlist16_small_basis_and_groups(pkg, oracle, cuda_device):
+    """Groups with fewer than 16 basis rows leave the remaining slots -inf / -1."""
+    rng = np.random.default_rng(11)
+    D = 128
+    qb, bb = [0, 40, 100], [0, 5, 300]
+    q = oracle.round_bf16(rng.standard_normal((100, D)).astype(np.float32) / 11)
+    b = oracle.round_bf16(rng.standard_normal((300, D)).astype(np.float32) / 11)
+    v, i = pkg.similarity_topk(_bf16(q, cuda_device), _bf16(b, cuda_device), 16,
+                               query_begin=torch.tensor(qb), basis_begin=torch.tensor(bb))
+    v, i = to_np(v), i.cpu().numpy()
+    assert np.all(i[:40, 5:] == -1) and np.all(np.isneginf(v[:40, 5:]))
+    assert np.all((i[:40, :5] >= 0) & (i[:40, :5] < 5)) and np.all((i[40:] >= 5) & (i[40:] < 300))
+    scores = oracle.topk_scores(q, b)
+    np.testing.assert_array_equal(np.sort(i[:40, :5], axis=1), np.tile(np.arange(5), (40, 1)))
+    _check_topk(oracle, q[40:], b[5:], v[40:], i[40:] - 5, 16)
+    assert np.all(np.diff(v[:40, :5], axis=1) <= 0) and np.all(np.isfinite(scores))
+    assert pkg.device_error_flags() == 0
+
+
 def test_groups(pkg, oracle, cuda_device):
     rng = np.random.default_rng(7)
     D = 256
