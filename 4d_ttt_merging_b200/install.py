@@ -9,6 +9,8 @@ blocks call, in the manner of the reference's own ``fast_affine.install``
 * ``vggt_omega.models.sparse_convex_kernels.streaming_top4`` /
   ``four_support_projected_gradient`` / ``four_support_active_set`` and their aliases in
   ``vggt_omega.models.sparse_convex``
+* ``vggt_omega.models.sparse_convex.build_ttt_protected_uniform_convex_plan`` (the released
+  planner, called by the aggregator's global branch, aggregator.py:922)
 * ``vggt_omega.models.token_merging.TokenPlan`` / ``WeightedBilinearTokenPlan`` /
   ``deterministic_weighted_normalizer`` / ``build_fastvggt_plan`` and their aliases in the
   planner modules that imported them by name.
@@ -31,6 +33,9 @@ REPLACEMENTS = {
         "streaming_top4": ops.streaming_top4,
         "four_support_projected_gradient": ops.four_support_projected_gradient,
         "four_support_active_set": ops.four_support_active_set,
+    },
+    "vggt_omega.models.sparse_convex": {
+        "build_ttt_protected_uniform_convex_plan": planners.build_ttt_protected_uniform_convex_plan,
     },
     "vggt_omega.models.token_merging": {
         "TokenPlan": token_plan.TokenPlan,

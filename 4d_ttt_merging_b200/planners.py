@@ -388,6 +388,7 @@ def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, thres
                                  query_begin=torch.tensor(qb), basis_begin=torch.tensor(bb))
         chosen = local_basis[idx]
         fit = _feature_fit(features, source_ids[rows], chosen)
+    if rows.numel():
         support[rows], weights[rows] = chosen, fit[0]
         cos[rows], res[rows], nrm[rows] = fit[1], fit[2], fit[3]
         assigned[rows] = True

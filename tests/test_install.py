@@ -8,8 +8,11 @@ from pathlib import Path
 
 import pytest
 
-# a reference checkout named by REFERENCE_ROOT (unset, or no checkout there: the test skips)
-REFERENCE = Path(os.environ["REFERENCE_ROOT"]) if os.environ.get("REFERENCE_ROOT") else None
+# a reference checkout named by REFERENCE_ROOT, else the pip install under baseline/_ref
+# (neither present: the test skips)
+_INSTALLED = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
+REFERENCE = (Path(os.environ["REFERENCE_ROOT"]) if os.environ.get("REFERENCE_ROOT")
+             else _INSTALLED if (_INSTALLED / "vggt_omega").exists() else None)
 
 
 @pytest.mark.skipif(REFERENCE is None or not (REFERENCE / "vggt_omega").exists(),
@@ -26,6 +29,9 @@ def test_install_patches_reference(pkg):
         assert sc.WeightedBilinearTokenPlan is pkg.WeightedBilinearTokenPlan
         assert sc.four_support_projected_gradient is pkg.four_support_projected_gradient
         assert "vggt_omega.models.sparse_convex_kernels.streaming_top4" in patched
+        agg = sys.modules["vggt_omega.models.aggregator"]
+        assert sc.build_ttt_protected_uniform_convex_plan is pkg.build_ttt_protected_uniform_convex_plan
+        assert agg.build_ttt_protected_uniform_convex_plan is pkg.build_ttt_protected_uniform_convex_plan
     finally:
         pkg.uninstall()
     assert sys.modules["vggt_omega.models.mass_bias_attention"].mass_bias_attention is not pkg.mass_bias_attention
