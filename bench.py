@@ -39,6 +39,12 @@ import time
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
+# the reference's own package, pip-installed (git-ignored; travels with the tree to the GPU box)
+REF_INSTALL = REPO / "baseline" / "_ref"
+# the settings of the reference's configs/ttt_best.py (METHOD_ENV) that its model code reads
+TTT_BEST_ENV = {"VGGT_TTT_REUSE_PLAN": "0", "VGGT_TTT_FIXED_TOPOLOGY": "0", "VGGT_TTT_LOCAL_SUPPORT_SEARCH": "1",
+                "VGGT_TTT_FIT_CHUNK": "4096", "VGGT_TTT_LOCAL_SOLVER": "projected", "VGGT_TRITON_ACTIVE_SET": "0",
+                "VGGT_TRITON_MASS_BIAS_ATTENTION": "1"}
 sys.path.insert(0, str(REPO))
 
 FRAMES = 32
@@ -398,6 +404,154 @@ def long_sequence(pkg, attn, dev, world: int, rank: int, steps: int, flush) -> d
 REFERENCE_MAX_STEPS = 3  # each reference step is seconds of CPU work: the run stays within a few minutes
 
 
+def full_forward_config3(pkg, dev, steps: int = 3, warmup: int = 2, frames: int = 16, size: int = 512) -> dict:
+    """Config 3: the reference's own VGGTOmega() (the pip install under baseline/_ref) with
+    random-init weights and bf16 autocast, token merging per configs/ttt_best.py: the released
+    planner (threshold 0.9, four supports, top-1 pruning off, event ratio 0.01, selection and
+    support geometry weight 0.01, guard tolerance 0), compact Q/K/V on all global layers but
+    8, 10, 11, 12, on `frames` frames of size x size uniform [0, 1] pixels.  The TTT pre-pass
+    outputs the planner takes (labels, sensitivity, 4-D geometry) are seeded synthetic inputs.
+    The same forward is timed twice with CUDA events: the stock reference (its Triton kernels)
+    and with install() routing the global layers (planner, compaction, mass-bias attention,
+    restore) through this library.  Reported per arm: frames/s of the whole forward, and the
+    share of the forward spent in the 19 global layers (planning included), in their planner
+    calls and in their attention modules."""
+    import torch
+    if not (REF_INSTALL / "vggt_omega").exists():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    if str(REF_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REF_INSTALL))
+    for k, v in TTT_BEST_ENV.items():
+        os.environ.setdefault(k, v)
+    import vggt_omega.models.aggregator as agg_mod
+    from vggt_omega.models.vggt_omega import VGGTOmega
+    torch.manual_seed(0)
+    with torch.device(dev):  # initialise on the GPU; a few buffers are built on the CPU regardless
+        model = VGGTOmega().eval()
+    model.to(dev)
+    agg = model.aggregator
+    ph = size // 16
+    patches = frames * ph * ph
+    gen = torch.Generator(device="cpu").manual_seed(3)
+    labels = (torch.rand(patches, generator=gen) < 0.08).long()
+    labels[torch.rand(patches, generator=gen) < 0.02] = 2
+    labels[:ph * ph] = 0
+    sensitivity = torch.rand(patches, generator=gen)
+    base = torch.randn(ph * ph, 3, generator=gen)
+    xyz = base[None] + 0.3 * torch.randn(frames, ph * ph, 3, generator=gen)
+    t = torch.linspace(-1, 1, frames)[:, None, None].expand(-1, ph * ph, 1)
+    geometry = torch.cat([xyz, t], -1).reshape(patches, 4)
+    agg.set_sparse_convex(enabled=True, threshold=0.90, planner="ttt_protected_uniform_convex", max_support=4,
+                          qkv_global_layers=tuple(l for l in range(19) if l not in {8, 10, 11, 12}),
+                          dense_global_layers=())
+    agg.set_sparse_convex_ttt_top1_pruning(False)
+    agg.set_sparse_convex_ttt_sensitive_event_ratio(0.01)
+    agg.set_sparse_convex_4d(geometry.to(dev), global_layers=tuple(range(19)), selection_weight=0.01,
+                             support_weight=0.01, guard_tolerance=0.0)
+    agg.set_sparse_convex_ttt_partition(labels.to(dev), sensitivity.to(dev))
+    images = torch.rand(1, frames, 3, size, size, device=dev, generator=torch.Generator(device=dev).manual_seed(4))
+    global_blocks = [agg.inter_frame_blocks[i] for i, kind in enumerate(agg.inter_frame_attention_types)
+                     if kind == "global"]
+
+    def run_arm():
+        events = {"global": [], "plan": [], "attn": []}
+
+        def record(name, fn):
+            def wrapped(*a, **kw):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                out = fn(*a, **kw)
+                e1.record()
+                events[name].append((e0, e1))
+                return out
+            return wrapped
+
+        run_block = agg._run_inter_frame_attention_block
+        planner = agg_mod.build_ttt_protected_uniform_convex_plan
+
+        def block(*a, **kw):
+            kind = a[6] if len(a) > 6 else kw.get("attention_type")
+            return record("global", run_block)(*a, **kw) if kind == "global" else run_block(*a, **kw)
+
+        started = {}
+
+        def attn_start(module, args):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            started[id(module)] = e
+
+        def attn_end(module, args, output):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            events["attn"].append((started.pop(id(module)), e))
+
+        hooks = []
+        for b in global_blocks:
+            hooks.append(b.attn.register_forward_pre_hook(attn_start))
+            hooks.append(b.attn.register_forward_hook(attn_end))
+        agg._run_inter_frame_attention_block = block
+        agg_mod.build_ttt_protected_uniform_convex_plan = record("plan", planner)
+        try:
+            with torch.no_grad():
+                for _ in range(warmup):
+                    out = model(images)
+                torch.cuda.synchronize()
+                for v in events.values():
+                    v.clear()
+                ms = []
+                for _ in range(steps):
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    out = model(images)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ms.append(e0.elapsed_time(e1))
+        finally:
+            del agg._run_inter_frame_attention_block
+            agg_mod.build_ttt_protected_uniform_convex_plan = planner
+            for h in hooks:
+                h.remove()
+        per_step = lambda name: sum(a.elapsed_time(b) for a, b in events[name]) / steps
+        fwd = statistics.median(ms)
+        stats = agg.sparse_convex_last_plan_stats
+        return out, {
+            "frames_per_s": frames / (fwd / 1e3), "forward_ms": fwd,
+            "global_layers_ms": per_step("global"), "global_share": per_step("global") / statistics.mean(ms),
+            "planner_ms": per_step("plan"), "global_attention_module_ms": per_step("attn"),
+            "global_attention_module_share": per_step("attn") / statistics.mean(ms),
+            "mean_kept_tokens": statistics.mean(s["kept_tokens"] for s in stats),
+            "original_tokens": stats[0]["original_tokens"] if stats else None,
+        }
+
+    ref_out, ref_stats = run_arm()
+    pkg.install()
+    try:
+        our_out, our_stats = run_arm()
+    finally:
+        pkg.uninstall()
+
+    def agree(a, b):
+        a, b = a.float().flatten(), b.float().flatten()
+        return {"cosine": float(torch.nn.functional.cosine_similarity(a, b, dim=0)),
+                "max_rel_err": float((a - b).abs().max() / b.abs().max().clamp_min(1e-12))}
+
+    result = {
+        "workload": f"config 3: VGGTOmega() forward, random init, bf16 autocast, {frames} frames of {size}x{size}, "
+                    "sparse-convex merging per configs/ttt_best.py (released planner, geometry-guarded supports); "
+                    "seeded synthetic TTT labels / sensitivity / geometry",
+        "steps": steps, "warmup": warmup,
+        "reference": ref_stats, "ours": our_stats,
+        "speedup_forward": ref_stats["forward_ms"] / our_stats["forward_ms"],
+        "output_agreement": {k: agree(our_out[k], ref_out[k]) for k in ("camera_and_register_tokens", "depth",
+                                                                          "pose_enc")},
+        "timing": "CUDA events around each forward (median of steps) and around every global layer, planner "
+                  "call and global attention module",
+    }
+    del model, ref_out, our_out
+    torch.cuda.empty_cache()
+    return result
+
+
 def run_reference(args) -> None:
     """The reference arm: its PyTorch CPU path on the GPU arm's config, metric and unit, on
     rank 0 only (other ranks exit without work).  Each step is the whole config-2 step; at
@@ -618,6 +772,11 @@ def run_ours(args) -> None:
                                                                 max(3, min(args.steps, 10)), flush)
     if world == 1:
         line["components"]["projection_config5"] = projection_stress(pkg, dev, hbm_peak)
+        if not args.no_config3:
+            try:
+                line["components"]["full_forward_config3"] = full_forward_config3(pkg, dev)
+            except Exception as e:  # the reference model path must not cost the headline line
+                line["components"]["full_forward_config3"] = {"error": f"{type(e).__name__}: {e}"[:500]}
     else:
         line["components"]["projection_config5_sharded"] = projection_sharded(pkg, dev, world, rank, local_rank,
                                                                               hbm_peak)
@@ -644,10 +803,19 @@ def main() -> None:
     ap.add_argument("--projection-tokens", type=int, default=1 << 20,
                     help="tokens of the --projection-only case (merged = tokens / 16; smaller for ncu captures)")
     ap.add_argument("--projection-reps", type=int, default=5, help="timed repetitions of --projection-only")
+    ap.add_argument("--config3-only", action="store_true",
+                    help="run only the config-3 full-forward comparison on one GPU and print its JSON")
+    ap.add_argument("--no-config3", action="store_true", help="skip the config-3 component of the N=1 line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    if args.projection_only:
+    if args.config3_only:
+        import torch
+        pkg = importlib.import_module("4d_ttt_merging_b200")
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        print(json.dumps(full_forward_config3(pkg, dev, steps=max(1, min(args.steps, 5)))), flush=True)
+    elif args.projection_only:
         import torch
         pkg = importlib.import_module("4d_ttt_merging_b200")
         dev = torch.device("cuda", 0)
