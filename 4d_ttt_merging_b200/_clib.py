@@ -63,6 +63,7 @@ _SIGNATURES = {
          _c_i64, _c_i64, _c_i64, _c_vp, _c_size, _c_vp],
     ),
     "vb200_proj_scatter_workspace_size": (_c_size, [_c_i64, _c_i64, _c_i64]),
+    "vb200_qkv_head_stats": (_c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_float, _c_vp, _c_size, _c_vp]),
     "vb200_geometry_shortlist": (
         _c_int, [_c_vp, _c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_i64, _c_float, _c_vp, _c_vp, _c_vp, _c_vp],
     ),

@@ -1995,12 +1995,17 @@ int compact_qkv_impl(int dtype, const void* qkv, int64_t rows, int64_t xs, int64
   if ((rc = check_rows(dtype, qkv, xs, 3 * C, "compact_qkv input")) != VB200_OK) return rc;
   if ((rc = check_rows(dtype, out, os, 3 * C, "compact_qkv output")) != VB200_OK) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  VB200_REQUIRE((pool_mask & ~(7 | VB200_STATS_READY)) == 0, "compact_qkv: bad pool_mask %d", pool_mask);
+  const bool stats_ready = (pool_mask & VB200_STATS_READY) != 0;
+  pool_mask &= 7;
   float2* stats = nullptr;
   if (ln_weight != nullptr) {
     const size_t need = vb200_compact_qkv_workspace_size(rows, C);
     VB200_REQUIRE(workspace != nullptr && workspace_bytes >= need,
                   "compact_qkv: workspace of %zu bytes required (got %zu)", need, workspace_bytes);
     stats = static_cast<float2*>(workspace);
+  }
+  if (ln_weight != nullptr && !stats_ready) {
 #define VB200_STATS(T)                                                                            \
   head_stats_kernel<T><<<row_blocks(rows), kWarpsPerBlock * 32, 0, st>>>(static_cast<const T*>(qkv), rows, \
                                                                        xs, static_cast<int>(C), eps, stats)
@@ -2058,6 +2063,30 @@ int compact_qkv_impl(int dtype, const void* qkv, int64_t rows, int64_t xs, int64
   return VB200_OK;
 }
 }  // namespace
+
+extern "C" int vb200_qkv_head_stats(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C, float eps,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  VB200_REQUIRE(dtype == VB200_BF16 || dtype == VB200_F16, "qkv_head_stats: dtype must be bf16 or fp16 (got %d)",
+                dtype);
+  VB200_REQUIRE(rows >= 0 && C > 0 && C % 256 == 0, "qkv_head_stats: bad sizes");
+  if (rows == 0) return VB200_OK;
+  VB200_REQUIRE(qkv != nullptr, "qkv_head_stats: null pointer");
+  const size_t need = vb200_compact_qkv_workspace_size(rows, C);
+  VB200_REQUIRE(workspace != nullptr && workspace_bytes >= need,
+                "qkv_head_stats: workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+  int rc;
+  if ((rc = check_rows(dtype, qkv, xs, 3 * C, "qkv_head_stats input")) != VB200_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float2* stats = static_cast<float2*>(workspace);
+  if (dtype == VB200_BF16)
+    head_stats_kernel<__nv_bfloat16><<<row_blocks(rows), kWarpsPerBlock * 32, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(qkv), rows, xs, static_cast<int>(C), eps, stats);
+  else
+    head_stats_kernel<__half><<<row_blocks(rows), kWarpsPerBlock * 32, 0, st>>>(static_cast<const __half*>(qkv), rows,
+                                                                                  xs, static_cast<int>(C), eps, stats);
+  VB200_CHECK_LAUNCH("head_stats_kernel");
+  return VB200_OK;
+}
 
 extern "C" int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t xs, int64_t C,
                                  const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,

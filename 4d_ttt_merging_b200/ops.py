@@ -35,6 +35,7 @@ __all__ = [
     "row_normalize_bf16",
     "row_gather",
     "head_layernorm",
+    "qkv_head_stats",
     "PlanCSR",
     "build_plan_csr",
 ]
@@ -311,6 +312,22 @@ def row_normalize_bf16(x: torch.Tensor, rows: torch.Tensor | None = None, eps: f
         out.data_ptr(), out.stride(0), C.stream_of(x.device))
     C.check(rc, "row_normalize_bf16")
     return out
+
+
+def qkv_head_stats(qkv: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """Per-head LayerNorm statistics of the q and k blocks of a [N, 3C] (or [1, N, 3C]) qkv
+    buffer (``vb200_qkv_head_stats``), as a workspace for ``compact_qkv(..., stats=...)``."""
+    x = qkv[0] if qkv.ndim == 3 else qkv
+    C.require_cuda(x, "qkv_head_stats")
+    if x.stride(-1) != 1 or x.data_ptr() % 16 or (x.stride(0) * x.element_size()) % 16:
+        x = x.contiguous()
+    c = x.shape[1] // 3
+    lib = C.lib()
+    ws_bytes = lib.vb200_compact_qkv_workspace_size(x.shape[0], c)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+    C.check(lib.vb200_qkv_head_stats(C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), c, float(eps),
+                                     ws.data_ptr(), ws_bytes, C.stream_of(x.device)), "qkv_head_stats")
+    return ws
 
 
 def head_layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:

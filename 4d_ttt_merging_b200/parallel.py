@@ -265,9 +265,14 @@ class ShardedGlobalBlock:
 
     @torch.no_grad()
     def step(self, tokens: torch.Tensor) -> torch.Tensor:
-        from .ops import mass_bias_attention
+        from .ops import mass_bias_attention, qkv_head_stats
         attn = self.attn
         H = attn.num_heads
+        if self._ln is None and attn.q_norm is not None:
+            from .attention_block import _ln_params
+            self._ln = _ln_params(attn.q_norm, attn.k_norm)
+        lw, lb, eps = self._ln if self._ln is not None else (None, None, 1e-5)
+        stats = None
         # The plan (a chain of small kernels) and the qkv GEMM both read only the tokens: the
         # GEMM runs on a side stream, concurrently with the plan, and joins before compaction.
         cur = torch.cuda.current_stream(tokens.device) if tokens.is_cuda else None
@@ -278,6 +283,10 @@ class ShardedGlobalBlock:
             with torch.cuda.stream(self._side):
                 e = self._ev("qkv_gemm")
                 qkv = attn.qkv_projection(tokens)
+                # the q/k LayerNorm statistics need only the GEMM's output: computed here, under
+                # the plan's kernels, instead of at the head of the compaction
+                if lw is not None:
+                    stats = qkv_head_stats(qkv, eps)
                 self._end(e)
         e = self._ev("merge")
         plan = self.plan(tokens)
@@ -289,13 +298,11 @@ class ShardedGlobalBlock:
         else:
             cur.wait_stream(self._side)
             qkv.record_stream(cur)
+            if stats is not None:
+                stats.record_stream(cur)
         B, N, C3 = qkv.shape
         C = C3 // 3
         e = self._ev("compact")
-        if self._ln is None and attn.q_norm is not None:
-            from .attention_block import _ln_params
-            self._ln = _ln_params(attn.q_norm, attn.k_norm)
-        lw, lb, eps = self._ln if self._ln is not None else (None, None, 1e-5)
         xchg = self._exchange(plan.kept_tokens, C, qkv.dtype, qkv.device) if self.world > 1 else None
         log_mass = plan.key_log_mass.reshape(-1)
         if xchg is not None:
@@ -304,13 +311,13 @@ class ShardedGlobalBlock:
             xchg.log_mass.copy_(log_mass)
             xchg.begin()
             packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111, out=xchg.packed,
-                                      kv_peers=xchg.kv_peers())
+                                      kv_peers=xchg.kv_peers(), stats=stats)
             self._end(e)
             e = self._ev("all_gather")
             kv, log_mass = xchg.finish()
             self._end(e)
         else:
-            packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111)  # [K_local, 3C]: q | k | v
+            packed = plan.compact_qkv(qkv[0], lw, lb, eps, pool_mask=0b111, stats=stats)  # [K_local, 3C]: q|k|v
             self._end(e)
             kv = packed[:, C:]
             if self.world > 1:

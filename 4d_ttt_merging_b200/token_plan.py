@@ -231,7 +231,8 @@ class WeightedBilinearTokenPlan:
 
     def compact_qkv(self, qkv: torch.Tensor, ln_weight: torch.Tensor | None = None,
                     ln_bias: torch.Tensor | None = None, eps: float = 1e-5,
-                    pool_mask: int = 0b111, out: torch.Tensor | None = None, kv_peers=None) -> torch.Tensor:
+                    pool_mask: int = 0b111, out: torch.Tensor | None = None, kv_peers=None,
+                    stats: torch.Tensor | None = None) -> torch.Tensor:
         """Fused q/k LayerNorm + Q||K||V compaction of a [N, 3C] (or [1, N, 3C]) qkv buffer in
         one kernel (``vb200_compact_qkv``); returns [M, 3C].  ``ln_weight`` / ``ln_bias`` are
         [2, 64] fp32 (q then k) or None.  Bit t of ``pool_mask`` pools tensor t (q, k, v);
@@ -240,7 +241,10 @@ class WeightedBilinearTokenPlan:
         GPUs read.  ``kv_peers`` = (pointer array, world, row0, row_stride[, multicast]): also
         store the k|v part of every merged row into those peer-mapped [rows, 2C] buffers at row
         row0 + j (``vb200_compact_qkv_peer``, the fused all-gather of the sharded layer); with
-        multicast set the array holds one multicast address covering every rank's buffer."""
+        multicast set the array holds one multicast address covering every rank's buffer.
+        ``stats``: the q/k LayerNorm statistics of this qkv already computed by
+        ``ops.qkv_head_stats`` (e.g. on the qkv GEMM's stream); the call then runs the compaction
+        alone."""
         x = qkv[0] if qkv.ndim == 3 else qkv
         C.require_cuda(x, "compact_qkv")
         if x.stride(-1) != 1 or x.data_ptr() % 16 or (x.stride(0) * x.element_size()) % 16:
@@ -259,7 +263,13 @@ class WeightedBilinearTokenPlan:
         csr = self.csr
         lib = C.lib()
         ws_bytes = lib.vb200_compact_qkv_workspace_size(x.shape[0], c) if lw is not None else 0
-        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+        if stats is not None and lw is not None:
+            if stats.numel() * stats.element_size() < ws_bytes or stats.device != x.device:
+                raise ValueError("compact_qkv: stats must come from ops.qkv_head_stats of this qkv")
+            ws = stats
+            pool_mask = int(pool_mask) | 8  # VB200_STATS_READY
+        else:
+            ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
         args = (C.dtype_code(x.dtype), x.data_ptr(), x.shape[0], x.stride(0), c, C.ptr(lw), C.ptr(lb), float(eps),
                 self._keep_flat.data_ptr(), self.kept_tokens, csr.corners, csr.seg_offsets.data_ptr(),
                 csr.entry_src.data_ptr(), csr.entry_w.data_ptr(), self._normalizer_flat.data_ptr(), int(pool_mask),

@@ -198,8 +198,17 @@ VB200_API size_t vb200_proj_scatter_workspace_size(int64_t M, int64_t n_entries,
  * Replaces the q_norm / k_norm + compact / compact_key sequence of
  * vggt_omega/models/layers/attention.py:337-374 (token_merging.py:343-376).
  * workspace: vb200_compact_qkv_workspace_size(rows, C) bytes (per-head LayerNorm statistics of
- * every row), 256-byte aligned; unused when ln_weight is NULL. */
+ * every row), 256-byte aligned; unused when ln_weight is NULL.  pool_mask | VB200_STATS_READY:
+ * the workspace already holds those statistics, written by vb200_qkv_head_stats for the same
+ * qkv and eps (e.g. on the stream of the qkv GEMM, concurrently with the plan); the call then
+ * launches the compaction alone. */
+#define VB200_STATS_READY 8
 VB200_API size_t vb200_compact_qkv_workspace_size(int64_t rows, int64_t C);
+/* The per-head LayerNorm statistics (mean, 1 / sqrt(var + eps)) of the q and k blocks of every
+ * qkv row, into a workspace of vb200_compact_qkv_workspace_size(rows, C) bytes: the first step of
+ * vb200_compact_qkv on its own, so that it can run as soon as the qkv GEMM has finished. */
+VB200_API int vb200_qkv_head_stats(int dtype, const void* qkv, int64_t rows, int64_t row_stride, int64_t C, float eps,
+                                   void* workspace, size_t workspace_bytes, void* stream);
 VB200_API int vb200_compact_qkv(int dtype, const void* qkv, int64_t rows, int64_t row_stride, int64_t C,
                                 const float* ln_weight, const float* ln_bias, float eps, const int64_t* keep,
                                 int64_t M, int64_t corners, const int32_t* seg_offsets,

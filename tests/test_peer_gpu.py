@@ -73,6 +73,13 @@ def test_compact_qkv_peer_writes_every_rank(pkg, cuda_device, dim):
     got = plan.compact_qkv(qkv, lw, lb, 1e-6, out=out, kv_peers=(ptrs, world, row0, stride))
     torch.cuda.synchronize()
     assert torch.equal(got, ref)
+    # the statistics computed ahead on another stream (vb200_qkv_head_stats) give the same rows
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        stats = pkg.ops.qkv_head_stats(qkv, 1e-6)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    assert torch.equal(plan.compact_qkv(qkv, lw, lb, 1e-6, stats=stats), ref)
     for b in bufs:
         assert torch.equal(b[row0:row0 + M, :2 * dim], ref[:, dim:])
         assert torch.all(b[:row0] == sentinel) and torch.all(b[row0 + M:] == sentinel)
