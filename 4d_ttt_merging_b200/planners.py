@@ -400,6 +400,65 @@ def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, thres
     return support, weights, cos, res, nrm
 
 
+class _EventTables:
+    """The feature-independent part of the TTT event-base selection for one clip: the sensitive
+    patches, their time / xyz bins, the bins' mean geometry and the score terms that do not
+    depend on the features, the bins kept when there are more than ``amount``, and the fill
+    count.  The global layers of one forward pass the same labels, sensitivity and geometry, so
+    the planner computes these once per clip (the last few clips are kept) and only the feature
+    terms per layer."""
+
+    _cache: list = []
+    _KEEP = 4
+
+    def __init__(self, geometry, labels, sensitivity, excluded, patches: int, amount: int, geometry_weight: float):
+        self.inputs = (geometry.clone(), labels.clone(), sensitivity.clone(), excluded.clone())
+        self.patches, self.amount, self.weight = patches, amount, geometry_weight
+        ids = torch.nonzero((labels == 1) & ~excluded).flatten()
+        self.ids = ids
+        self.n = ids.numel()
+        if amount <= 0 or self.n == 0:
+            return
+        geo = geometry.index_select(0, ids)
+        xyz = torch.floor((geo[:, :3] + 4.0) / 0.5).long().clamp(0, 31)
+        time_bin = (ids // patches) // 4
+        code = ((time_bin * 37 + xyz[:, 0]) * 37 + xyz[:, 1]) * 37 + xyz[:, 2]
+        _, inverse = torch.unique(code, return_inverse=True)
+        groups = int(inverse.max()) + 1
+        counts = torch.bincount(inverse, minlength=groups)
+        order = inverse.argsort(stable=True)
+        center_g = torch.segment_reduce(geo.index_select(0, order), "mean", lengths=counts)
+        sens = sensitivity.index_select(0, ids)
+        self.inverse, self.groups, self.counts, self.order = inverse, groups, counts, order
+        self.geo_term = geometry_weight * (geo - center_g.index_select(0, inverse)).square().sum(-1)
+        self.sens_term = 0.005 * sens
+        self.sens = sens
+        self.select = None
+        if groups > amount:
+            group_score = torch.segment_reduce(sens.index_select(0, order), "mean", lengths=counts) * counts.float().sqrt()
+            self.select = group_score.topk(amount).indices
+        self.fill = min(amount - groups, self.n - groups) if groups < amount else 0
+
+    def matches(self, geometry, labels, sensitivity, excluded, patches, amount, geometry_weight) -> bool:
+        g, l, s, e = self.inputs
+        if (patches, amount, geometry_weight) != (self.patches, self.amount, self.weight):
+            return False
+        if g.shape != geometry.shape or l.shape != labels.shape or s.shape != sensitivity.shape \
+                or e.shape != excluded.shape or g.device != geometry.device:
+            return False
+        same = ((g != geometry).any() | (l != labels).any() | (s != sensitivity).any() | (e != excluded).any())
+        return not bool(same)
+
+    @classmethod
+    def get(cls, *args):
+        for t in cls._cache:
+            if t.matches(*args):
+                return t
+        t = cls(*args)
+        cls._cache = [t] + cls._cache[: cls._KEEP - 1]
+        return t
+
+
 def _ttt_event_bases(features, geometry, labels, sensitivity, excluded, *, patches: int, amount: int,
                      geometry_weight: float) -> torch.Tensor:
     """TTT-proposed event bases (sparse_convex.py:1268-1324) on the device: sensitive patches
@@ -407,43 +466,31 @@ def _ttt_event_bases(features, geometry, labels, sensitivity, excluded, *, patch
     whose feature is closest to the bin's normalised mean feature, with a geometry penalty and a
     0.005 sensitivity bonus (lowest id on ties); with more bins than ``amount`` the bins with the
     largest mean sensitivity x sqrt(size) win; with fewer, the most sensitive remaining patches
-    fill up.  Sorted unique patch ids."""
-    ids = torch.nonzero((labels == 1) & ~excluded).flatten()
-    if amount <= 0 or ids.numel() == 0:
+    fill up.  Sorted unique patch ids.  The binning and every feature-independent term come
+    from the clip's cached _EventTables; per call only the feature terms are computed."""
+    tab = _EventTables.get(geometry, labels, sensitivity, excluded, patches, amount, geometry_weight)
+    ids = tab.ids
+    if amount <= 0 or tab.n == 0:
         return ids[:0]
-    geo = geometry.index_select(0, ids)
-    xyz = torch.floor((geo[:, :3] + 4.0) / 0.5).long().clamp(0, 31)
-    time_bin = (ids // patches) // 4
-    code = ((time_bin * 37 + xyz[:, 0]) * 37 + xyz[:, 1]) * 37 + xyz[:, 2]
-    _, inverse = torch.unique(code, return_inverse=True)
-    groups = int(inverse.max()) + 1
-    counts = torch.bincount(inverse, minlength=groups)
-    order = inverse.argsort(stable=True)
+    inverse = tab.inverse
     feat = features.index_select(0, ids).float()
-    mean_f = torch.segment_reduce(feat.index_select(0, order), "mean", lengths=counts)
+    mean_f = torch.segment_reduce(feat.index_select(0, tab.order), "mean", lengths=tab.counts)
     center_f = torch.nn.functional.normalize(mean_f, dim=-1, eps=1e-8)
-    center_g = torch.segment_reduce(geo.index_select(0, order), "mean", lengths=counts)
-    sens = sensitivity.index_select(0, ids)
-    score = ((feat * center_f.index_select(0, inverse)).sum(-1)
-             - geometry_weight * (geo - center_g.index_select(0, inverse)).square().sum(-1) + 0.005 * sens)
-    best = torch.full((groups,), -torch.inf, device=ids.device)
+    score = (feat * center_f.index_select(0, inverse)).sum(-1) - tab.geo_term + tab.sens_term
+    best = torch.full((tab.groups,), -torch.inf, device=ids.device)
     best.scatter_reduce_(0, inverse, score, reduce="amax", include_self=True)
     sentinel = labels.numel()
     candidate = torch.where(score == best.index_select(0, inverse), ids, torch.full_like(ids, sentinel))
-    rep = torch.full((groups,), sentinel, device=ids.device, dtype=torch.long)
-    rep.scatter_reduce_(0, inverse, candidate, reduce="amin", include_self=True)
-    rep = rep[rep < sentinel]
-    if rep.numel() > amount:
-        group_score = torch.segment_reduce(sens.index_select(0, order), "mean", lengths=counts) * counts.float().sqrt()
-        rep = rep.index_select(0, group_score.topk(amount).indices)
-    if rep.numel() < amount:
-        chosen = torch.zeros(labels.numel(), device=ids.device, dtype=torch.bool)
+    rep = torch.full((tab.groups,), sentinel, device=ids.device, dtype=torch.long)
+    rep.scatter_reduce_(0, inverse, candidate, reduce="amin", include_self=True)  # every bin has a member
+    if tab.select is not None:
+        rep = rep.index_select(0, tab.select)
+    elif tab.fill > 0:
+        chosen = torch.zeros(sentinel, device=ids.device, dtype=torch.bool)
         chosen[rep] = True
-        remaining = ids[~chosen.index_select(0, ids)]
-        fill = min(amount - rep.numel(), remaining.numel())
-        if fill:
-            rep = torch.cat([rep, remaining.index_select(0, sensitivity.index_select(0, remaining).topk(fill).indices)])
-    return torch.unique(rep)
+        masked = torch.where(chosen.index_select(0, ids), torch.full_like(tab.sens, -torch.inf), tab.sens)
+        rep = torch.cat([rep, ids.index_select(0, masked.topk(tab.fill).indices)])
+    return torch.sort(rep).values
 
 
 @torch.no_grad()
