@@ -17,9 +17,9 @@
 //                      low-confidence / raw-event predicates (:199-230, :321-341).
 //
 // All arithmetic is fp32 with IEEE division and square root.  The descriptors are small
-// (a few hundred thousand patches of 32-256 channels); one warp per patch row keeps a source
-// row in registers and reads the candidate rows through L1, where neighbouring patches'
-// windows overlap.
+// (a few hundred thousand patches of 32-256 channels); the match gives each candidate of a patch
+// its own lane and reads the candidate rows through L1, where neighbouring patches' windows
+// overlap.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -52,60 +52,190 @@ __global__ void __launch_bounds__(kTttWarps * 32)
   for (int c = lane; c < C; c += 32) out[r * C + c] = __fdiv_rn(to_f32<T>(xr[c]), norm);
 }
 
-// One warp per source patch; channel c = lane + 32 i lives in register i (C <= 256).
+// One warp per source patch, one lane per candidate (lane l takes candidates l, l + 32, ...):
+// the source row sits in shared memory (read as broadcasts), each lane walks its candidate's
+// target row in 16-byte vectors (L1 hits: neighbouring patches share most of their windows) and
+// keeps its own best (strict '>' in candidate order, so the first of equal maxima) and second.
+// The warp then combines them: best = the largest value at the lowest candidate index, second
+// = the largest of everything else (the owning lane's second, every other lane's best), which is
+// what the reference's sequential scan produces.  C <= 256.
+template <typename T>
+__device__ __forceinline__ float dot_row(const float* __restrict__ s, const T* __restrict__ t, int C) {
+  float acc = 0.f;
+  if constexpr (sizeof(T) == 4) {
+    for (int c = 0; c < C; c += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(t + c));
+      acc = fmaf(s[c], v.x, acc);
+      acc = fmaf(s[c + 1], v.y, acc);
+      acc = fmaf(s[c + 2], v.z, acc);
+      acc = fmaf(s[c + 3], v.w, acc);
+    }
+  } else {
+    for (int c = 0; c < C; c += 8) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(t + c));
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = fmaf(s[c + i], to_f32<T>(e[i]), acc);
+    }
+  }
+  return acc;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kTttWarps * 32)
     local_top2_match_kernel(const T* __restrict__ source, const T* __restrict__ target, long long rows, int H, int W,
                             int C, int ry, int rx, int reverse, float* __restrict__ best_out,
                             float* __restrict__ second_out, int32_t* __restrict__ dy_out,
                             int32_t* __restrict__ dx_out) {
-  const long long row = static_cast<long long>(blockIdx.x) * kTttWarps + (threadIdx.x >> 5);
+  __shared__ float src_s[kTttWarps][256];
+  const int warp = threadIdx.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * kTttWarps + warp;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const long long pc = static_cast<long long>(H) * W;
   const long long pair = row / pc;
   const int patch = static_cast<int>(row - pair * pc);
   const int y = patch / W, x = patch - (patch / W) * W;
-  float s[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = lane + 32 * i;
-    s[i] = c < C ? to_f32<T>(source[row * C + c]) : 0.f;
-  }
-  float best = -INFINITY, second = -INFINITY;
-  int by = 0, bx = 0;
+  float* s = src_s[warp];
+  for (int c = lane; c < C; c += 32) s[c] = to_f32<T>(source[row * C + c]);
+  __syncwarp();
   const int span_x = 2 * rx + 1;
   const int candidates = (2 * ry + 1) * span_x;
-  for (int k = 0; k < candidates; ++k) {
+  float best = -INFINITY, second = -INFINITY;
+  int bk = 0x7fffffff;
+  for (int k = lane; k < candidates; k += 32) {
     const int cy = k / span_x, cx = k - (k / span_x) * span_x;
-    const int oy = reverse ? ry - cy : cy - ry;
-    const int ox = reverse ? rx - cx : cx - rx;
-    const int ty = y + oy, tx = x + ox;
+    const int ty = y + (reverse ? ry - cy : cy - ry), tx = x + (reverse ? rx - cx : cx - rx);
     float sim = -INFINITY;
-    if (ty >= 0 && ty < H && tx >= 0 && tx < W) {  // uniform across the warp
-      const T* t = target + (pair * pc + static_cast<long long>(ty) * W + tx) * C;
-      float acc = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int c = lane + 32 * i;
-        if (c < C) acc = fmaf(s[i], to_f32<T>(__ldg(t + c)), acc);
-      }
-      sim = warp_allsum(acc);
-    }
+    if (ty >= 0 && ty < H && tx >= 0 && tx < W)
+      sim = dot_row<T>(s, target + (pair * pc + static_cast<long long>(ty) * W + tx) * C, C);
     const bool better = sim > best;
     second = better ? best : fmaxf(second, sim);
     if (better) {
       best = sim;
-      by = oy;
-      bx = ox;
+      bk = k;
     }
   }
+  // warp combine: the largest best, at the lowest candidate index among equal values
+  float m = best;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  int kmin = best == m ? bk : 0x7fffffff;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+  float sec = bk == kmin ? second : best;  // the owner offers its second, every other lane its best
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sec = fmaxf(sec, __shfl_xor_sync(0xffffffffu, sec, o));
   if (lane == 0) {
-    best_out[row] = best;
-    second_out[row] = second;
-    dy_out[row] = by;
-    dx_out[row] = bx;
+    const int cy = kmin / span_x, cx = kmin - (kmin / span_x) * span_x;
+    best_out[row] = m;
+    second_out[row] = sec;
+    dy_out[row] = reverse ? ry - cy : cy - ry;
+    dx_out[row] = reverse ? rx - cx : cx - rx;
   }
+}
+
+// Tiled form (the default when the window fits): one CTA per (pair, tile x tile source patches).
+// The tile's target window with its halo ((tile + 2 ry) x (tile + 2 rx) rows of C channels, fp32)
+// and the tile's source rows are staged in shared memory once, so every target row is read from
+// L2 once per tile instead of once per neighbouring patch.  Each warp then takes the tile's
+// patches in turn, one lane per candidate as in local_top2_match_kernel (same order and
+// tie-breaking); the target rows are padded by 4 floats so that the lanes' 16-byte reads of
+// different rows spread over all banks.
+constexpr int kTiledWarps = 16;
+
+__global__ void __launch_bounds__(kTiledWarps * 32)
+    local_top2_tiled_kernel(const float* __restrict__ source, const float* __restrict__ target, int H, int W, int C,
+                            int ry, int rx, int reverse, int tile, float* __restrict__ best_out,
+                            float* __restrict__ second_out, int32_t* __restrict__ dy_out,
+                            int32_t* __restrict__ dx_out) {
+  extern __shared__ __align__(16) float tsm[];
+  const int tiles_x = (W + tile - 1) / tile;
+  const int ty0 = (blockIdx.x / tiles_x) * tile, tx0 = (blockIdx.x % tiles_x) * tile;
+  const long long pair = blockIdx.y;
+  const long long pc = static_cast<long long>(H) * W;
+  const int HY = tile + 2 * ry, HX = tile + 2 * rx;
+  const int stride = C + 4;  // floats per staged target row
+  float* tgt_s = tsm;
+  float* src_s = tsm + static_cast<size_t>(HY) * HX * stride;
+  const int q4 = C / 4;
+  // stage the target window (rows outside the grid are never read) and the tile's source rows
+#pragma unroll 4
+  for (int i = threadIdx.x; i < HY * HX * q4; i += blockDim.x) {
+    const int r = i / q4, q = i - r * q4;
+    const int gy = ty0 - ry + r / HX, gx = tx0 - rx + r % HX;
+    if (gy >= 0 && gy < H && gx >= 0 && gx < W)
+      *reinterpret_cast<float4*>(tgt_s + static_cast<size_t>(r) * stride + 4 * q) =
+          __ldg(reinterpret_cast<const float4*>(target + ((pair * pc + static_cast<long long>(gy) * W + gx) * C) + 4 * q));
+  }
+  for (int i = threadIdx.x; i < tile * tile * q4; i += blockDim.x) {
+    const int r = i / q4, q = i - r * q4;
+    const int gy = ty0 + r / tile, gx = tx0 + r % tile;
+    if (gy < H && gx < W)
+      *reinterpret_cast<float4*>(src_s + static_cast<size_t>(r) * C + 4 * q) =
+          __ldg(reinterpret_cast<const float4*>(source + ((pair * pc + static_cast<long long>(gy) * W + gx) * C) + 4 * q));
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int span_x = 2 * rx + 1;
+  const int candidates = (2 * ry + 1) * span_x;
+  for (int p = warp; p < tile * tile; p += kTiledWarps) {
+    const int y = ty0 + p / tile, x = tx0 + p % tile;
+    if (y >= H || x >= W) continue;  // uniform across the warp
+    const float* sv = src_s + static_cast<size_t>(p) * C;
+    float best = -INFINITY, second = -INFINITY;
+    int bk = 0x7fffffff;
+    for (int k = lane; k < candidates; k += 32) {
+      const int cy = k / span_x, cx = k - (k / span_x) * span_x;
+      const int oy = reverse ? ry - cy : cy - ry, ox = reverse ? rx - cx : cx - rx;
+      float sim = -INFINITY;
+      if (y + oy >= 0 && y + oy < H && x + ox >= 0 && x + ox < W) {
+        const float* tv = tgt_s + static_cast<size_t>((p / tile + ry + oy) * HX + (p % tile + rx + ox)) * stride;
+        // four independent partial sums (channel c mod 4), added at the end
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < C; c += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(sv + c);
+          const float4 b = *reinterpret_cast<const float4*>(tv + c);
+          a0 = fmaf(a.x, b.x, a0);
+          a1 = fmaf(a.y, b.y, a1);
+          a2 = fmaf(a.z, b.z, a2);
+          a3 = fmaf(a.w, b.w, a3);
+        }
+        sim = (a0 + a1) + (a2 + a3);
+      }
+      const bool better = sim > best;
+      second = better ? best : fmaxf(second, sim);
+      if (better) {
+        best = sim;
+        bk = k;
+      }
+    }
+    float m = best;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    int kmin = best == m ? bk : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    float sec = bk == kmin ? second : best;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sec = fmaxf(sec, __shfl_xor_sync(0xffffffffu, sec, o));
+    if (lane == 0) {
+      const long long row = pair * pc + static_cast<long long>(y) * W + x;
+      const int cy = kmin / span_x, cx = kmin - (kmin / span_x) * span_x;
+      best_out[row] = m;
+      second_out[row] = sec;
+      dy_out[row] = reverse ? ry - cy : cy - ry;
+      dx_out[row] = reverse ? rx - cx : cx - rx;
+    }
+  }
+}
+
+constexpr size_t kTileSmemMax = 200 * 1024;
+
+inline size_t tiled_smem(int tile, int ry, int rx, int C) {
+  return (static_cast<size_t>(tile + 2 * ry) * (tile + 2 * rx) * (C + 4) + static_cast<size_t>(tile) * tile * C) *
+         sizeof(float);
 }
 
 // One thread per element; flow (x, y) is truncated toward zero like a float -> int cast.
@@ -221,12 +351,31 @@ extern "C" int vb200_local_top2_match(int dtype, const void* source, const void*
   VB200_REQUIRE(dtype == VB200_F32 || dtype == VB200_BF16 || dtype == VB200_F16, "local_top2_match: bad dtype %d",
                 dtype);
   VB200_REQUIRE(pairs >= 0 && H > 0 && W > 0 && C >= 1 && C <= 256, "local_top2_match: need 1 <= C <= 256");
+  VB200_REQUIRE(C % (dtype == VB200_F32 ? 4 : 8) == 0 && (reinterpret_cast<uintptr_t>(target) & 15u) == 0,
+                "local_top2_match: rows must be 16-byte aligned (C a multiple of 4 for f32, 8 for 16-bit)");
   VB200_REQUIRE(radius_y >= 0 && radius_x >= 0 && radius_y < H && radius_x < W,
                 "local_top2_match: radii must lie in [0, H) x [0, W)");
   const long long rows = pairs * H * W;
   if (rows == 0) return VB200_OK;
   VB200_REQUIRE(source && target && best && second && dy && dx, "local_top2_match: null pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == VB200_F32 && (reinterpret_cast<uintptr_t>(source) & 15u) == 0 && pairs <= 65535) {
+    // the tiled kernel when an 8 x 8 (or 4 x 4) tile's window fits in shared memory
+    for (int tile : {8, 4}) {
+      const size_t smem = tiled_smem(tile, radius_y, radius_x, static_cast<int>(C));
+      if (smem > kTileSmemMax) continue;
+      VB200_CHECK_CUDA(cudaFuncSetAttribute(local_top2_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(smem)),
+                       "cudaFuncSetAttribute");
+      const dim3 grid(static_cast<unsigned>(((H + tile - 1) / tile) * ((W + tile - 1) / tile)),
+                      static_cast<unsigned>(pairs));
+      local_top2_tiled_kernel<<<grid, kTiledWarps * 32, smem, st>>>(
+          static_cast<const float*>(source), static_cast<const float*>(target), static_cast<int>(H),
+          static_cast<int>(W), static_cast<int>(C), radius_y, radius_x, reverse ? 1 : 0, tile, best, second, dy, dx);
+      VB200_CHECK_LAUNCH("local_top2_tiled_kernel");
+      return VB200_OK;
+    }
+  }
 #define VB200_LTM(T)                                                                                     \
   local_top2_match_kernel<T><<<blocks_of(rows, kTttWarps), kTttWarps * 32, 0, st>>>(                     \
       static_cast<const T*>(source), static_cast<const T*>(target), rows, static_cast<int>(H),            \

@@ -278,6 +278,23 @@ def _median_ms(fn, reps: int) -> float:
     return statistics.median(ms)
 
 
+def _median_gpu_ms(fn, reps: int) -> float:
+    """Median GPU time of fn() over ``reps`` calls: the GPU first sleeps (~25 ms) while the host
+    queues every call, so each event pair times the GPU's work, not the host's launch rate."""
+    import torch
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    torch.cuda._sleep(50_000_000)
+    for e0, e1 in ev:
+        e0.record()
+        fn()
+        e1.record()
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in ev)
+
+
 def projection_stress(pkg, dev, hbm_peak: float, N: int = 1 << 20, reps: int = 5) -> dict:
     """Config 5 (top-4 projection bandwidth stress) on one GPU: N = 1,048,576 tokens,
     M = 65,536 merged tokens, D = 1024 bf16 (plan: _config5_plan, sampled on the GPU).  Times
@@ -565,6 +582,69 @@ def full_forward_config3(pkg, dev, steps: int = 3, warmup: int = 2, frames: int 
     return result
 
 
+def ttt_prepass(pkg, dev, frames: int = 32, grid: int = 32, channels: int = 64, radius: int = 4,
+                reps: int = 20) -> dict:
+    """The TTT pre-pass kernels at the released configuration's size (configs/ttt_best.py: 64-dim
+    token-match descriptors, radius 4, 32-frame chunks; a 512 x 512 frame is 32 x 32 patches):
+    descriptor normalisation, forward and backward exact-window top-2 matching, the integer warp
+    of a 3-channel field, fused motion cues and fused sensitivity labels, each timed with CUDA
+    events (median of ``reps``, GPU time: the calls are queued behind a GPU sleep).  Beside
+    them, the reference's own Triton kernels
+    (vggt_omega/utils/ttt_kernels.py, from baseline/_ref) on the same inputs and GPU."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(7)
+    raw = torch.randn(frames, grid, grid, channels, device=dev, generator=g)
+    desc = pkg.ttt_kernels.normalize_rows(raw)
+    src, tgt = desc[:-1].contiguous(), desc[1:].contiguous()
+    field = torch.randn(frames - 1, grid, grid, 3, device=dev, generator=g)
+    flow = torch.randint(-radius, radius + 1, (frames - 1, grid, grid, 2), device=dev, generator=g).float()
+    conf = torch.rand(frames - 1, grid, grid, device=dev, generator=g)
+    pred = torch.randn(frames, grid, grid, 4, device=dev, generator=g)
+    res, cnf, bnd = pkg.ttt_kernels.fused_motion_cues(flow, flow, pred, conf, conf)
+    scal = [torch.tensor(v, device=dev) for v in (1.0, 1.0, 0.5, 0.5)]
+
+    def ops(m):
+        return {
+            "normalize_rows": lambda: m.normalize_rows(raw),
+            "local_top2_match_fwd": lambda: m.local_top2_match(src, tgt, radius, radius),
+            "local_top2_match_bwd": lambda: m.local_top2_match(tgt, src, radius, radius, reverse_order=True),
+            "integer_gather_warp": lambda: m.integer_gather_warp(field, flow),
+            "fused_motion_cues": lambda: m.fused_motion_cues(flow, flow, pred, conf, conf),
+            "fused_sensitivity_labels": lambda: m.fused_sensitivity_labels(
+                res, cnf, bnd, uncertain_confidence=0.1, residual_scale=scal[0], boundary_scale=scal[1],
+                residual_threshold=scal[2], boundary_threshold=scal[3]),
+        }
+
+    def time_all(table):
+        out = {}
+        for name, fn in table.items():
+            out[name] = round(_median_gpu_ms(fn, reps) * 1e3, 2)
+        return out
+
+    result = {"workload": f"TTT pre-pass: {frames} frames of {grid}x{grid} patches, {channels}-dim descriptors, "
+                          f"radius {radius} ({(2 * radius + 1) ** 2} candidates); CUDA events, median of {reps}, "
+                          "calls queued behind a GPU sleep (GPU time, not launch rate)",
+              "ours_us": time_all(ops(pkg.ttt_kernels))}
+    rows = (frames - 1) * grid * grid
+    result["local_top2_match_candidates_per_s"] = rows * (2 * radius + 1) ** 2 / (
+        result["ours_us"]["local_top2_match_fwd"] / 1e6)
+    if (REF_INSTALL / "vggt_omega").exists():
+        try:
+            if str(REF_INSTALL) not in sys.path:
+                sys.path.insert(0, str(REF_INSTALL))
+            os.environ["VGGT_TRITON_NORMALIZE"] = "1"  # the reference's Triton normalisation, not F.normalize
+            import vggt_omega.utils.ttt_kernels as ref_tk
+            result["reference_triton_us"] = time_all(ops(ref_tk))
+            a = pkg.ttt_kernels.local_top2_match(src, tgt, radius, radius)
+            b = ref_tk.local_top2_match(src, tgt, radius, radius)
+            result["agreement_vs_reference"] = {
+                "best_max_abs_diff": float((a[0] - b[0]).abs().max()),
+                "offsets_equal_share": float(((a[2] == b[2]) & (a[3] == b[3])).float().mean())}
+        except Exception as e:  # the reference's kernels are a comparison only
+            result["reference_triton_us"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    return result
+
+
 def run_reference(args) -> None:
     """The reference arm: its PyTorch CPU path on the GPU arm's config, metric and unit, on
     rank 0 only (other ranks exit without work).  Each step is the whole config-2 step; at
@@ -785,6 +865,7 @@ def run_ours(args) -> None:
                                                                 max(3, min(args.steps, 10)), flush)
     if world == 1:
         line["components"]["projection_config5"] = projection_stress(pkg, dev, hbm_peak)
+        line["components"]["ttt_prepass"] = ttt_prepass(pkg, dev)
         if not args.no_config3:
             try:
                 line["components"]["full_forward_config3"] = full_forward_config3(pkg, dev)
@@ -819,10 +900,18 @@ def main() -> None:
     ap.add_argument("--config3-only", action="store_true",
                     help="run only the config-3 full-forward comparison on one GPU and print its JSON")
     ap.add_argument("--no-config3", action="store_true", help="skip the config-3 component of the N=1 line")
+    ap.add_argument("--ttt-only", action="store_true",
+                    help="run only the TTT pre-pass kernel timings on one GPU and print their JSON")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
-    if args.config3_only:
+    if args.ttt_only:
+        import torch
+        pkg = importlib.import_module("4d_ttt_merging_b200")
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        print(json.dumps(ttt_prepass(pkg, dev)), flush=True)
+    elif args.config3_only:
         import torch
         pkg = importlib.import_module("4d_ttt_merging_b200")
         dev = torch.device("cuda", 0)

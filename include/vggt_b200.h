@@ -422,7 +422,8 @@ VB200_API int vb200_four_support_active_set(const float* gram, const float* rhs,
  * (ttt_kernels.py:233-249), whose default is F.normalize(value.float(), eps=1e-6). */
 VB200_API int vb200_row_l2_normalize(int dtype, const void* x, int64_t rows, int64_t C, float eps, float* out,
                                      void* stream);
-/* Exact-window cosine top-2 of [pairs, H, W, C] descriptors (1 <= C <= 256): for every source
+/* Exact-window cosine top-2 of [pairs, H, W, C] descriptors (1 <= C <= 256, C a multiple of 4
+ * for f32 and of 8 for 16-bit types, rows 16-byte aligned): for every source
  * patch (p, y, x) the best and second-best dot product with target[p, y + oy, x + ox] over
  * |oy| <= radius_y, |ox| <= radius_x inside the grid, and the (dy, dx) of the best.  Candidates
  * run in row-major offset order (reverse != 0: the reversed order the backward match uses); a
