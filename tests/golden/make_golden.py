@@ -287,6 +287,46 @@ def main() -> None:
                                      md["confidence_mean"], md["motion_residual_mean"], md["motion_boundary_mean"]],
                                     np.float64)
 
+    # ---------------- config 1 at its full size, and config 5 scaled down ----------------
+    # Inputs from the oracle's seeded numpy generators (oracle/synth.py); outputs from the
+    # reference's own CPU path: the SDPA call with the log-mass mask of layers/attention.py:386-400
+    # and WeightedBilinearTokenPlan.compact / restore.  To keep the fixture small only some heads
+    # and channels of the large outputs are stored (they are exact slices of the full results).
+    from oracle import synth
+    c1 = synth.c1_inputs(seed=0)
+    q, k, v = (torch.from_numpy(c1[n]) for n in ("q", "k", "v"))
+    log_m = torch.from_numpy(c1["log_mass"])
+    att = torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=log_m[None, None, None, :])
+    out["c1_heads"] = np.array([5], np.int64)
+    out["c1_attention"] = _np(att[0, out["c1_heads"]])
+    N1, M1 = c1["N"], c1["M"]
+    parent1 = torch.from_numpy(c1["parent"])[None]
+    w1 = torch.from_numpy(c1["weights"])[None]
+    norm1 = deterministic_weighted_normalizer(parent1, w1, M1)
+    plan1 = WeightedBilinearTokenPlan(
+        keep=torch.from_numpy(c1["keep"])[None], source_original=torch.from_numpy(c1["src"])[None],
+        source_parent_compact=parent1, source_pool_weights=w1, source_restore_weights=w1, original_tokens=N1,
+        normalizer=norm1, key_log_mass=norm1[..., 0].log())
+    merged = att[0].transpose(0, 1)[:M1].reshape(1, M1, -1)  # [1, M, 16 x 64]: the first M query rows
+    restored = plan1.restore(merged)
+    out["c1_restore_cols"] = _np(restored[0, :, 320:384])  # head 5's 64 channels
+    out["c1_normalizer"] = _np(norm1[0, :, 0])
+    N5, M5, D5 = 8192, 512, 16
+    keep5, src5, parent5, w5 = synth.zipf_plan(5, N5, M5)
+    p5, ww5 = torch.from_numpy(parent5)[None], torch.from_numpy(w5)[None]
+    norm5 = deterministic_weighted_normalizer(p5, ww5, M5)
+    plan5 = WeightedBilinearTokenPlan(
+        keep=torch.from_numpy(keep5)[None], source_original=torch.from_numpy(src5)[None], source_parent_compact=p5,
+        source_pool_weights=ww5, source_restore_weights=ww5, original_tokens=N5, normalizer=norm5,
+        key_log_mass=norm5[..., 0].log())
+    g5 = torch.Generator().manual_seed(55)
+    x5 = torch.randn(1, N5, D5, generator=g5)
+    y5 = torch.randn(1, M5, D5, generator=g5)
+    # x5 / y5 are regenerated by the tests from torch.Generator().manual_seed(55) (randn, CPU)
+    out["c5_normalizer"] = _np(norm5[0, :, 0])
+    out["c5_compact"] = _np(plan5.compact(x5))
+    out["c5_restore"] = _np(plan5.restore(y5))
+
     # ---------------- CPU generator stream ----------------
     out["rand_seed3"] = _np(torch.rand(2, 4, 4, 2, generator=torch.Generator(device="cpu").manual_seed(3)))
 

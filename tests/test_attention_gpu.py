@@ -64,14 +64,18 @@ def test_bias_rounding_and_no_bias(pkg, oracle, cuda_device, bias_dtype):
     assert_close(out0, oracle.mass_bias_attention(q, k, v, None, dtype="bf16", round_p=True), "bf16")
 
 
-def test_config1_shape_fp32(pkg, oracle, cuda_device):
-    """Config 1 (fp32): N=4116 queries over M=1029 merged keys with integer masses, 16 heads
-    (4 heads checked against the oracle to keep the CPU side short)."""
+def test_config1_shape_fp32(pkg, oracle, golden, cuda_device):
+    """Config 1 (fp32): N=4116 queries over M=1029 merged keys with integer masses, all 16
+    heads in one launch: the reference-generated golden head (its SDPA-with-mask call) and
+    three more heads against the oracle, to the fp32 bar."""
     c1 = oracle.c1_inputs(seed=0)
-    q, k, v = c1["q"][:, :4], c1["k"][:, :4], c1["v"][:, :4]
-    out = _run(pkg, q, k, v, c1["log_mass"], "f32", cuda_device)
-    ref = oracle.mass_bias_attention(q, k, v, c1["log_mass"])
-    assert_close(out, ref, "f32")
+    out = _run(pkg, c1["q"], c1["k"], c1["v"], c1["log_mass"], "f32", cuda_device)
+    h = int(golden["c1_heads"][0])
+    assert_close(out[0, h], golden["c1_attention"][0], "f32")
+    for hh in (0, 9, 15):
+        sl = slice(hh, hh + 1)
+        ref = oracle.mass_bias_attention(c1["q"][:, sl], c1["k"][:, sl], c1["v"][:, sl], c1["log_mass"])
+        assert_close(out[:, sl], ref, "f32")
 
 
 def test_strided_views_and_autocast(pkg, oracle, cuda_device):

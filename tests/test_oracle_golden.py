@@ -246,3 +246,36 @@ def test_ttt_prepass_matches_reference(oracle, golden):
     labels = g("labels").reshape(res.shape)
     assert np.all(labels[0] == 0)
     assert np.all(event[labels == 1]) and np.all(low[labels == 2])  # labels come from the raw predicates
+
+
+def c5_inputs():
+    """The scaled-down config-5 values of the golden (torch CPU generator, seed 55)."""
+    import torch
+    g = torch.Generator().manual_seed(55)
+    x = torch.randn(1, 8192, 16, generator=g)[0].numpy()
+    y = torch.randn(1, 512, 16, generator=g)[0].numpy()
+    return x, y
+
+
+def test_config1_and_config5_goldens(oracle, golden):
+    """Config 1 at its full size (4,116 queries over 1,029 keys, 16 heads, integer masses; the
+    reference's SDPA call with the log-mass mask and its restore) and config 5 scaled to 8,192
+    tokens / 512 merged rows (Zipf parents; the reference's compact and restore): the oracle
+    against the stored heads / channels of the reference's outputs."""
+    c1 = oracle.c1_inputs(seed=0)
+    h = int(golden["c1_heads"][0])
+    att = oracle.mass_bias_attention(c1["q"][:, [h]], c1["k"][:, [h]], c1["v"][:, [h]], c1["log_mass"])
+    np.testing.assert_allclose(att[0], golden["c1_attention"], rtol=1e-4, atol=2e-6)
+    np.testing.assert_allclose(oracle.normalizer(c1["parent"], c1["weights"], c1["M"]), golden["c1_normalizer"],
+                               rtol=1e-6)
+    merged = golden["c1_attention"][0][: c1["M"]]  # head h's output rows [:M] are these merged rows' channels
+    restored = oracle.restore(merged, c1["keep"], c1["src"], c1["parent"], c1["weights"], c1["N"])
+    np.testing.assert_allclose(restored, golden["c1_restore_cols"], rtol=1e-6, atol=1e-7)
+    keep, src, parent, w = oracle.zipf_plan(5, 8192, 512)
+    norm = oracle.normalizer(parent, w, 512)
+    np.testing.assert_allclose(norm, golden["c5_normalizer"], rtol=1e-6)
+    x, y = c5_inputs()
+    np.testing.assert_allclose(oracle.compact(x, keep, src, parent, w, norm), golden["c5_compact"][0], rtol=1e-5,
+                               atol=1e-6)
+    np.testing.assert_allclose(oracle.restore(y, keep, src, parent, w, 8192), golden["c5_restore"][0], rtol=1e-6,
+                               atol=1e-7)

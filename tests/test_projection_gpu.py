@@ -43,6 +43,27 @@ def test_golden_plan_ops(pkg, golden, cuda_device):
     np.testing.assert_array_equal(to_np(plan.restore(y.bfloat16())), g["plan_restore_bf16"])
 
 
+def test_golden_config1_and_config5(pkg, oracle, golden, cuda_device):
+    """The reference-generated goldens at size: config 1's restore of 1,029 merged rows to 4,116
+    tokens (the golden's channels of head 5) and config 5 scaled to 8,192 tokens / 512 merged rows
+    with Zipf parents (compact and restore), fp32."""
+    dev = cuda_device
+    c1 = oracle.c1_inputs(seed=0)
+    plan = _plan(pkg, c1["keep"], c1["src"], c1["parent"], c1["weights"], c1["N"], dev=dev)
+    np.testing.assert_allclose(to_np(plan.normalizer[0, :, 0]), golden["c1_normalizer"], rtol=1e-6)
+    merged = torch.from_numpy(golden["c1_attention"][0][: c1["M"]]).to(dev)
+    np.testing.assert_allclose(to_np(plan.restore(merged[None])[0]), golden["c1_restore_cols"], rtol=1e-6, atol=1e-7)
+    keep, src, parent, w = oracle.zipf_plan(5, 8192, 512)
+    plan5 = _plan(pkg, keep, src, parent, w, 8192, dev=dev)
+    np.testing.assert_allclose(to_np(plan5.normalizer[0, :, 0]), golden["c5_normalizer"], rtol=1e-6)
+    g = torch.Generator().manual_seed(55)
+    x = torch.randn(1, 8192, 16, generator=g).to(dev)
+    y = torch.randn(1, 512, 16, generator=g).to(dev)
+    np.testing.assert_allclose(to_np(plan5.compact(x)), golden["c5_compact"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(to_np(plan5.restore(y)), golden["c5_restore"], rtol=1e-6, atol=1e-6)
+    assert pkg.device_error_flags() == 0
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
 @pytest.mark.parametrize("C", [64, 1024, 3072])
 def test_random_plans(pkg, oracle, cuda_device, dtype, C):
