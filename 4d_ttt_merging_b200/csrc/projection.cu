@@ -1263,8 +1263,9 @@ __global__ void csr_mass_kernel(const int32_t* __restrict__ seg_offsets, const f
 // [q_begin[g], q_begin[g+1]), merged rows [b_begin[g], b_begin[g+1]); its entries fill
 // [q_begin[g], q_begin[g+1]) x corners of the entry arrays.  Masses follow in csr_mass_kernel.
 constexpr int kCsrGroupThreads = 1024;
+constexpr int kCsrMaxParts = 8;  // CTAs per frame group in the grouped CSR build
 constexpr int kCsrGroupMaxSegments = 8 * 1024;    // shared-memory counters per group
-constexpr int kCsrGroupMaxEntries = 16 * 1024;    // shared-memory entries per group (12 bytes each)
+constexpr int kCsrGroupMaxEntries = 16 * 1024;    // shared-memory entries per group (10 bytes each)
 
 __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1295,43 +1296,49 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
     csr_grouped_kernel(const int64_t* __restrict__ parent, const float* __restrict__ weights,
                        const int64_t* __restrict__ src_rows, int corners, long long M,
                        const int64_t* __restrict__ q_begin, const int64_t* __restrict__ b_begin, int groups,
-                       int max_segments, int max_entries, int32_t* __restrict__ seg_offsets,
+                       int parts, int max_segments, int max_entries, int32_t* __restrict__ seg_offsets,
                        int32_t* __restrict__ entry_src, float* __restrict__ entry_w) {
   extern __shared__ __align__(16) int csr_smem[];
   __shared__ int warp_tot[32];
-  // shared memory: counters [max_segments] | staged weights [max_entries] | placed weights
-  // [max_entries] | staged segment of each pair (int16 pairs) | placed source index (int16)
+  __shared__ int n_staged, n_below;
+  // shared memory: counters [max_segments] | placed weights [max_entries] | staged segment of each
+  // pair (int16) | staged source (int16) | placed source (int16); a staged pair's weight is read
+  // again from global memory (an L2 hit) when it is placed
   int* cnt = csr_smem;
-  float* w_in = reinterpret_cast<float*>(cnt + max_segments);
-  float* e_w = w_in + max_entries;
-  uint16_t* seg_in = reinterpret_cast<uint16_t*>(e_w + max_entries);
-  uint16_t* e_src = seg_in + max_entries;
-  const int g = blockIdx.x;
+  float* e_w = reinterpret_cast<float*>(cnt + max_segments);
+  uint16_t* st_seg = reinterpret_cast<uint16_t*>(e_w + max_entries);
+  uint16_t* st_src = st_seg + max_entries;
+  uint16_t* e_src = st_src + max_entries;
+  const int g = blockIdx.x / parts, part = blockIdx.x - (blockIdx.x / parts) * parts;
   const long long q0 = q_begin[g], q1 = q_begin[g + 1], b0 = b_begin[g], b1 = b_begin[g + 1];
   const int rows = static_cast<int>(b1 - b0);
-  const int nseg = rows * corners;
+  const int per = (rows + parts - 1) / parts;
+  const int lo = min(rows, part * per), hi = min(rows, lo + per);  // this CTA's merged rows [lo, hi)
+  const int nseg = (hi - lo) * corners;
   const int n = static_cast<int>((q1 - q0) * corners);
   const long long e_base = q0 * corners;
-  if (nseg > max_segments || n > max_entries || (nseg == 0 && n > 0)) {
+  if (nseg > max_segments || n > max_entries || (rows == 0 && n > 0)) {
     if (threadIdx.x == 0) atomicOr(&g_proj_err, kErrBadArgument);  // the host checks make this unreachable
     return;
   }
-  constexpr uint16_t kDropped = 0xffff;
+  if (threadIdx.x == 0) {
+    n_staged = 0;
+    n_below = 0;
+  }
   for (int i = threadIdx.x; i < nseg; i += blockDim.x) cnt[i] = 0;
-  // stage every pair's segment and weight: four coalesced loads per thread in flight at a time,
-  // and one error report per thread (an atomic between the loads would serialise them)
+  __syncthreads();
+  // Every part scans all of the group's pairs: it stages the pairs whose parent lies in its rows
+  // and counts the valid pairs below them (its entries' offset in the group).  Four coalesced
+  // loads per thread in flight at a time, one error report per thread.
   bool bad = false;
+  int below = 0;
   const int stride = blockDim.x;
   for (int e0 = threadIdx.x; e0 < n; e0 += 4 * stride) {
     int64_t pv[4];
-    float wv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int e = e0 + u * stride;
-      if (e < n) {
-        pv[u] = parent[e_base + e];
-        wv[u] = weights[e_base + e];
-      }
+      if (e < n) pv[u] = parent[e_base + e];
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -1340,41 +1347,48 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
         const long long p = pv[u] - b0;
         const bool ok = p >= 0 && p < rows;
         bad |= !ok;
-        seg_in[e] = ok ? static_cast<uint16_t>(p * corners + e % corners) : kDropped;
-        w_in[e] = wv[u];
+        if (ok && p < lo) {
+          ++below;
+        } else if (ok && p < hi) {
+          const int slot = atomicAdd(&n_staged, 1);
+          st_seg[slot] = static_cast<uint16_t>((p - lo) * corners + e % corners);
+          st_src[slot] = static_cast<uint16_t>(e / corners);
+        }
       }
     }
   }
-  if (bad) atomicOr(&g_proj_err, kErrBadArgument);
+  if (bad && part == 0) atomicOr(&g_proj_err, kErrBadArgument);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) below += __shfl_xor_sync(0xffffffffu, below, o);
+  if ((threadIdx.x & 31) == 0 && below) atomicAdd(&n_below, below);
   __syncthreads();
-  for (int e = threadIdx.x; e < n; e += blockDim.x)
-    if (seg_in[e] != kDropped) atomicAdd(&cnt[seg_in[e]], 1);
+  const int staged = n_staged;
+  for (int i = threadIdx.x; i < staged; i += blockDim.x) atomicAdd(&cnt[st_seg[i]], 1);
   __syncthreads();
   // exclusive scan: thread t scans a contiguous chunk of the counts
-  const int per = (nseg + blockDim.x - 1) / blockDim.x;
-  const int i0 = min(nseg, static_cast<int>(threadIdx.x) * per), i1 = min(nseg, i0 + per);
+  const long long off0 = e_base + n_below;  // this part's first entry
+  const int chunk = (nseg + blockDim.x - 1) / blockDim.x;
+  const int i0 = min(nseg, static_cast<int>(threadIdx.x) * chunk), i1 = min(nseg, i0 + chunk);
   int local = 0;
   for (int i = i0; i < i1; ++i) local += cnt[i];
   int run = block_exclusive_scan(local, warp_tot);
   for (int i = i0; i < i1; ++i) {
     const int c = cnt[i];
-    cnt[i] = run;  // the segment's first entry (group-relative), the cursor below
-    seg_offsets[b0 * corners + i] = static_cast<int32_t>(e_base + run);
+    cnt[i] = run;  // the segment's first entry (part-relative), the cursor below
+    seg_offsets[(b0 + lo) * corners + i] = static_cast<int32_t>(off0 + run);
     run += c;
   }
   __syncthreads();
   // placement (arbitrary order inside a segment for now)
-  for (int e = threadIdx.x; e < n; e += blockDim.x) {
-    const int sg = seg_in[e];
-    if (sg == kDropped) continue;
+  for (int i = threadIdx.x; i < staged; i += blockDim.x) {
+    const int sg = st_seg[i];
     const int pos = atomicAdd(&cnt[sg], 1);
-    e_src[pos] = static_cast<uint16_t>(e / corners);
-    e_w[pos] = w_in[e];
+    e_src[pos] = st_src[i];
+    e_w[pos] = weights[e_base + static_cast<long long>(st_src[i]) * corners + sg % corners];
   }
   __syncthreads();
-  const int total = cnt[nseg - 1];  // cursor of the last segment = pairs placed
-  if (g == groups - 1 && threadIdx.x == 0)
-    for (long long j = b1 * corners; j <= M * corners; ++j) seg_offsets[j] = static_cast<int32_t>(e_base + total);
+  if (g == groups - 1 && part == parts - 1 && threadIdx.x == 0)
+    for (long long j = b1 * corners; j <= M * corners; ++j) seg_offsets[j] = static_cast<int32_t>(off0 + staged);
   // ascending source order inside each segment (segments hold a few entries each)
   for (int i = threadIdx.x; i < nseg; i += blockDim.x) {
     const int a = i > 0 ? cnt[i - 1] : 0, b = cnt[i];
@@ -1392,22 +1406,22 @@ __global__ void __launch_bounds__(kCsrGroupThreads)
     }
   }
   __syncthreads();
-  for (int e0 = threadIdx.x; e0 < total; e0 += 4 * stride) {
+  for (int e0 = threadIdx.x; e0 < staged; e0 += 4 * stride) {
     long long sv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int e = e0 + u * stride;
-      if (e < total) {
-        const long long s = q0 + e_src[e];
-        sv[u] = src_rows ? src_rows[s] : s;
+      if (e < staged) {
+        const long long src = q0 + e_src[e];
+        sv[u] = src_rows ? src_rows[src] : src;
       }
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int e = e0 + u * stride;
-      if (e < total) {
-        entry_src[e_base + e] = static_cast<int32_t>(sv[u]);
-        entry_w[e_base + e] = e_w[e];
+      if (e < staged) {
+        entry_src[off0 + e] = static_cast<int32_t>(sv[u]);
+        entry_w[off0 + e] = e_w[e];
       }
     }
   }
@@ -1930,16 +1944,23 @@ extern "C" int vb200_plan_csr_build_grouped(const int64_t* parent, const float* 
                 max_group_rows, max_group_sources, (long long)corners, kCsrGroupMaxSegments, kCsrGroupMaxEntries);
   VB200_REQUIRE(seg_offsets && q_begin && b_begin && (S == 0 || (parent && weights && entry_src && entry_w)),
                 "plan_csr_build_grouped: null pointer");
-  const int max_segments = static_cast<int>(std::max<long long>(1, static_cast<long long>(max_group_rows) * corners));
+  // parts per group: enough CTAs to spread the build over the GPU (each part owns a range of the
+  // group's merged rows and scans all of its pairs)
+  int sms = 0, dev = 0;
+  VB200_CHECK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  VB200_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+  const int parts = std::max(1, std::min({kCsrMaxParts, sms / groups, std::max(1, max_group_rows)}));
+  const int per = (max_group_rows + parts - 1) / parts;
+  const int max_segments = static_cast<int>(std::max<long long>(1, static_cast<long long>(per) * corners));
   const int max_entries = static_cast<int>(std::max<long long>(2, (static_cast<long long>(max_group_sources) * corners + 1) & ~1ll));
-  const size_t smem = static_cast<size_t>(max_segments) * 4 + static_cast<size_t>(max_entries) * 12;
+  const size_t smem = static_cast<size_t>(max_segments) * 4 + static_cast<size_t>(max_entries) * 10;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   VB200_CHECK_CUDA(cudaFuncSetAttribute(csr_grouped_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)),
                    "cudaFuncSetAttribute");
-  csr_grouped_kernel<<<groups, kCsrGroupThreads, smem, st>>>(parent, weights, src_rows, static_cast<int>(corners), M,
-                                                               q_begin, b_begin, groups, max_segments, max_entries,
-                                                               seg_offsets, entry_src, entry_w);
+  csr_grouped_kernel<<<groups * parts, kCsrGroupThreads, smem, st>>>(
+      parent, weights, src_rows, static_cast<int>(corners), M, q_begin, b_begin, groups, parts, max_segments,
+      max_entries, seg_offsets, entry_src, entry_w);
   VB200_CHECK_LAUNCH("csr_grouped_kernel");
   if (M > 0 && (mass || log_mass)) {
     csr_mass_kernel<<<row_blocks(M), kWarpsPerBlock * 32, 0, st>>>(seg_offsets, entry_w, M, static_cast<int>(corners),

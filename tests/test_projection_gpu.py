@@ -220,10 +220,12 @@ def test_hot_row_gather_matches_plain(pkg, oracle, cuda_device, dtype, C, monkey
     assert pkg.device_error_flags() == 0
 
 
-@pytest.mark.parametrize("sizes", [[(3087, 1029)] * 3, [(500, 40), (0, 7), (1200, 300), (37, 5)]],
-                         ids=["frame_groups", "ragged"])
+@pytest.mark.parametrize("sizes", [[(3087, 1029)] * 3, [(500, 40), (0, 7), (1200, 300), (37, 5)], [(60, 20)] * 40,
+                                   [(3601, 515)]],
+                         ids=["frame_groups", "ragged", "many_groups", "one_group"])
 def test_grouped_csr_equals_general(pkg, cuda_device, sizes):
-    """vb200_plan_csr_build_grouped (one CTA per group) against the general radix-sort build:
+    """vb200_plan_csr_build_grouped (up to eight CTAs per group, each owning a range of the
+    group's merged rows) against the general radix-sort build:
     identical segment offsets, entries, masses and log-masses, for frame-group shapes and for
     ragged groups (one without sources, skewed parents giving long segments)."""
     rng = np.random.default_rng(len(sizes))
