@@ -36,9 +36,61 @@ __device__ __forceinline__ float warp_allsum(float v) {
 
 inline unsigned blocks_of(long long n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
 
+// G lanes per row (G a power of two, G x 16-byte vectors cover the row in as few passes as
+// possible: 32 / G rows per warp), the sum of squares reduced over the G lanes, fp32 out.
 template <typename T>
 __global__ void __launch_bounds__(kTttWarps * 32)
-    row_l2_normalize_kernel(const T* __restrict__ x, long long rows, int C, float eps, float* __restrict__ out) {
+    row_l2_normalize_kernel(const T* __restrict__ x, long long rows, int C, int G, float eps, float* __restrict__ out) {
+  constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
+  const int lane = threadIdx.x & 31;
+  const long long r = (static_cast<long long>(blockIdx.x) * kTttWarps + (threadIdx.x >> 5)) * (32 / G) + lane / G;
+  const int sub = lane % G;
+  const int nv = C / V;
+  constexpr int kKeep = 4;  // vectors per lane kept in registers between the two passes
+  const uint4* xr = reinterpret_cast<const uint4*>(x + r * C);
+  uint4 keep[kKeep];
+  float ss = 0.f;
+  auto sumsq = [&](const uint4& raw) {
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float f = to_f32<T>(e[i]);
+      ss = fmaf(f, f, ss);
+    }
+  };
+  if (r < rows) {
+#pragma unroll
+    for (int j = 0; j < kKeep; ++j) {
+      if (sub + j * G < nv) {
+        keep[j] = __ldg(xr + sub + j * G);
+        sumsq(keep[j]);
+      }
+    }
+    for (int v = sub + kKeep * G; v < nv; v += G) sumsq(__ldg(xr + v));
+  }
+  for (int o = G / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (r >= rows) return;
+  const float norm = fmaxf(sqrtf(ss), eps);
+  auto scale = [&](const uint4& raw, int v) {
+    const T* e = reinterpret_cast<const T*>(&raw);
+    float o[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) o[i] = __fdiv_rn(to_f32<T>(e[i]), norm);
+#pragma unroll
+    for (int i = 0; i < V; i += 4)
+      *reinterpret_cast<float4*>(out + r * C + v * V + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+  };
+#pragma unroll
+  for (int j = 0; j < kKeep; ++j)
+    if (sub + j * G < nv) scale(keep[j], sub + j * G);
+  for (int v = sub + kKeep * G; v < nv; v += G) scale(__ldg(xr + v), v);
+}
+
+// Rows that are not 16-byte vectors (C not a multiple of the vector, or unaligned): one warp per
+// row, scalar loads.
+template <typename T>
+__global__ void __launch_bounds__(kTttWarps * 32)
+    row_l2_normalize_scalar_kernel(const T* __restrict__ x, long long rows, int C, float eps, float* __restrict__ out) {
   const long long r = static_cast<long long>(blockIdx.x) * kTttWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -334,9 +386,20 @@ extern "C" int vb200_row_l2_normalize(int dtype, const void* x, int64_t rows, in
   if (rows == 0) return VB200_OK;
   VB200_REQUIRE(x && out, "row_l2_normalize: null pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-#define VB200_NRM(T)                                                                                        \
-  row_l2_normalize_kernel<T><<<blocks_of(rows, kTttWarps), kTttWarps * 32, 0, st>>>(static_cast<const T*>(x), \
-                                                                                      rows, static_cast<int>(C), eps, out)
+#define VB200_NRM(T)                                                                                   \
+  do {                                                                                                  \
+    constexpr int V = 16 / static_cast<int>(sizeof(T));                                                 \
+    if (C % V == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) { \
+      int G = 1;                                                                                        \
+      while (G < 32 && G * 2 * V <= C) G *= 2;                                                          \
+      const long long warps = (rows + (32 / G) - 1) / (32 / G);                                        \
+      row_l2_normalize_kernel<T><<<blocks_of(warps, kTttWarps), kTttWarps * 32, 0, st>>>(               \
+          static_cast<const T*>(x), rows, static_cast<int>(C), G, eps, out);                            \
+    } else {                                                                                            \
+      row_l2_normalize_scalar_kernel<T><<<blocks_of(rows, kTttWarps), kTttWarps * 32, 0, st>>>(         \
+          static_cast<const T*>(x), rows, static_cast<int>(C), eps, out);                               \
+    }                                                                                                   \
+  } while (0)
   if (dtype == VB200_F32) VB200_NRM(float);
   else if (dtype == VB200_BF16) VB200_NRM(__nv_bfloat16);
   else VB200_NRM(__half);

@@ -132,3 +132,14 @@ def test_argument_errors(pkg, cuda_device):
         tk.fused_motion_cues(a, a, torch.zeros(2, 4, 4, 3, device=cuda_device), a[..., 0], a[..., 0])
     with pytest.raises(RuntimeError, match="CUDA"):
         tk.local_top2_match(a.cpu(), a.cpu(), 1, 1)
+
+
+@pytest.mark.parametrize("shape,dtype", [((5, 37), torch.float32), ((7, 64), torch.bfloat16), ((3, 1024), torch.float32),
+                                         ((9, 8), torch.float16)])
+def test_normalize_rows_paths(pkg, oracle, cuda_device, shape, dtype):
+    """Both launch forms of vb200_row_l2_normalize: 16-byte vectors with 1-32 lanes per row, and
+    the scalar fallback (a row that is not a whole number of vectors)."""
+    x = torch.randn(*shape, generator=torch.Generator().manual_seed(sum(shape))).to(cuda_device, dtype)
+    got = pkg.ttt_kernels.normalize_rows(x)
+    ref = oracle.ttt_prepass.normalize_rows(x.float().cpu().numpy())
+    np.testing.assert_allclose(got.cpu().numpy(), ref, rtol=1e-6, atol=1e-7)
