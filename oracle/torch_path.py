@@ -1,5 +1,5 @@
-"""The reference's own PyTorch call sequence for one benchmark step, on CPU (BASELINE / TEST
-INFRASTRUCTURE: the timed CPU baseline and reference arm of bench.py; never a product path).
+"""The reference's own PyTorch call sequence for one benchmark step, on CPU (CPU baseline and
+test infrastructure: the timed CPU baseline and reference arm of bench.py; never a product path).
 
 The reference (shuang-yang18/4D_TTT_merging) is a PyTorch program whose GPU kernels are Triton;
 on a CPU it runs the PyTorch operators below.  This module restates that sequence with the
