@@ -359,19 +359,20 @@ def _fit_temporal_local(features, basis_ids, *, frames: int, patches: int, thres
     lo = [max(1, b - 1) for b in starts]
     hi = [min(frames - 1, e) for e in ends]
     cut = torch.tensor([1] + starts + ends + lo + [h + 1 for h in hi], device=dev) * patches
-    s_pos = torch.searchsorted(source_ids, cut[1:1 + 2 * len(starts)]).tolist()
-    b_pos = torch.searchsorted(basis_ids, torch.cat([cut[:1], cut[1 + 2 * len(starts):]])).tolist()
     g = len(starts)
+    pos = torch.cat([torch.searchsorted(source_ids, cut[1:1 + 2 * g]),
+                     torch.searchsorted(basis_ids, torch.cat([cut[:1], cut[1 + 2 * g:]]))]).tolist()  # one sync
+    s_pos, b_pos = pos[:2 * g], pos[2 * g:]
     s_begin, s_end = s_pos[:g], s_pos[g:]
     b0, b_lo, b_hi = b_pos[0], b_pos[1:1 + g], b_pos[1 + g:]
     # one query row per grouped source, one concatenated basis list per group
-    q_rows, b_lists, qb, bb = [], [], [0], [0]
+    # (consecutive groups: frames [1, 9), [9, 17), ... so their sources form one contiguous run)
+    b_lists, qb, bb = [], [0], [0]
     for k in range(g):
-        q_rows.append(torch.arange(s_begin[k], s_end[k], device=dev))
         b_lists.append(torch.cat([basis_ids[:b0], basis_ids[b_lo[k]:b_hi[k]]]))
         qb.append(qb[-1] + s_end[k] - s_begin[k])
         bb.append(bb[-1] + b_lists[-1].numel())
-    rows = torch.cat(q_rows)
+    rows = torch.arange(s_begin[0], s_end[-1], device=dev)
     local_basis = torch.cat(b_lists)
     support = basis_ids[:1].expand(n, 4).clone()
     weights = torch.zeros((n, 4), device=dev, dtype=torch.float32)
@@ -621,7 +622,9 @@ def build_ttt_protected_uniform_convex_plan(
     original_to_compact[keep] = torch.arange(keep.numel(), device=dev)
     parent = original_to_compact.index_select(0, patch_ids.index_select(0, support_local.reshape(-1)))
     parent = parent.view(-1, 4)
-    if bool((parent < 0).any()):
+    counts = torch.stack([(parent < 0).any().long(), (~accepted).sum()]
+                         + [c.sum().long() for c in guard_counter]).tolist()  # one sync for the checks
+    if counts[0]:
         raise RuntimeError("protected TTT convex support must remain physical")
     source_original = patch_ids.index_select(0, source_local)
     csr = build_plan_csr(parent, weights, keep.numel(), src_rows=source_original)
@@ -638,10 +641,10 @@ def build_ttt_protected_uniform_convex_plan(
                   "top1_pruning_enabled": bool(pruning), "protected_uniform_bases": int(stable.numel()),
                   "top1_pruned_uniform_bases": freed, "sensitive_event_budget": budget,
                   "sensitive_event_proposals": int(proposal.numel()), "sensitive_event_bases": int(event.numel()),
-                  "fit_failure_promotions": int((~accepted).sum()), "physical_patch_tokens": int(keep_local.numel()),
+                  "fit_failure_promotions": int(counts[1]), "physical_patch_tokens": int(keep_local.numel()),
                   "selection_geometry_weight": float(selection_geometry_weight),
                   "support_geometry_weight": float(support_geometry_weight),
                   "support_geometry_guard_tolerance": support_geometry_guard_tolerance,
                   "geometry_guard_enabled": guard is not None,
-                  "geometry_guard_selected": int(sum(int(c.sum()) for c in guard_counter))},
+                  "geometry_guard_selected": int(sum(counts[2:]))},
     )
